@@ -1,0 +1,585 @@
+// Additive X-ray rasterization forward and backward.
+//
+// Forward (reference: csrc/RasterizeToPixelsFwd.cu:56-186): one CTA per
+// (view, tile), one thread per pixel; the tile's sorted Gaussian list is
+// staged through shared memory in batches.  Differences in how the work is
+// done (the result is the same sum over the same contributing set):
+//   * every staged Gaussian carries a bit mask of the warps (pixel blocks of
+//     8x4 for tile sizes divisible by 8) whose pixels can reach the
+//     |alpha| >= 1e-5 cut-off; a warp only evaluates the Gaussians of its
+//     mask bits (ballot + find-first-set), so pairs that the reference
+//     evaluates and then discards are never evaluated;
+//   * float32 evaluates sigma*log2(e) with a pre-scaled conic and one ex2.
+//
+// Backward (reference: csrc/RasterizeToPixelsBwd.cu:76-265 "pixel" and
+// 349-480 "primitive"): one CTA per (view, tile) with the tile's upstream
+// gradient in shared memory; each warp takes whole Gaussians and walks only
+// the pixel rectangle that can contribute.  Per (Gaussian, tile) it reduces
+// six moments of the contributing pixels,
+//   S0 = sum v e,  Sx = sum v e dx,  Sy = sum v e dy,
+//   Sxx = sum v e dx^2,  Sxy = sum v e dx dy,  Syy = sum v e dy^2
+// (+ Ax, Ay = sum |v e (conic d)|_x,y for absgrad), with e = exp(-sigma) and
+// d = pixel - mean, and adds them to a per-(view, Gaussian) record with two
+// vector reductions.  Every reference gradient is a fixed linear map of
+// these moments:
+//   v_means2d = w mu (a Sx + b Sy, b Sx + c Sy)
+//   v_conics  = -w mu (Sxx/2, Sxy, Syy/2)
+//   v_opacity = mu S0,   v_mu = w S0,   v_means2d_abs = |w mu| (Ax, Ay)
+#include <math_constants.h>
+
+#include "r2s_common.cuh"
+
+namespace r2s {
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+__host__ __device__ __forceinline__ size_t al16(size_t x) { return (x + 15) & ~size_t(15); }
+constexpr float kAlphaMin2D = 1e-5f;
+
+// ---------------------------------------------------------------------------
+// Culling extents (see cull_extent in r2s_preprocess.cu for the margins)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void conic_cull_extents(float a, float b, float c, float amp,
+                                                   float thresh, float& ex, float& ey) {
+    if (isnan(amp) || isnan(a) || isnan(b) || isnan(c)) {
+        ex = ey = CUDART_INF_F;
+        return;
+    }
+    const float aa = fabsf(amp);
+    if (!(aa >= thresh)) {
+        ex = ey = -1.0f;
+        return;
+    }
+    const float det = a * c - b * b;
+    if (!(a > 0.f && c > 0.f && det > 0.f)) {
+        ex = ey = CUDART_INF_F;
+        return;
+    }
+    const float cond = (a * c) / det;
+    if (!isfinite(cond) || cond > 1e6f) {
+        ex = ey = CUDART_INF_F;
+        return;
+    }
+    const float s_cut = logf(aa / thresh) * 1.0001f + 1e-4f;
+    const float rel = 1.0f + 1e-4f + 4e-7f * cond;
+    ex = sqrtf(2.0f * s_cut * (c / det) * rel) * 1.0001f + 1e-3f;
+    ey = sqrtf(2.0f * s_cut * (a / det) * rel) * 1.0001f + 1e-3f;
+}
+
+// Inclusive index range [lo, hi] of tile-local pixels whose centre lies within
+// [m - e, m + e], clamped to [0, lim]; empty when lo > hi.
+__device__ __forceinline__ void cull_range(float m, float e, float origin, int lim, int& lo,
+                                           int& hi) {
+    if (!(e >= 0.f)) {
+        lo = 1;
+        hi = 0;
+        return;
+    }
+    if (!isfinite(m) || isinf(e)) {
+        lo = 0;
+        hi = lim;
+        return;
+    }
+    const float flo = fmaxf(m - e - origin - 0.5f, 0.0f);
+    const float fhi = fminf(m + e - origin - 0.5f, static_cast<float>(lim));
+    if (flo > fhi) {
+        lo = 1;
+        hi = 0;
+        return;
+    }
+    lo = static_cast<int>(ceilf(flo));
+    hi = static_cast<int>(floorf(fhi));
+}
+
+// ---------------------------------------------------------------------------
+// Pixel layout of a tile CTA
+// ---------------------------------------------------------------------------
+struct TileGeom {
+    int T;        // tile edge
+    int nthr;     // T*T threads
+    bool blocked; // warps own 8x4 pixel blocks
+    __device__ __forceinline__ void pixel(int tid, int& lx, int& ly) const {
+        if (blocked) {
+            const int w = tid >> 5, l = tid & 31, wx = T >> 3;
+            lx = (w % wx) * 8 + (l & 7);
+            ly = (w / wx) * 4 + (l >> 3);
+        } else {
+            ly = tid / T;
+            lx = tid - ly * T;
+        }
+    }
+    // bounding box of warp w's pixels, clipped to [0, cmax] x [0, rmax]
+    __device__ __forceinline__ int4 warp_box(int w, int cmax, int rmax) const {
+        int c0, c1, r0, r1;
+        if (blocked) {
+            const int wx = T >> 3;
+            c0 = (w % wx) * 8;
+            c1 = c0 + 7;
+            r0 = (w / wx) * 4;
+            r1 = r0 + 3;
+        } else {
+            const int first = w * 32, last = min(w * 32 + 31, nthr - 1);
+            r0 = first / T;
+            r1 = last / T;
+            c0 = (r0 == r1) ? first - r0 * T : 0;
+            c1 = (r0 == r1) ? last - r1 * T : T - 1;
+        }
+        c1 = min(c1, cmax);
+        r1 = min(r1, rmax);
+        return make_int4(c0, c1, r0, r1);
+    }
+};
+
+__device__ __forceinline__ unsigned warp_lane_mask(int nthr, int warp) {
+    const int n = nthr - warp * 32;
+    return n >= 32 ? 0xffffffffu : ((1u << n) - 1u);
+}
+
+template <typename S>
+struct RasterSrc {
+    const float4* splats;  // fused float32 records [C*N][2]
+    const S* means2d;      // reference-layout inputs [C*N][2]
+    const S* conics;       // [C*N][3]
+    const S* opac;         // [C*N]
+    const S* mus;          // [C*N]
+};
+
+template <typename S, bool SPLATS>
+__device__ __forceinline__ void load_gauss(const RasterSrc<S>& src, int64_t g, S& mx, S& my, S& a,
+                                           S& b, S& c, S& wmu, float& ex, float& ey) {
+    if constexpr (SPLATS) {
+        const float4 p = src.splats[2 * g];
+        const float4 q = src.splats[2 * g + 1];
+        mx = p.x;
+        my = p.y;
+        a = p.z;
+        b = p.w;
+        c = q.x;
+        wmu = q.y;
+        ex = q.z;
+        ey = q.w;
+    } else {
+        mx = src.means2d[2 * g];
+        my = src.means2d[2 * g + 1];
+        a = src.conics[3 * g];
+        b = src.conics[3 * g + 1];
+        c = src.conics[3 * g + 2];
+        wmu = src.opac[g] * src.mus[g];
+        conic_cull_extents((float)a, (float)b, (float)c, (float)wmu, kAlphaMin2D, ex, ey);
+    }
+}
+
+// ===========================================================================
+// Forward
+// ===========================================================================
+template <typename S, bool SPLATS>
+__global__ void raster_fwd_kernel(RasterSrc<S> src, const int32_t* __restrict__ offsets,
+                                  const int32_t* __restrict__ flatten_ids, int64_t n_keys,
+                                  int64_t n_isects, uint32_t W, uint32_t H, TileGeom geo,
+                                  uint32_t ntx, uint32_t nty, S* __restrict__ image) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int nthr = geo.nthr;
+    const size_t arr = al16((size_t)nthr * sizeof(S));
+    S* s_mx = reinterpret_cast<S*>(smem_raw);
+    S* s_my = reinterpret_cast<S*>(smem_raw + arr);
+    S* s_a = reinterpret_cast<S*>(smem_raw + 2 * arr);
+    S* s_b = reinterpret_cast<S*>(smem_raw + 3 * arr);
+    S* s_c = reinterpret_cast<S*>(smem_raw + 4 * arr);
+    S* s_w = reinterpret_cast<S*>(smem_raw + 5 * arr);
+    uint32_t* s_mask = reinterpret_cast<uint32_t*>(smem_raw + 6 * arr);
+    int4* s_box = reinterpret_cast<int4*>(smem_raw + 6 * arr + al16((size_t)nthr * 4));
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int T = geo.T;
+    const int64_t cam = blockIdx.z;
+    const uint32_t tx = blockIdx.x, ty = blockIdx.y;
+    const int64_t key = cam * (int64_t)ntx * nty + (int64_t)ty * ntx + tx;
+    const int X0 = tx * T, Y0 = ty * T;
+    const int cmax = min(T - 1, (int)W - 1 - X0), rmax = min(T - 1, (int)H - 1 - Y0);
+    const int n_warps = (nthr + 31) >> 5;
+    if (tid < n_warps) s_box[tid] = geo.warp_box(tid, cmax, rmax);
+
+    int lx, ly;
+    geo.pixel(tid, lx, ly);
+    const bool inside = lx <= cmax && ly <= rmax;
+    const S px = static_cast<S>(X0 + lx) + static_cast<S>(0.5);
+    const S py = static_cast<S>(Y0 + ly) + static_cast<S>(0.5);
+    const int start = offsets[key];
+    const int end = key + 1 < n_keys ? offsets[key + 1] : (int)n_isects;
+    const unsigned wmask = warp_lane_mask(nthr, warp);
+    S acc = static_cast<S>(0);
+    __syncthreads();
+
+    for (int b0 = start; b0 < end; b0 += nthr) {
+        const int n = min(nthr, end - b0);
+        __syncthreads();
+        if (tid < n) {
+            const int64_t g = flatten_ids[b0 + tid];
+            S mx, my, a, b, c, wmu;
+            float ex, ey;
+            load_gauss<S, SPLATS>(src, g, mx, my, a, b, c, wmu, ex, ey);
+            int c_lo, c_hi, r_lo, r_hi;
+            cull_range((float)mx, ex, (float)X0, cmax, c_lo, c_hi);
+            cull_range((float)my, ey, (float)Y0, rmax, r_lo, r_hi);
+            uint32_t m = 0;
+            if (c_lo <= c_hi && r_lo <= r_hi) {
+                for (int w = 0; w < n_warps; ++w) {
+                    const int4 bx = s_box[w];
+                    if (c_lo <= bx.y && c_hi >= bx.x && r_lo <= bx.w && r_hi >= bx.z) m |= 1u << w;
+                }
+            }
+            s_mx[tid] = mx;
+            s_my[tid] = my;
+            if constexpr (std::is_same<S, float>::value) {
+                s_a[tid] = 0.5f * kLog2e * a;
+                s_b[tid] = kLog2e * b;
+                s_c[tid] = 0.5f * kLog2e * c;
+            } else {
+                s_a[tid] = a;
+                s_b[tid] = b;
+                s_c[tid] = c;
+            }
+            s_w[tid] = wmu;
+            s_mask[tid] = m;
+        }
+        __syncthreads();
+        for (int c0 = 0; c0 < n; c0 += 32) {
+            const int j = c0 + lane;
+            unsigned bits = __ballot_sync(wmask, j < n && ((s_mask[j] >> warp) & 1u));
+            while (bits) {
+                const int t = c0 + __ffs(bits) - 1;
+                bits &= bits - 1;
+                const S dx = px - s_mx[t];
+                const S dy = py - s_my[t];
+                if constexpr (std::is_same<S, float>::value) {
+                    const float u = fmaf(s_a[t], dx, s_b[t] * dy);
+                    const float s = fmaf(dx, u, s_c[t] * dy * dy);
+                    const float al = s_w[t] * exp2f(-s);
+                    acc += (s < 0.f || fabsf(al) < kAlphaMin2D) ? 0.f : al;
+                } else {
+                    const S sig = static_cast<S>(0.5) * (s_a[t] * dx * dx + s_c[t] * dy * dy) +
+                                  s_b[t] * dx * dy;
+                    const S al = s_w[t] * expf_neg(sig);
+                    const bool skip = sig < static_cast<S>(0) ||
+                                      fabsf(static_cast<float>(al)) < static_cast<S>(1e-5);
+                    acc += skip ? static_cast<S>(0) : al;
+                }
+            }
+        }
+    }
+    if (inside) image[(cam * H + (Y0 + ly)) * (int64_t)W + X0 + lx] = acc;
+}
+
+// ===========================================================================
+// Backward: sufficient statistics per (view, Gaussian)
+// ===========================================================================
+template <typename S>
+__device__ __forceinline__ void stats_red(S* dst, const S v[8], bool with_abs) {
+    if constexpr (std::is_same<S, float>::value) {
+        red_add_v4(dst, v[0], v[1], v[2], v[3]);
+        if (with_abs) red_add_v4(dst + 4, v[4], v[5], v[6], v[7]);
+        else red_add_v2(dst + 4, v[4], v[5]);
+    } else {
+        const int n = with_abs ? 8 : 6;
+        for (int k = 0; k < n; ++k) atomicAdd(dst + k, v[k]);
+    }
+}
+
+template <typename S, bool SPLATS, int EXPMODE>
+__global__ void raster_bwd_kernel(RasterSrc<S> src, const int32_t* __restrict__ offsets,
+                                  const int32_t* __restrict__ flatten_ids, int64_t n_keys,
+                                  int64_t n_isects, const S* __restrict__ v_image, uint32_t W,
+                                  uint32_t H, int T, uint32_t ntx, uint32_t nty, int with_abs,
+                                  S* __restrict__ stats) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int nthr = blockDim.x;
+    const int TP = T + 1;
+    S* s_v = reinterpret_cast<S*>(smem_raw);
+    S* s_mx = s_v + T * TP;
+    S* s_my = s_mx + nthr;
+    S* s_a = s_my + nthr;
+    S* s_b = s_a + nthr;
+    S* s_c = s_b + nthr;
+    S* s_w = s_c + nthr;
+    int32_t* s_g = reinterpret_cast<int32_t*>(s_w + nthr);
+    uint32_t* s_box = reinterpret_cast<uint32_t*>(s_g + nthr);
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int n_warps = nthr >> 5;
+    const int64_t cam = blockIdx.z;
+    const uint32_t tx = blockIdx.x, ty = blockIdx.y;
+    const int64_t key = cam * (int64_t)ntx * nty + (int64_t)ty * ntx + tx;
+    const int X0 = tx * T, Y0 = ty * T;
+    const int cmax = min(T - 1, (int)W - 1 - X0), rmax = min(T - 1, (int)H - 1 - Y0);
+    const int start = offsets[key];
+    const int end = key + 1 < n_keys ? offsets[key + 1] : (int)n_isects;
+    if (start >= end) return;
+
+    const S* vcam = v_image + cam * (int64_t)H * W;
+    for (int p = tid; p < T * T; p += nthr) {
+        const int r = p / T, c = p - r * T;
+        s_v[r * TP + c] = (c <= cmax && r <= rmax) ? vcam[(int64_t)(Y0 + r) * W + X0 + c]
+                                                   : static_cast<S>(0);
+    }
+
+    for (int b0 = start; b0 < end; b0 += nthr) {
+        const int n = min(nthr, end - b0);
+        __syncthreads();
+        if (tid < n) {
+            const int64_t g = flatten_ids[b0 + tid];
+            S mx, my, a, b, c, wmu;
+            float ex, ey;
+            load_gauss<S, SPLATS>(src, g, mx, my, a, b, c, wmu, ex, ey);
+            int c_lo, c_hi, r_lo, r_hi;
+            cull_range((float)mx, ex, (float)X0, cmax, c_lo, c_hi);
+            cull_range((float)my, ey, (float)Y0, rmax, r_lo, r_hi);
+            if (c_lo > c_hi || r_lo > r_hi) c_lo = 1, c_hi = 0, r_lo = 0, r_hi = 0;
+            s_mx[tid] = mx;
+            s_my[tid] = my;
+            s_a[tid] = a;
+            s_b[tid] = b;
+            s_c[tid] = c;
+            s_w[tid] = wmu;
+            s_g[tid] = (int32_t)g;
+            s_box[tid] = (uint32_t)c_lo | ((uint32_t)c_hi << 8) | ((uint32_t)r_lo << 16) |
+                         ((uint32_t)r_hi << 24);
+        }
+        __syncthreads();
+        for (int t = warp; t < n; t += n_warps) {
+            const uint32_t bx = s_box[t];
+            const int c_lo = bx & 0xff, c_hi = (bx >> 8) & 0xff;
+            const int r_lo = (bx >> 16) & 0xff, r_hi = bx >> 24;
+            if (c_lo > c_hi) continue;
+            const int w = c_hi - c_lo + 1;
+            const int npx = w * (r_hi - r_lo + 1);
+            const float inv_w = 1.0f / (float)w;
+            const S mx = s_mx[t], my = s_my[t], a = s_a[t], b = s_b[t], c = s_c[t], wmu = s_w[t];
+            S acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            for (int p = lane; p < npx; p += 32) {
+                const int rr = __float2int_rz(((float)p + 0.5f) * inv_w);
+                const int cc = p - rr * w;
+                const int lx = c_lo + cc, ly = r_lo + rr;
+                const S v = s_v[ly * TP + lx];
+                const S dx = static_cast<S>(X0 + lx) + static_cast<S>(0.5) - mx;
+                const S dy = static_cast<S>(Y0 + ly) + static_cast<S>(0.5) - my;
+                S e;
+                bool skip;
+                if constexpr (std::is_same<S, float>::value) {
+                    const float A = 0.5f * kLog2e * a, B = kLog2e * b, Cc = 0.5f * kLog2e * c;
+                    const float u = fmaf(A, dx, B * dy);
+                    const float s = fmaf(dx, u, Cc * dy * dy);
+                    e = exp2f(-s);
+                    skip = s < 0.f || fabsf(wmu * e) < kAlphaMin2D;
+                } else {
+                    const S sig = static_cast<S>(0.5) * (a * dx * dx + c * dy * dy) + b * dx * dy;
+                    if constexpr (EXPMODE == 0) {
+                        e = expf_neg(sig);
+                        skip = sig < static_cast<S>(0) ||
+                               fabsf(static_cast<float>(wmu * e)) < static_cast<S>(1e-5);
+                    } else {
+                        e = exp(-sig);
+                        skip = sig < static_cast<S>(0) || fabs(wmu * e) < static_cast<S>(1e-5);
+                    }
+                }
+                const S ve = skip ? static_cast<S>(0) : v * e;
+                const S vx = ve * dx, vy = ve * dy;
+                acc[0] += ve;
+                acc[1] += vx;
+                acc[2] += vy;
+                acc[3] += vx * dx;
+                acc[4] += vx * dy;
+                acc[5] += vy * dy;
+                if (with_abs) {
+                    acc[6] += fabs(a * vx + b * vy);
+                    acc[7] += fabs(b * vx + c * vy);
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < 8; ++k) acc[k] = warp_sum(acc[k]);
+            if (lane == 0) stats_red(stats + (int64_t)s_g[t] * 8, acc, with_abs != 0);
+        }
+    }
+}
+
+// Per-(view, Gaussian) gradients of the reference from the statistics.
+template <typename S>
+__global__ void raster_unpack_kernel(const S* __restrict__ stats, const S* __restrict__ conics,
+                                     const S* __restrict__ opac, const S* __restrict__ mus,
+                                     int64_t total, S* __restrict__ v_abs, S* __restrict__ v_m2,
+                                     S* __restrict__ v_con, S* __restrict__ v_op,
+                                     S* __restrict__ v_mu) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= total) return;
+    const S* st = stats + i * 8;
+    const S S0 = st[0], Sx = st[1], Sy = st[2], Sxx = st[3], Sxy = st[4], Syy = st[5];
+    const S a = conics[3 * i], b = conics[3 * i + 1], c = conics[3 * i + 2];
+    const S w = opac[i], mu = mus[i];
+    const S wm = w * mu;
+    v_m2[2 * i] = wm * (a * Sx + b * Sy);
+    v_m2[2 * i + 1] = wm * (b * Sx + c * Sy);
+    v_con[3 * i] = -wm * static_cast<S>(0.5) * Sxx;
+    v_con[3 * i + 1] = -wm * Sxy;
+    v_con[3 * i + 2] = -wm * static_cast<S>(0.5) * Syy;
+    v_op[i] = mu * S0;
+    v_mu[i] = w * S0;
+    if (v_abs) {
+        v_abs[2 * i] = fabs(wm) * st[6];
+        v_abs[2 * i + 1] = fabs(wm) * st[7];
+    }
+}
+
+// ---------------------------------------------------------------------------
+// launchers
+// ---------------------------------------------------------------------------
+int check_tiles(int64_t C, uint32_t W, uint32_t H, uint32_t T, uint32_t ntx, uint32_t nty) {
+    R2S_REQUIRE(T > 0 && T * T <= 1024, "tile_size must be positive with tile_size**2 <= 1024");
+    R2S_REQUIRE(ntx > 0 && nty > 0, "rasterize: tile grid must be non-empty");
+    R2S_REQUIRE((uint64_t)ntx * T >= W && (uint64_t)nty * T >= H,
+                "rasterize: tile grid does not cover the image");
+    R2S_REQUIRE(C <= 65535 && nty <= 65535, "rasterize: too many views or tile rows for one launch");
+    return R2S_OK;
+}
+
+template <typename S, bool SPLATS>
+int launch_raster_fwd(const RasterSrc<S>& src, const int32_t* offsets, const int32_t* flatten_ids,
+                      int64_t C, int64_t n_isects, uint32_t W, uint32_t H, uint32_t T,
+                      uint32_t ntx, uint32_t nty, S* image, cudaStream_t stream) {
+    TileGeom geo;
+    geo.T = (int)T;
+    geo.nthr = (int)(T * T);
+    geo.blocked = (T % 8) == 0;
+    const int n_warps = (geo.nthr + 31) / 32;
+    const size_t smem = 6 * al16((size_t)geo.nthr * sizeof(S)) + al16((size_t)geo.nthr * 4) +
+                        (size_t)n_warps * 16;
+    auto kern = raster_fwd_kernel<S, SPLATS>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const dim3 grid(ntx, nty, (unsigned)C);
+    kern<<<grid, geo.nthr, smem, stream>>>(src, offsets, flatten_ids, C * (int64_t)ntx * nty,
+                                           n_isects, W, H, geo, ntx, nty, image);
+    return check_launch("rasterize_to_pixels_fwd");
+}
+
+template <typename S, bool SPLATS, int EXPMODE>
+int launch_raster_bwd(const RasterSrc<S>& src, const int32_t* offsets, const int32_t* flatten_ids,
+                      const S* v_image, int64_t C, int64_t N, int64_t n_isects, uint32_t W,
+                      uint32_t H, uint32_t T, uint32_t ntx, uint32_t nty, int with_abs, S* stats,
+                      cudaStream_t stream) {
+    cudaMemsetAsync(stats, 0, (size_t)C * N * 8 * sizeof(S), stream);
+    if (n_isects == 0) return check_launch("rasterize_to_pixels_bwd");
+    // at least one warp; 4 warps for 16x16 tiles
+    int nthr = (int)(T * T);
+    nthr = nthr < 128 ? 128 : (nthr > 256 ? 256 : nthr);
+    nthr = (nthr + 31) / 32 * 32;
+    const size_t smem = (size_t)T * (T + 1) * sizeof(S) + (size_t)nthr * (6 * sizeof(S) + 8);
+    auto kern = raster_bwd_kernel<S, SPLATS, EXPMODE>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const dim3 grid(ntx, nty, (unsigned)C);
+    kern<<<grid, nthr, smem, stream>>>(src, offsets, flatten_ids, C * (int64_t)ntx * nty, n_isects,
+                                       v_image, W, H, (int)T, ntx, nty, with_abs, stats);
+    return check_launch("rasterize_to_pixels_bwd");
+}
+
+}  // namespace r2s
+
+using namespace r2s;
+
+extern "C" int r2s_rasterize_to_pixels_fwd(int dtype, const void* means2d, const void* conics,
+                                           const void* opacities, const void* mus,
+                                           const int32_t* offsets, const int32_t* flatten_ids,
+                                           int64_t C, int64_t N, int64_t n_isects, uint32_t W,
+                                           uint32_t H, uint32_t T, uint32_t ntx, uint32_t nty,
+                                           void* image, r2s_stream_t stream) {
+    R2S_REQUIRE(C >= 0 && N >= 0 && n_isects >= 0, "rasterize_to_pixels_fwd: negative size");
+    const size_t es = dtype == R2S_F64 ? 8 : 4;
+    if (C == 0 || (int64_t)W * H == 0) return R2S_OK;
+    if (N == 0 || n_isects == 0) {
+        cudaMemsetAsync(image, 0, (size_t)C * W * H * es, stream);
+        return check_launch("rasterize_to_pixels_fwd");
+    }
+    if (int rc = check_tiles(C, W, H, T, ntx, nty)) return rc;
+    return R2S_DTYPE_DISPATCH(dtype, "rasterize_to_pixels_fwd", [&] {
+        RasterSrc<scalar_t> src{nullptr, (const scalar_t*)means2d, (const scalar_t*)conics,
+                                (const scalar_t*)opacities, (const scalar_t*)mus};
+        return launch_raster_fwd<scalar_t, false>(src, offsets, flatten_ids, C, n_isects, W, H, T,
+                                                  ntx, nty, (scalar_t*)image, stream);
+    });
+}
+
+extern "C" int r2s_rasterize_to_pixels_bwd(int dtype, int mode, const void* means2d,
+                                           const void* conics, const void* opacities,
+                                           const void* mus, const int32_t* offsets,
+                                           const int32_t* flatten_ids, const void* v_image,
+                                           int64_t C, int64_t N, int64_t n_isects, uint32_t W,
+                                           uint32_t H, uint32_t T, uint32_t ntx, uint32_t nty,
+                                           void* stats, void* v_abs, void* v_m2, void* v_con,
+                                           void* v_op, void* v_mu, r2s_stream_t stream) {
+    R2S_REQUIRE(C >= 0 && N >= 0 && n_isects >= 0, "rasterize_to_pixels_bwd: negative size");
+    R2S_REQUIRE(mode == 0 || mode == 1, "rasterize_to_pixels_bwd: mode must be 0 or 1");
+    const int64_t total = C * N;
+    const size_t es = dtype == R2S_F64 ? 8 : 4;
+    if (total == 0) return R2S_OK;
+    if (n_isects == 0 || (int64_t)W * H == 0) {
+        cudaMemsetAsync(v_m2, 0, total * 2 * es, stream);
+        cudaMemsetAsync(v_con, 0, total * 3 * es, stream);
+        cudaMemsetAsync(v_op, 0, total * es, stream);
+        cudaMemsetAsync(v_mu, 0, total * es, stream);
+        if (v_abs) cudaMemsetAsync(v_abs, 0, total * 2 * es, stream);
+        return check_launch("rasterize_to_pixels_bwd");
+    }
+    if (int rc = check_tiles(C, W, H, T, ntx, nty)) return rc;
+    return R2S_DTYPE_DISPATCH(dtype, "rasterize_to_pixels_bwd", [&] {
+        RasterSrc<scalar_t> src{nullptr, (const scalar_t*)means2d, (const scalar_t*)conics,
+                                (const scalar_t*)opacities, (const scalar_t*)mus};
+        int rc = mode == 0
+                     ? launch_raster_bwd<scalar_t, false, 0>(src, offsets, flatten_ids,
+                                                             (const scalar_t*)v_image, C, N,
+                                                             n_isects, W, H, T, ntx, nty,
+                                                             v_abs != nullptr, (scalar_t*)stats,
+                                                             stream)
+                     : launch_raster_bwd<scalar_t, false, 1>(src, offsets, flatten_ids,
+                                                             (const scalar_t*)v_image, C, N,
+                                                             n_isects, W, H, T, ntx, nty,
+                                                             v_abs != nullptr, (scalar_t*)stats,
+                                                             stream);
+        if (rc) return rc;
+        raster_unpack_kernel<scalar_t><<<grid_for(total), kThreads, 0, stream>>>(
+            (const scalar_t*)stats, (const scalar_t*)conics, (const scalar_t*)opacities,
+            (const scalar_t*)mus, total, (scalar_t*)v_abs, (scalar_t*)v_m2, (scalar_t*)v_con,
+            (scalar_t*)v_op, (scalar_t*)v_mu);
+        return check_launch("rasterize_to_pixels_bwd");
+    });
+}
+
+extern "C" int r2s_raster_splats_fwd_f32(const float* splats, const int32_t* offsets,
+                                         const int32_t* flatten_ids, int64_t C, int64_t N,
+                                         int64_t n_isects, uint32_t W, uint32_t H, uint32_t T,
+                                         uint32_t ntx, uint32_t nty, float* image,
+                                         r2s_stream_t stream) {
+    R2S_REQUIRE(C >= 0 && N >= 0 && n_isects >= 0, "raster_splats_fwd: negative size");
+    if (C == 0 || (int64_t)W * H == 0) return R2S_OK;
+    if (N == 0 || n_isects == 0) {
+        cudaMemsetAsync(image, 0, (size_t)C * W * H * 4, stream);
+        return check_launch("raster_splats_fwd");
+    }
+    if (int rc = check_tiles(C, W, H, T, ntx, nty)) return rc;
+    RasterSrc<float> src{(const float4*)splats, nullptr, nullptr, nullptr, nullptr};
+    return launch_raster_fwd<float, true>(src, offsets, flatten_ids, C, n_isects, W, H, T, ntx,
+                                          nty, image, stream);
+}
+
+extern "C" int r2s_raster_splats_bwd_f32(const float* splats, const int32_t* offsets,
+                                         const int32_t* flatten_ids, const float* v_image,
+                                         int64_t C, int64_t N, int64_t n_isects, uint32_t W,
+                                         uint32_t H, uint32_t T, uint32_t ntx, uint32_t nty,
+                                         int with_abs, float* stats, r2s_stream_t stream) {
+    R2S_REQUIRE(C >= 0 && N >= 0 && n_isects >= 0, "raster_splats_bwd: negative size");
+    if (C * N == 0) return R2S_OK;
+    if ((int64_t)W * H == 0) {
+        cudaMemsetAsync(stats, 0, (size_t)C * N * 32, stream);
+        return check_launch("raster_splats_bwd");
+    }
+    if (int rc = check_tiles(C, W, H, T, ntx, nty)) return rc;
+    RasterSrc<float> src{(const float4*)splats, nullptr, nullptr, nullptr, nullptr};
+    return launch_raster_bwd<float, true, 0>(src, offsets, flatten_ids, v_image, C, N, n_isects, W,
+                                             H, T, ntx, nty, with_abs, stats, stream);
+}

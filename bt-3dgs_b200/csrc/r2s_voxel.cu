@@ -1,0 +1,599 @@
+// 3D voxelization forward and backward.
+//
+// Forward (reference: csrc/VoxelizeToVoxelsFwd.cu:68-221): one CTA per brick,
+// one thread per voxel.  Threads are laid out x-fastest (the reference maps
+// threadIdx.x to z, VoxelizeToVoxelsFwd.cu:98-108, which makes every store
+// stride dim1*dim2); here a warp owns an 8x4x1 voxel row block, its stores
+// are contiguous 32-byte segments, and it evaluates only the staged
+// Gaussians whose cut-off box (alpha >= 1e-6) reaches its voxels.
+//
+// Backward (reference: csrc/VoxelizeToVoxelsBwd.cu:70-250 and 321-441): one
+// CTA per brick with the brick's upstream gradient in shared memory; warps
+// take whole Gaussians, walk the voxel box that can contribute and reduce ten
+// moments of the contributing voxels,
+//   S0 = sum v e, S_i = sum v e d_i, S_ij = sum v e d_i d_j (i <= j),
+// which map linearly to the reference gradients:
+//   v_means3d = w Q (Sx, Sy, Sz),   v_opacity = S0,
+//   v_conics  = -w (Sxx/2, Sxy, Sxz, Syy/2, Syz, Szz/2).
+//
+// Z-slabs: the fused entry points take a brick-layer range and a volume
+// pointer at the slab's first voxel row, so one GPU can voxelize only its
+// slab of the global grid with keys and offsets of the global binning.
+#include <math_constants.h>
+
+#include <algorithm>
+
+#include "r2s_common.cuh"
+
+namespace r2s {
+
+namespace {
+
+constexpr float kLog2eV = 1.4426950408889634f;
+constexpr float kAlphaMin3D = 1e-6f;
+
+__host__ __device__ __forceinline__ size_t al16v(size_t x) { return (x + 15) & ~size_t(15); }
+
+__device__ __forceinline__ void cull_range_v(float m, float e, float origin, int lim, int& lo,
+                                             int& hi) {
+    if (!(e >= 0.f)) {
+        lo = 1;
+        hi = 0;
+        return;
+    }
+    if (!isfinite(m) || isinf(e)) {
+        lo = 0;
+        hi = lim;
+        return;
+    }
+    const float flo = fmaxf(m - e - origin - 0.5f, 0.0f);
+    const float fhi = fminf(m + e - origin - 0.5f, static_cast<float>(lim));
+    if (flo > fhi) {
+        lo = 1;
+        hi = 0;
+        return;
+    }
+    lo = static_cast<int>(ceilf(flo));
+    hi = static_cast<int>(floorf(fhi));
+}
+
+// Cut-off extents of w*exp(-sigma) >= thresh from a 3D conic (symmetric
+// inverse covariance, upper triangle c00 c01 c02 c11 c12 c22).
+__device__ __forceinline__ void conic3_cull(const float q[6], float amp, float thresh, float e[3]) {
+    bool nan = isnan(amp);
+#pragma unroll
+    for (int k = 0; k < 6; ++k) nan |= isnan(q[k]);
+    if (nan) {
+        e[0] = e[1] = e[2] = CUDART_INF_F;
+        return;
+    }
+    const float aa = fabsf(amp);
+    if (!(aa >= thresh)) {
+        e[0] = e[1] = e[2] = -1.f;
+        return;
+    }
+    // covariance = inverse(conic) by cofactors
+    const float c00 = q[3] * q[5] - q[4] * q[4];
+    const float c11 = q[0] * q[5] - q[2] * q[2];
+    const float c22 = q[0] * q[3] - q[1] * q[1];
+    const float c01 = q[2] * q[4] - q[1] * q[5];
+    const float c02 = q[1] * q[4] - q[2] * q[3];
+    const float det = q[0] * c00 + q[1] * c01 + q[2] * c02;
+    if (!(q[0] > 0.f && q[3] > 0.f && q[5] > 0.f && det > 0.f && c00 > 0.f && c11 > 0.f &&
+          c22 > 0.f)) {
+        e[0] = e[1] = e[2] = CUDART_INF_F;
+        return;
+    }
+    const float cond = (q[0] * q[3] * q[5]) / det;
+    if (!isfinite(cond) || cond > 1e6f) {
+        e[0] = e[1] = e[2] = CUDART_INF_F;
+        return;
+    }
+    const float s_cut = logf(aa / thresh) * 1.0001f + 1e-4f;
+    const float rel = 1.0f + 1e-4f + 4e-7f * cond;
+    e[0] = sqrtf(2.0f * s_cut * (c00 / det) * rel) * 1.0001f + 1e-3f;
+    e[1] = sqrtf(2.0f * s_cut * (c11 / det) * rel) * 1.0001f + 1e-3f;
+    e[2] = sqrtf(2.0f * s_cut * (c22 / det) * rel) * 1.0001f + 1e-3f;
+}
+
+template <typename S>
+struct VoxSrc {
+    const float4* vsplats;  // fused float32 records [N][4]
+    const S* means3d;       // [N][3]
+    const S* conics;        // [N][6]
+    const S* opac;          // [N]
+};
+
+template <typename S, bool SPLATS>
+__device__ __forceinline__ void load_vgauss(const VoxSrc<S>& src, int64_t g, S m[3], S q[6], S& w,
+                                            float e[3]) {
+    if constexpr (SPLATS) {
+        const float4 a = src.vsplats[4 * g], b = src.vsplats[4 * g + 1],
+                     c = src.vsplats[4 * g + 2], d = src.vsplats[4 * g + 3];
+        m[0] = a.x; m[1] = a.y; m[2] = a.z;
+        q[0] = a.w; q[1] = b.x; q[2] = b.y; q[3] = b.z; q[4] = b.w; q[5] = c.x;
+        w = c.y;
+        e[0] = c.z; e[1] = c.w; e[2] = d.x;
+    } else {
+#pragma unroll
+        for (int k = 0; k < 3; ++k) m[k] = src.means3d[3 * g + k];
+#pragma unroll
+        for (int k = 0; k < 6; ++k) q[k] = src.conics[6 * g + k];
+        w = src.opac[g];
+        float qf[6];
+#pragma unroll
+        for (int k = 0; k < 6; ++k) qf[k] = (float)q[k];
+        conic3_cull(qf, (float)w, kAlphaMin3D, e);
+    }
+}
+
+struct BrickGeom {
+    int T;
+    int nthr;  // T^3
+    __device__ __forceinline__ void voxel(int tid, int& lx, int& ly, int& lz) const {
+        lz = tid / (T * T);
+        const int r = tid - lz * T * T;
+        ly = r / T;
+        lx = r - ly * T;
+    }
+};
+
+// ===========================================================================
+// Forward
+// ===========================================================================
+template <typename S, bool SPLATS>
+__global__ void voxel_fwd_kernel(VoxSrc<S> src, const int32_t* __restrict__ offsets,
+                                 const int32_t* __restrict__ flatten_ids, int64_t n_keys,
+                                 int64_t n_isects, uint32_t dim2, uint32_t dim1, uint32_t dim0,
+                                 BrickGeom geo, uint32_t nt2, uint32_t nt1, uint32_t layer_begin,
+                                 S* __restrict__ vol) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int nthr = geo.nthr, T = geo.T;
+    const size_t arr = al16v((size_t)nthr * sizeof(S));
+    S* s_p[10];
+#pragma unroll
+    for (int k = 0; k < 10; ++k) s_p[k] = reinterpret_cast<S*>(smem_raw + k * arr);
+    uint32_t* s_mask = reinterpret_cast<uint32_t*>(smem_raw + 10 * arr);
+    const int n_warps = (nthr + 31) >> 5;
+    const size_t mask_bytes = al16v((size_t)max(nthr, n_warps * 6) * 4);
+    uint2* s_box = reinterpret_cast<uint2*>(smem_raw + 10 * arr + mask_bytes);
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t bx = blockIdx.x, by = blockIdx.y, bz_local = blockIdx.z;
+    const uint32_t bz = bz_local + layer_begin;
+    const int64_t key = ((int64_t)bz_local * nt1 + by) * nt2 + bx;
+    const int X0 = bx * T, Y0 = by * T, Z0 = bz * T;
+    const int xmax = min(T - 1, (int)dim2 - 1 - X0);
+    const int ymax = min(T - 1, (int)dim1 - 1 - Y0);
+    const int zmax = min(T - 1, (int)dim0 - 1 - Z0);
+    int lx, ly, lz;
+    geo.voxel(tid, lx, ly, lz);
+    const bool inside = lx <= xmax && ly <= ymax && lz <= zmax;
+    {
+        // per-warp voxel bounding box of the inside voxels, built with shared
+        // atomics (exact for partial warps too); s_mask doubles as scratch
+        int* bb = reinterpret_cast<int*>(s_mask);  // [n_warps][6]
+        for (int i = tid; i < n_warps * 6; i += nthr) bb[i] = (i % 6) & 1 ? -1 : 255;
+        __syncthreads();
+        if (inside) {
+            atomicMin(&bb[warp * 6 + 0], lx);
+            atomicMax(&bb[warp * 6 + 1], lx);
+            atomicMin(&bb[warp * 6 + 2], ly);
+            atomicMax(&bb[warp * 6 + 3], ly);
+            atomicMin(&bb[warp * 6 + 4], lz);
+            atomicMax(&bb[warp * 6 + 5], lz);
+        }
+        __syncthreads();
+        if (tid < n_warps) {
+            const int* q = bb + tid * 6;
+            uint2 b;
+            if (q[1] < 0) {
+                b.x = 0x00ff00ffu;  // empty: lo 255 > hi 0
+                b.y = 0x000000ffu;
+            } else {
+                b.x = (uint32_t)q[0] | ((uint32_t)q[1] << 8) | ((uint32_t)q[2] << 16) |
+                      ((uint32_t)q[3] << 24);
+                b.y = (uint32_t)q[4] | ((uint32_t)q[5] << 8);
+            }
+            s_box[tid] = b;
+        }
+        __syncthreads();
+    }
+    const S px = static_cast<S>(X0 + lx) + static_cast<S>(0.5);
+    const S py = static_cast<S>(Y0 + ly) + static_cast<S>(0.5);
+    const S pz = static_cast<S>(Z0 + lz) + static_cast<S>(0.5);
+    const int start = offsets[key];
+    const int end = key + 1 < n_keys ? offsets[key + 1] : (int)n_isects;
+    const unsigned wmask = (nthr - warp * 32) >= 32 ? 0xffffffffu : ((1u << (nthr - warp * 32)) - 1u);
+    S acc = static_cast<S>(0);
+    __syncthreads();
+
+    for (int b0 = start; b0 < end; b0 += nthr) {
+        const int n = min(nthr, end - b0);
+        __syncthreads();
+        if (tid < n) {
+            const int64_t g = flatten_ids[b0 + tid];
+            S m[3], q[6], w;
+            float e[3];
+            load_vgauss<S, SPLATS>(src, g, m, q, w, e);
+            int xl, xh, yl, yh, zl, zh;
+            cull_range_v((float)m[0], e[0], (float)X0, xmax, xl, xh);
+            cull_range_v((float)m[1], e[1], (float)Y0, ymax, yl, yh);
+            cull_range_v((float)m[2], e[2], (float)Z0, zmax, zl, zh);
+            uint32_t msk = 0;
+            if (xl <= xh && yl <= yh && zl <= zh) {
+                for (int wv = 0; wv < n_warps; ++wv) {
+                    const uint2 b = s_box[wv];
+                    const int bx0 = b.x & 0xff, bx1 = (b.x >> 8) & 0xff;
+                    const int by0 = (b.x >> 16) & 0xff, by1 = b.x >> 24;
+                    const int bz0 = b.y & 0xff, bz1 = (b.y >> 8) & 0xff;
+                    if (xl <= bx1 && xh >= bx0 && yl <= by1 && yh >= by0 && zl <= bz1 && zh >= bz0)
+                        msk |= 1u << wv;
+                }
+            }
+            s_p[0][tid] = m[0];
+            s_p[1][tid] = m[1];
+            s_p[2][tid] = m[2];
+            if constexpr (std::is_same<S, float>::value) {
+                s_p[3][tid] = 0.5f * kLog2eV * q[0];
+                s_p[4][tid] = kLog2eV * q[1];
+                s_p[5][tid] = kLog2eV * q[2];
+                s_p[6][tid] = 0.5f * kLog2eV * q[3];
+                s_p[7][tid] = kLog2eV * q[4];
+                s_p[8][tid] = 0.5f * kLog2eV * q[5];
+            } else {
+#pragma unroll
+                for (int k = 0; k < 6; ++k) s_p[3 + k][tid] = q[k];
+            }
+            s_p[9][tid] = w;
+            s_mask[tid] = msk;
+        }
+        __syncthreads();
+        for (int c0 = 0; c0 < n; c0 += 32) {
+            const int j = c0 + lane;
+            unsigned bits = __ballot_sync(wmask, j < n && ((s_mask[j] >> warp) & 1u));
+            while (bits) {
+                const int t = c0 + __ffs(bits) - 1;
+                bits &= bits - 1;
+                const S dx = px - s_p[0][t];
+                const S dy = py - s_p[1][t];
+                const S dz = pz - s_p[2][t];
+                if constexpr (std::is_same<S, float>::value) {
+                    const float u = fmaf(s_p[3][t], dx, fmaf(s_p[4][t], dy, s_p[5][t] * dz));
+                    const float v = fmaf(s_p[6][t], dy, s_p[7][t] * dz);
+                    const float s = fmaf(dx, u, fmaf(dy, v, s_p[8][t] * dz * dz));
+                    const float al = s_p[9][t] * exp2f(-s);
+                    acc += (s < 0.f || fabsf(al) < kAlphaMin3D) ? 0.f : al;
+                } else {
+                    const S sig = static_cast<S>(0.5) * (s_p[3][t] * dx * dx + s_p[6][t] * dy * dy +
+                                                         s_p[8][t] * dz * dz) +
+                                  s_p[4][t] * dx * dy + s_p[5][t] * dx * dz + s_p[7][t] * dy * dz;
+                    const S al = s_p[9][t] * expf_neg(sig);
+                    const bool skip = sig < static_cast<S>(0) ||
+                                      fabsf(static_cast<float>(al)) < static_cast<S>(1e-6);
+                    acc += skip ? static_cast<S>(0) : al;
+                }
+            }
+        }
+    }
+    if (inside)
+        vol[((int64_t)(Z0 + lz - (int)layer_begin * T) * dim1 + (Y0 + ly)) * dim2 + X0 + lx] = acc;
+}
+
+// ===========================================================================
+// Backward statistics
+// ===========================================================================
+template <typename S>
+__device__ __forceinline__ void vstats_red(S* dst, const S v[10]) {
+    if constexpr (std::is_same<S, float>::value) {
+        red_add_v4(dst, v[0], v[1], v[2], v[3]);
+        red_add_v4(dst + 4, v[4], v[5], v[6], v[7]);
+        red_add_v2(dst + 8, v[8], v[9]);
+    } else {
+        for (int k = 0; k < 10; ++k) atomicAdd(dst + k, v[k]);
+    }
+}
+
+template <typename S, bool SPLATS, int EXPMODE>
+__global__ void voxel_bwd_kernel(VoxSrc<S> src, const int32_t* __restrict__ offsets,
+                                 const int32_t* __restrict__ flatten_ids, int64_t n_keys,
+                                 int64_t n_isects, const S* __restrict__ v_vol, uint32_t dim2,
+                                 uint32_t dim1, uint32_t dim0, int T, uint32_t nt2, uint32_t nt1,
+                                 uint32_t layer_begin, S* __restrict__ stats) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int nthr = blockDim.x;
+    const int TT = T * T, TTT = T * T * T;
+    S* s_v = reinterpret_cast<S*>(smem_raw);
+    const size_t arr = al16v((size_t)nthr * sizeof(S));
+    unsigned char* base = smem_raw + al16v((size_t)TTT * sizeof(S));
+    S* s_p[10];
+#pragma unroll
+    for (int k = 0; k < 10; ++k) s_p[k] = reinterpret_cast<S*>(base + k * arr);
+    int32_t* s_g = reinterpret_cast<int32_t*>(base + 10 * arr);
+    uint2* s_box = reinterpret_cast<uint2*>(base + 10 * arr + al16v((size_t)nthr * 4));
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int n_warps = nthr >> 5;
+    const uint32_t bx = blockIdx.x, by = blockIdx.y, bz_local = blockIdx.z;
+    const uint32_t bz = bz_local + layer_begin;
+    const int64_t key = ((int64_t)bz_local * nt1 + by) * nt2 + bx;
+    const int X0 = bx * T, Y0 = by * T, Z0 = bz * T;
+    const int xmax = min(T - 1, (int)dim2 - 1 - X0);
+    const int ymax = min(T - 1, (int)dim1 - 1 - Y0);
+    const int zmax = min(T - 1, (int)dim0 - 1 - Z0);
+    const int start = offsets[key];
+    const int end = key + 1 < n_keys ? offsets[key + 1] : (int)n_isects;
+    if (start >= end) return;
+    const int64_t zoff = (int64_t)layer_begin * T;
+    for (int p = tid; p < TTT; p += nthr) {
+        const int z = p / TT, r = p - z * TT, y = r / T, x = r - y * T;
+        s_v[p] = (x <= xmax && y <= ymax && z <= zmax)
+                     ? v_vol[((Z0 + z - zoff) * dim1 + (Y0 + y)) * (int64_t)dim2 + X0 + x]
+                     : static_cast<S>(0);
+    }
+    for (int b0 = start; b0 < end; b0 += nthr) {
+        const int n = min(nthr, end - b0);
+        __syncthreads();
+        if (tid < n) {
+            const int64_t g = flatten_ids[b0 + tid];
+            S m[3], q[6], w;
+            float e[3];
+            load_vgauss<S, SPLATS>(src, g, m, q, w, e);
+            int xl, xh, yl, yh, zl, zh;
+            cull_range_v((float)m[0], e[0], (float)X0, xmax, xl, xh);
+            cull_range_v((float)m[1], e[1], (float)Y0, ymax, yl, yh);
+            cull_range_v((float)m[2], e[2], (float)Z0, zmax, zl, zh);
+            if (xl > xh || yl > yh || zl > zh) xl = 1, xh = 0, yl = yh = zl = zh = 0;
+#pragma unroll
+            for (int k = 0; k < 3; ++k) s_p[k][tid] = m[k];
+#pragma unroll
+            for (int k = 0; k < 6; ++k) s_p[3 + k][tid] = q[k];
+            s_p[9][tid] = w;
+            s_g[tid] = (int32_t)g;
+            uint2 b;
+            b.x = (uint32_t)xl | ((uint32_t)xh << 8) | ((uint32_t)yl << 16) | ((uint32_t)yh << 24);
+            b.y = (uint32_t)zl | ((uint32_t)zh << 8);
+            s_box[tid] = b;
+        }
+        __syncthreads();
+        for (int t = warp; t < n; t += n_warps) {
+            const uint2 b = s_box[t];
+            const int xl = b.x & 0xff, xh = (b.x >> 8) & 0xff;
+            if (xl > xh) continue;
+            const int yl = (b.x >> 16) & 0xff, yh = b.x >> 24;
+            const int zl = b.y & 0xff, zh = (b.y >> 8) & 0xff;
+            const int wx = xh - xl + 1, wy = yh - yl + 1;
+            const int wxy = wx * wy;
+            const int npx = wxy * (zh - zl + 1);
+            const float inv_wxy = 1.0f / (float)wxy, inv_wx = 1.0f / (float)wx;
+            const S mx = s_p[0][t], my = s_p[1][t], mz = s_p[2][t];
+            const S q0 = s_p[3][t], q1 = s_p[4][t], q2 = s_p[5][t], q3 = s_p[6][t],
+                    q4 = s_p[7][t], q5 = s_p[8][t], w = s_p[9][t];
+            S acc[10] = {0, 0, 0, 0, 0, 0, 0, 0, 0, 0};
+            for (int p = lane; p < npx; p += 32) {
+                const int zz = __float2int_rz(((float)p + 0.5f) * inv_wxy);
+                const int r = p - zz * wxy;
+                const int yy = __float2int_rz(((float)r + 0.5f) * inv_wx);
+                const int xx = r - yy * wx;
+                const int lx = xl + xx, ly = yl + yy, lz = zl + zz;
+                const S v = s_v[(lz * T + ly) * T + lx];
+                const S dx = static_cast<S>(X0 + lx) + static_cast<S>(0.5) - mx;
+                const S dy = static_cast<S>(Y0 + ly) + static_cast<S>(0.5) - my;
+                const S dz = static_cast<S>(Z0 + lz) + static_cast<S>(0.5) - mz;
+                S e;
+                bool skip;
+                if constexpr (std::is_same<S, float>::value) {
+                    const float A = 0.5f * kLog2eV * q0, B = kLog2eV * q1, Cq = kLog2eV * q2;
+                    const float D = 0.5f * kLog2eV * q3, E = kLog2eV * q4, F = 0.5f * kLog2eV * q5;
+                    const float u = fmaf(A, dx, fmaf(B, dy, Cq * dz));
+                    const float vv = fmaf(D, dy, E * dz);
+                    const float s = fmaf(dx, u, fmaf(dy, vv, F * dz * dz));
+                    e = exp2f(-s);
+                    skip = s < 0.f || fabsf(w * e) < kAlphaMin3D;
+                } else {
+                    const S sig = static_cast<S>(0.5) * (q0 * dx * dx + q3 * dy * dy + q5 * dz * dz) +
+                                  q1 * dx * dy + q2 * dx * dz + q4 * dy * dz;
+                    if constexpr (EXPMODE == 0) {
+                        e = expf_neg(sig);
+                        skip = sig < static_cast<S>(0) ||
+                               fabsf(static_cast<float>(w * e)) < static_cast<S>(1e-6);
+                    } else {
+                        e = exp(-sig);
+                        skip = sig < static_cast<S>(0) || fabs(w * e) < static_cast<S>(1e-6);
+                    }
+                }
+                const S ve = skip ? static_cast<S>(0) : v * e;
+                const S vx = ve * dx, vy = ve * dy, vz = ve * dz;
+                acc[0] += ve;
+                acc[1] += vx;
+                acc[2] += vy;
+                acc[3] += vz;
+                acc[4] += vx * dx;
+                acc[5] += vx * dy;
+                acc[6] += vx * dz;
+                acc[7] += vy * dy;
+                acc[8] += vy * dz;
+                acc[9] += vz * dz;
+            }
+#pragma unroll
+            for (int k = 0; k < 10; ++k) acc[k] = warp_sum(acc[k]);
+            if (lane == 0) vstats_red(stats + (int64_t)s_g[t] * 12, acc);
+        }
+    }
+}
+
+template <typename S>
+__global__ void voxel_unpack_kernel(const S* __restrict__ stats, const S* __restrict__ conics,
+                                    const S* __restrict__ opac, int64_t N, S* __restrict__ v_m3,
+                                    S* __restrict__ v_con, S* __restrict__ v_op) {
+    const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (g >= N) return;
+    const S* st = stats + g * 12;
+    const S* q = conics + g * 6;
+    const S w = opac[g];
+    v_m3[3 * g] = w * (q[0] * st[1] + q[1] * st[2] + q[2] * st[3]);
+    v_m3[3 * g + 1] = w * (q[1] * st[1] + q[3] * st[2] + q[4] * st[3]);
+    v_m3[3 * g + 2] = w * (q[2] * st[1] + q[4] * st[2] + q[5] * st[3]);
+    const S h = static_cast<S>(0.5);
+    v_con[6 * g] = -w * h * st[4];
+    v_con[6 * g + 1] = -w * st[5];
+    v_con[6 * g + 2] = -w * st[6];
+    v_con[6 * g + 3] = -w * h * st[7];
+    v_con[6 * g + 4] = -w * st[8];
+    v_con[6 * g + 5] = -w * h * st[9];
+    v_op[g] = st[0];
+}
+
+int check_bricks(uint32_t T, uint32_t nt2, uint32_t nt1, uint32_t layers) {
+    R2S_REQUIRE(T > 0 && T * T * T <= 1024,
+                "3D tile_size must be positive with tile_size**3 <= 1024");
+    R2S_REQUIRE(nt2 > 0 && nt1 > 0 && nt2 <= 65535 && nt1 <= 65535 && layers <= 65535,
+                "voxelize: brick grid out of range");
+    return R2S_OK;
+}
+
+template <typename S, bool SPLATS>
+int launch_voxel_fwd(const VoxSrc<S>& src, const int32_t* offsets, const int32_t* flatten_ids,
+                     int64_t n_isects, uint32_t dim2, uint32_t dim1, uint32_t dim0, uint32_t T,
+                     uint32_t nt2, uint32_t nt1, uint32_t layer_begin, uint32_t layer_end, S* vol,
+                     cudaStream_t stream) {
+    BrickGeom geo;
+    geo.T = (int)T;
+    geo.nthr = (int)(T * T * T);
+    const int n_warps = (geo.nthr + 31) / 32;
+    const size_t smem = 10 * al16v((size_t)geo.nthr * sizeof(S)) +
+                        al16v((size_t)std::max(geo.nthr, n_warps * 6) * 4) + n_warps * 8;
+    auto kern = voxel_fwd_kernel<S, SPLATS>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const uint32_t layers = layer_end - layer_begin;
+    const dim3 grid(nt2, nt1, layers);
+    kern<<<grid, geo.nthr, smem, stream>>>(src, offsets, flatten_ids,
+                                           (int64_t)layers * nt1 * nt2, n_isects, dim2, dim1, dim0,
+                                           geo, nt2, nt1, layer_begin, vol);
+    return check_launch("voxelize_to_voxels_fwd");
+}
+
+template <typename S, bool SPLATS, int EXPMODE>
+int launch_voxel_bwd(const VoxSrc<S>& src, const int32_t* offsets, const int32_t* flatten_ids,
+                     const S* v_vol, int64_t N, int64_t n_isects, uint32_t dim2, uint32_t dim1,
+                     uint32_t dim0, uint32_t T, uint32_t nt2, uint32_t nt1, uint32_t layer_begin,
+                     uint32_t layer_end, S* stats, cudaStream_t stream) {
+    cudaMemsetAsync(stats, 0, (size_t)N * 12 * sizeof(S), stream);
+    if (n_isects == 0) return check_launch("voxelize_to_voxels_bwd");
+    const int nthr = 256;
+    const size_t smem = al16v((size_t)T * T * T * sizeof(S)) + 10 * al16v((size_t)nthr * sizeof(S)) +
+                        al16v((size_t)nthr * 4) + (size_t)nthr * 8;
+    auto kern = voxel_bwd_kernel<S, SPLATS, EXPMODE>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const uint32_t layers = layer_end - layer_begin;
+    const dim3 grid(nt2, nt1, layers);
+    kern<<<grid, nthr, smem, stream>>>(src, offsets, flatten_ids, (int64_t)layers * nt1 * nt2,
+                                       n_isects, v_vol, dim2, dim1, dim0, (int)T, nt2, nt1,
+                                       layer_begin, stats);
+    return check_launch("voxelize_to_voxels_bwd");
+}
+
+}  // namespace
+
+}  // namespace r2s
+
+using namespace r2s;
+
+extern "C" int r2s_voxelize_to_voxels_fwd(int dtype, const void* means3d, const void* conics,
+                                          const void* opacities, const int32_t* offsets,
+                                          const int32_t* flatten_ids, int64_t N, int64_t n_isects,
+                                          uint32_t dim2, uint32_t dim1, uint32_t dim0, uint32_t T,
+                                          uint32_t nt2, uint32_t nt1, uint32_t nt0, void* volume,
+                                          r2s_stream_t stream) {
+    R2S_REQUIRE(N >= 0 && n_isects >= 0, "voxelize_to_voxels_fwd: negative size");
+    const size_t es = dtype == R2S_F64 ? 8 : 4;
+    const int64_t nvox = (int64_t)dim0 * dim1 * dim2;
+    if (nvox == 0) return R2S_OK;
+    if (N == 0 || n_isects == 0) {
+        cudaMemsetAsync(volume, 0, nvox * es, stream);
+        return check_launch("voxelize_to_voxels_fwd");
+    }
+    if (int rc = check_bricks(T, nt2, nt1, nt0)) return rc;
+    R2S_REQUIRE((uint64_t)nt2 * T >= dim2 && (uint64_t)nt1 * T >= dim1 && (uint64_t)nt0 * T >= dim0,
+                "voxelize: brick grid does not cover the volume");
+    return R2S_DTYPE_DISPATCH(dtype, "voxelize_to_voxels_fwd", [&] {
+        VoxSrc<scalar_t> src{nullptr, (const scalar_t*)means3d, (const scalar_t*)conics,
+                             (const scalar_t*)opacities};
+        return launch_voxel_fwd<scalar_t, false>(src, offsets, flatten_ids, n_isects, dim2, dim1,
+                                                 dim0, T, nt2, nt1, 0, nt0, (scalar_t*)volume,
+                                                 stream);
+    });
+}
+
+extern "C" int r2s_voxelize_to_voxels_bwd(int dtype, int mode, const void* means3d,
+                                          const void* conics, const void* opacities,
+                                          const int32_t* offsets, const int32_t* flatten_ids,
+                                          const void* v_volume, int64_t N, int64_t n_isects,
+                                          uint32_t dim2, uint32_t dim1, uint32_t dim0, uint32_t T,
+                                          uint32_t nt2, uint32_t nt1, uint32_t nt0, void* stats,
+                                          void* v_means3d, void* v_conics, void* v_opacities,
+                                          r2s_stream_t stream) {
+    R2S_REQUIRE(N >= 0 && n_isects >= 0, "voxelize_to_voxels_bwd: negative size");
+    R2S_REQUIRE(mode == 0 || mode == 1, "voxelize_to_voxels_bwd: mode must be 0 or 1");
+    const size_t es = dtype == R2S_F64 ? 8 : 4;
+    if (N == 0) return R2S_OK;
+    if (n_isects == 0 || (int64_t)dim0 * dim1 * dim2 == 0) {
+        cudaMemsetAsync(v_means3d, 0, N * 3 * es, stream);
+        cudaMemsetAsync(v_conics, 0, N * 6 * es, stream);
+        cudaMemsetAsync(v_opacities, 0, N * es, stream);
+        return check_launch("voxelize_to_voxels_bwd");
+    }
+    if (int rc = check_bricks(T, nt2, nt1, nt0)) return rc;
+    return R2S_DTYPE_DISPATCH(dtype, "voxelize_to_voxels_bwd", [&] {
+        VoxSrc<scalar_t> src{nullptr, (const scalar_t*)means3d, (const scalar_t*)conics,
+                             (const scalar_t*)opacities};
+        int rc = mode == 0 ? launch_voxel_bwd<scalar_t, false, 0>(
+                                 src, offsets, flatten_ids, (const scalar_t*)v_volume, N, n_isects,
+                                 dim2, dim1, dim0, T, nt2, nt1, 0, nt0, (scalar_t*)stats, stream)
+                           : launch_voxel_bwd<scalar_t, false, 1>(
+                                 src, offsets, flatten_ids, (const scalar_t*)v_volume, N, n_isects,
+                                 dim2, dim1, dim0, T, nt2, nt1, 0, nt0, (scalar_t*)stats, stream);
+        if (rc) return rc;
+        voxel_unpack_kernel<scalar_t><<<grid_for(N), kThreads, 0, stream>>>(
+            (const scalar_t*)stats, (const scalar_t*)conics, (const scalar_t*)opacities, N,
+            (scalar_t*)v_means3d, (scalar_t*)v_conics, (scalar_t*)v_opacities);
+        return check_launch("voxelize_to_voxels_bwd");
+    });
+}
+
+extern "C" int r2s_voxel_splats_fwd_f32(const float* vsplats, const int32_t* offsets,
+                                        const int32_t* flatten_ids, int64_t N, int64_t n_isects,
+                                        uint32_t dim2, uint32_t dim1, uint32_t dim0, uint32_t T,
+                                        uint32_t nt2, uint32_t nt1, uint32_t nt0,
+                                        uint32_t layer_begin, uint32_t layer_end, float* volume,
+                                        r2s_stream_t stream) {
+    R2S_REQUIRE(N >= 0 && n_isects >= 0, "voxel_splats_fwd: negative size");
+    R2S_REQUIRE(layer_begin <= layer_end && layer_end <= nt0, "voxel_splats_fwd: bad layer range");
+    if (int rc = check_bricks(T, nt2, nt1, nt0)) return rc;
+    const int64_t zb = (int64_t)layer_begin * T;
+    const int64_t ze = std::min<int64_t>((int64_t)layer_end * T, dim0);
+    if (ze <= zb || (int64_t)dim1 * dim2 == 0) return R2S_OK;
+    if (N == 0 || n_isects == 0) {
+        cudaMemsetAsync(volume, 0, (size_t)(ze - zb) * dim1 * dim2 * 4, stream);
+        return check_launch("voxel_splats_fwd");
+    }
+    VoxSrc<float> src{(const float4*)vsplats, nullptr, nullptr, nullptr};
+    return launch_voxel_fwd<float, true>(src, offsets, flatten_ids, n_isects, dim2, dim1, dim0, T,
+                                         nt2, nt1, layer_begin, layer_end, volume, stream);
+}
+
+extern "C" int r2s_voxel_splats_bwd_f32(const float* vsplats, const int32_t* offsets,
+                                        const int32_t* flatten_ids, const float* v_volume,
+                                        int64_t N, int64_t n_isects, uint32_t dim2, uint32_t dim1,
+                                        uint32_t dim0, uint32_t T, uint32_t nt2, uint32_t nt1,
+                                        uint32_t nt0, uint32_t layer_begin, uint32_t layer_end,
+                                        float* stats, r2s_stream_t stream) {
+    R2S_REQUIRE(N >= 0 && n_isects >= 0, "voxel_splats_bwd: negative size");
+    R2S_REQUIRE(layer_begin <= layer_end && layer_end <= nt0, "voxel_splats_bwd: bad layer range");
+    if (int rc = check_bricks(T, nt2, nt1, nt0)) return rc;
+    if (N == 0) return R2S_OK;
+    VoxSrc<float> src{(const float4*)vsplats, nullptr, nullptr, nullptr};
+    return launch_voxel_bwd<float, true, 0>(src, offsets, flatten_ids, v_volume, N, n_isects, dim2,
+                                            dim1, dim0, T, nt2, nt1, layer_begin, layer_end, stats,
+                                            stream);
+}

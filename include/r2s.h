@@ -1,0 +1,338 @@
+/*
+ * r2s.h - C ABI of libr2s.so, the sm_100a implementation of the r2splat
+ * Gaussian backend (cone-beam projection rendering, voxelization and their
+ * first-order VJPs).
+ *
+ * The reference binds its operators through pybind11
+ * (r2splat/cuda/csrc/ext.cpp:7-27, declarations r2splat/cuda/include/Ops.h:9-79).
+ * This header exposes the same 18 operators as plain C functions: device
+ * pointers, element counts, scalar parameters and a CUDA stream; no torch types.
+ * The Python package r2splat (r2splat/cuda/_wrapper.py) binds them through
+ * ctypes and keeps the reference's Python signatures.  Fused entry points used
+ * by the r2splat.ops fast path follow the 18 operators.
+ *
+ * Conventions
+ *   - Every function returns R2S_OK (0) or an error code; r2s_last_error()
+ *     returns the message of the last failure on the calling thread.
+ *   - All pointers are device pointers unless stated otherwise; all work is
+ *     enqueued on `stream` and nothing synchronizes the host.
+ *   - `dtype` selects float32 (R2S_F32) or float64 (R2S_F64) for every
+ *     floating-point buffer of the call; integer buffers are int32 unless
+ *     stated (isect ids are int64, as in the reference).
+ *   - Outputs are written in full (callers need not zero them) unless the
+ *     comment says "accumulated".
+ *   - The library never allocates device memory: scratch space ("workspace")
+ *     is passed in by the caller and sized by the matching *_workspace_bytes().
+ */
+#ifndef R2S_H
+#define R2S_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define R2S_API __attribute__((visibility("default")))
+#else
+#define R2S_API
+#endif
+
+typedef struct CUstream_st* r2s_stream_t; /* == cudaStream_t */
+
+enum { R2S_F32 = 0, R2S_F64 = 1 };
+enum {
+    R2S_OK = 0,
+    R2S_ERR_ARG = 1,         /* invalid argument (maps to RuntimeError, like TORCH_CHECK) */
+    R2S_ERR_CUDA = 2,        /* CUDA launch/runtime error */
+    R2S_ERR_CAPACITY = 3,    /* an index space exceeds int32 (reference limit) */
+    R2S_ERR_UNSUPPORTED = 4  /* shape outside what this build supports */
+};
+
+R2S_API const char* r2s_version(void);
+/* Copies the last error message of this thread into buf (NUL-terminated,
+ * truncated to len-1 bytes); returns the full message length. */
+R2S_API size_t r2s_last_error(char* buf, size_t len);
+
+/* ------------------------------------------------------------------------
+ * Parameter transform: quats [N,4] (w,x,y,z; normalized in-kernel), raw
+ * scales [N,3] -> covars [N,6] upper triangle (00,01,02,11,12,22),
+ * max_scales [N].  Replaces parameter_transform_fwd_tensor
+ * (r2splat/cuda/include/Ops.h:9-10; csrc/ParameterTransform.cpp:33-83).
+ */
+R2S_API int r2s_parameter_transform_fwd(int dtype, const void* quats, const void* raw_scales,
+                                double scale_min, double scale_max, void* covars,
+                                void* max_scales, int64_t n, r2s_stream_t stream);
+/* VJP of the above.  Replaces parameter_transform_bwd_tensor
+ * (Ops.h:11-13; csrc/ParameterTransform.cpp:89-143). */
+R2S_API int r2s_parameter_transform_bwd(int dtype, const void* quats, const void* raw_scales,
+                                double scale_min, double scale_max, const void* v_covars,
+                                void* v_quats, void* v_raw_scales, int64_t n,
+                                r2s_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * World -> image cone-beam projection.  means [N,3], covars [N,6],
+ * viewmats [C,4,4] row-major, Ks [C,3,3] -> means2d [C,N,2],
+ * cov2d [C,N,6] (3x3 ray-space covariance, upper triangle), radii [C,N,2].
+ * Replaces world_to_image_projection_fwd_tensor
+ * (Ops.h:31-34; csrc/WorldToImageProjection.cpp:37-120).
+ */
+R2S_API int r2s_world_to_image_projection_fwd(int dtype, const void* means, const void* covars,
+                                      const void* viewmats, const void* Ks, int64_t C,
+                                      int64_t N, uint32_t width, uint32_t height,
+                                      double eps2d, double radius_clip, void* means2d,
+                                      void* cov2d, int32_t* radii, r2s_stream_t stream);
+/* VJP: v_means2d [C,N,2], v_cov2d [C,N,6] -> v_means [N,3], v_covars [N,6]
+ * (summed over views).  Replaces world_to_image_projection_bwd_tensor
+ * (Ops.h:35-38; csrc/WorldToImageProjection.cpp:126-206). */
+R2S_API int r2s_world_to_image_projection_bwd(int dtype, const void* means, const void* covars,
+                                      const void* viewmats, const void* Ks, int64_t C,
+                                      int64_t N, uint32_t width, uint32_t height,
+                                      const void* v_means2d, const void* v_cov2d,
+                                      void* v_means, void* v_covars, r2s_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Conics and line-integral factor: cov2d [T,6] (T = C*N) -> conics [T,3],
+ * mus [T].  Replaces conics_mu_fwd_tensor (Ops.h:25-26; csrc/ConicsMu.cpp:34-80).
+ */
+R2S_API int r2s_conics_mu_fwd(int dtype, const void* cov2d, double eps, void* conics, void* mus,
+                      int64_t total, r2s_stream_t stream);
+/* Replaces conics_mu_bwd_tensor (Ops.h:27-29; csrc/ConicsMu.cpp:86-159). */
+R2S_API int r2s_conics_mu_bwd(int dtype, const void* cov2d, double eps, const void* conics,
+                      const void* mus, const void* v_conics, const void* v_mus,
+                      void* v_cov2d, int64_t total, r2s_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * World -> volume mapping.  means [N,3], covars [N,6], ranges [3], centers [3]
+ * (device) -> means3d [N,3], conics [N,6], radii [N,3].  max_scales is
+ * accepted for interface parity and unused, as in the reference.
+ * Replaces world_to_volume_mapping_fwd_tensor
+ * (Ops.h:40-44; csrc/WorldToVolumeMapping.cpp:36-112).
+ */
+R2S_API int r2s_world_to_volume_mapping_fwd(int dtype, const void* means, const void* covars,
+                                    const void* max_scales, const void* ranges,
+                                    const void* centers, int64_t N, uint32_t dim2,
+                                    uint32_t dim1, uint32_t dim0, double eps3d,
+                                    double radius_clip, void* means3d, void* conics,
+                                    int32_t* radii, r2s_stream_t stream);
+/* Replaces world_to_volume_mapping_bwd_tensor
+ * (Ops.h:45-48; csrc/WorldToVolumeMapping.cpp:118-192). */
+R2S_API int r2s_world_to_volume_mapping_bwd(int dtype, const void* means, const void* covars,
+                                    const void* ranges, const void* centers, int64_t N,
+                                    uint32_t dim2, uint32_t dim1, uint32_t dim0,
+                                    double eps3d, const void* v_means3d,
+                                    const void* v_conics, void* v_means, void* v_covars,
+                                    r2s_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Tile binning.  The reference's isect_tiles (Ops.h:15-16;
+ * csrc/IsectTiles.cpp:30-170) counts tiles per (view, Gaussian), scans,
+ * emits (key = view*n_tiles + tile, value = view*N + g) and radix-sorts the
+ * keys stably.  Here the same sorted arrays are produced by a stable
+ * counting placement in two calls with one host read of n_isects between
+ * them (the reference syncs at the same point, IsectTiles.cpp:100):
+ *
+ *   r2s_isect_tiles_prepare  -> tiles_per_gauss [C,N], rects [C*N] (8 B
+ *                               each), tile_offsets [C,nty,ntx] (int32),
+ *                               *n_isects_dev (one int64, device)
+ *   r2s_bin_place            -> flatten_ids [n_isects] (int32) and, if
+ *                               isect_ids != NULL, isect_ids [n_isects]
+ *                               (int64), bit-identical to the reference's
+ *                               sorted outputs.
+ *
+ * radii is [C,N,2] when radii_is_rect, else [C,N].  `workspace` must hold
+ * r2s_bin_workspace_bytes(C, N, nty*ntx, 0) bytes.
+ */
+R2S_API int64_t r2s_bin_workspace_bytes(int64_t n_segments, int64_t n_items,
+                                int64_t tiles_per_segment, int layered);
+R2S_API int r2s_isect_tiles_prepare(int dtype, const void* means2d, const int32_t* radii,
+                            int radii_is_rect, int64_t C, int64_t N, uint32_t tile_size,
+                            uint32_t n_tiles_w, uint32_t n_tiles_h,
+                            int32_t* tiles_per_gauss, void* rects, void* workspace,
+                            int64_t workspace_bytes, int32_t* tile_offsets,
+                            int64_t* n_isects_dev, r2s_stream_t stream);
+/* 3D counterpart of the above for isect_tiles_3d (Ops.h:20-21;
+ * csrc/IsectTiles3D.cpp:31-162): means3d [N,3], radii [N,3] ->
+ * tiles_per_gauss [N], rects [N] (16 B each), tile_offsets [nt0,nt1,nt2],
+ * *n_isects_dev.  The 3D key space is handled as nt0 layers of nt1*nt2 tiles,
+ * so the workspace is r2s_bin_workspace_bytes(nt0, N, nt1*nt2, 1). */
+R2S_API int r2s_isect_tiles_3d_prepare(int dtype, const void* means3d, const int32_t* radii,
+                               int64_t N, uint32_t tile_size, uint32_t nt2, uint32_t nt1,
+                               uint32_t nt0, int32_t* tiles_per_gauss, void* rects,
+                               void* workspace, int64_t workspace_bytes,
+                               int32_t* tile_offsets, int64_t* n_isects_dev,
+                               r2s_stream_t stream);
+/* Places the records after a *_prepare call.  layered = 0 for the 2D path
+ * (segments = views, items = C*N) and 1 for the 3D path (segments = z
+ * layers, items = N Gaussians).  key_base/segment_base let a caller bin a
+ * contiguous range of segments (z-slab sharding); pass 0 for the full key
+ * space. */
+R2S_API int r2s_bin_place(const void* rects, int64_t n_segments, int64_t n_items,
+                  int64_t tiles_per_segment, uint32_t tiles_x, int layered,
+                  int64_t segment_base, const void* workspace, int64_t workspace_bytes,
+                  const int32_t* tile_offsets, int64_t n_isects, int32_t* flatten_ids,
+                  int64_t* isect_ids, r2s_stream_t stream);
+/* Per-tile start offsets of a sorted key array.  Replaces
+ * isect_offset_encode_tensor (Ops.h:17-18; csrc/IsectTiles.cpp:176-215) and
+ * isect_offset_encode_3d_tensor (Ops.h:22-23; csrc/IsectTiles3D.cpp:168-204):
+ * offsets[k] = first index i with isect_ids[i] >= k, k in [0, n_keys). */
+R2S_API int r2s_isect_offset_encode(const int64_t* isect_ids, int64_t n_isects, int64_t n_keys,
+                            int32_t* offsets, r2s_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Additive X-ray rasterization (no alpha compositing):
+ * image[c,i,j] = sum over the tile's list of w*mu*exp(-sigma), skipping
+ * sigma < 0 and |alpha| < 1e-5.  Inputs are [C,N,...] flattened
+ * (means2d 2, conics 3, opacities 1, mus 1), tile_offsets [C,nty,ntx],
+ * flatten_ids [n_isects]; output image [C,H,W].  Replaces
+ * rasterize_to_pixels_fwd_tensor (Ops.h:50-53; csrc/RasterizeToPixels.cpp:25-115).
+ */
+R2S_API int r2s_rasterize_to_pixels_fwd(int dtype, const void* means2d, const void* conics,
+                                const void* opacities, const void* mus,
+                                const int32_t* tile_offsets, const int32_t* flatten_ids,
+                                int64_t C, int64_t N, int64_t n_isects, uint32_t width,
+                                uint32_t height, uint32_t tile_size, uint32_t n_tiles_w,
+                                uint32_t n_tiles_h, void* image, r2s_stream_t stream);
+/* VJP w.r.t. means2d, conics, opacities, mus (+ |d means2d| summed per
+ * pixel when v_means2d_abs != NULL).  Both reference modes map here:
+ * mode 0 = "pixel" (rasterize_to_pixels_bwd_tensor, Ops.h:54-58;
+ * RasterizeToPixels.cpp:121-223) and mode 1 = "primitive"
+ * (rasterize_to_pixels_bwd_per_gaussian_tensor, Ops.h:59-64;
+ * RasterizeToPixels.cpp:225-317).  The modes differ only in the precision
+ * of exp for float64 inputs, as in the reference.  `stats` is caller
+ * scratch of C*N*8 elements of dtype. */
+R2S_API int r2s_rasterize_to_pixels_bwd(int dtype, int mode, const void* means2d,
+                                const void* conics, const void* opacities, const void* mus,
+                                const int32_t* tile_offsets, const int32_t* flatten_ids,
+                                const void* v_image, int64_t C, int64_t N, int64_t n_isects,
+                                uint32_t width, uint32_t height, uint32_t tile_size,
+                                uint32_t n_tiles_w, uint32_t n_tiles_h, void* stats,
+                                void* v_means2d_abs, void* v_means2d, void* v_conics,
+                                void* v_opacities, void* v_mus, r2s_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Voxelization: vol[z,y,x] = sum over the brick's list of w*exp(-sigma)
+ * (6-term quadratic), skipping sigma < 0 and |alpha| < 1e-6.  means3d [N,3],
+ * conics [N,6], opacities [N], tile_offsets [nt0,nt1,nt2] -> vol
+ * [dim0,dim1,dim2].  Replaces voxelize_to_voxels_fwd_tensor
+ * (Ops.h:66-69; csrc/VoxelizeToVoxels.cpp:31-108).
+ */
+R2S_API int r2s_voxelize_to_voxels_fwd(int dtype, const void* means3d, const void* conics,
+                               const void* opacities, const int32_t* tile_offsets,
+                               const int32_t* flatten_ids, int64_t N, int64_t n_isects,
+                               uint32_t dim2, uint32_t dim1, uint32_t dim0,
+                               uint32_t tile_size, uint32_t nt2, uint32_t nt1, uint32_t nt0,
+                               void* volume, r2s_stream_t stream);
+/* VJP -> v_means3d [N,3], v_conics [N,6], v_opacities [N].  mode 0 =
+ * voxelize_to_voxels_bwd_tensor (Ops.h:70-74; VoxelizeToVoxels.cpp:114-192),
+ * mode 1 = voxelize_to_voxels_bwd_per_gaussian_tensor (Ops.h:75-79;
+ * VoxelizeToVoxels.cpp:194-278).  `stats` is caller scratch of N*12
+ * elements of dtype. */
+R2S_API int r2s_voxelize_to_voxels_bwd(int dtype, int mode, const void* means3d, const void* conics,
+                               const void* opacities, const int32_t* tile_offsets,
+                               const int32_t* flatten_ids, const void* v_volume, int64_t N,
+                               int64_t n_isects, uint32_t dim2, uint32_t dim1, uint32_t dim0,
+                               uint32_t tile_size, uint32_t nt2, uint32_t nt1, uint32_t nt0,
+                               void* stats, void* v_means3d, void* v_conics,
+                               void* v_opacities, r2s_stream_t stream);
+
+/* ========================================================================
+ * Fused float32 entry points used by r2splat.ops (the training/inference
+ * fast path).  Each replaces a chain of reference calls in
+ * r2splat/ops/direct.py and r2splat/ops/explicit.py with fewer launches and
+ * fewer [C,N] intermediates; results equal the chain's.
+ * ====================================================================== */
+
+/* Parameter transform + softplus(raw_opacities) in one pass
+ * (direct.py:93-117: parameter_transform_fwd + torch softplus). */
+R2S_API int r2s_prepare_gaussians_f32(const float* quats, const float* raw_scales,
+                              const float* raw_opacities, double scale_min,
+                              double scale_max, float* covars, float* max_scales,
+                              float* opacities, int64_t n, r2s_stream_t stream);
+
+/* Projection + conics/mu + tile rectangle for all (view, Gaussian) pairs
+ * (direct.py:170-187: world_to_image_projection_fwd, conics_mu_fwd, the
+ * opacity expand and the first pass of isect_tiles).  Writes means2d
+ * [C,N,2], radii [C,N,2], splats [C,N,8] (x, y, conic a, b, c, w*mu,
+ * cull extent x, cull extent y), rects [C*N] (8 B) and tiles_per_gauss
+ * [C,N] (nullable). */
+R2S_API int r2s_project_splats_f32(const float* means, const float* covars,
+                           const float* opacities, const float* viewmats, const float* Ks,
+                           int64_t C, int64_t N, uint32_t width, uint32_t height,
+                           uint32_t tile_size, uint32_t n_tiles_w, uint32_t n_tiles_h,
+                           double eps2d, double radius_clip, float* means2d, int32_t* radii,
+                           float* splats, void* rects, int32_t* tiles_per_gauss,
+                           r2s_stream_t stream);
+/* Counting phase of the binning from precomputed rects (both layouts). */
+R2S_API int r2s_bin_prepare(const void* rects, int64_t n_segments, int64_t n_items,
+                    int64_t tiles_per_segment, uint32_t tiles_x, int layered,
+                    int64_t segment_base, void* workspace, int64_t workspace_bytes,
+                    int32_t* tile_offsets, int64_t* n_isects_dev, r2s_stream_t stream);
+/* Rasterize from splat records (float32, any tile size). */
+R2S_API int r2s_raster_splats_fwd_f32(const float* splats, const int32_t* tile_offsets,
+                              const int32_t* flatten_ids, int64_t C, int64_t N,
+                              int64_t n_isects, uint32_t width, uint32_t height,
+                              uint32_t tile_size, uint32_t n_tiles_w, uint32_t n_tiles_h,
+                              float* image, r2s_stream_t stream);
+/* Backward sufficient statistics per (view, Gaussian), accumulated over
+ * tiles: stats [C*N, 8] = (S0, Sx, Sy, Sxx, Sxy, Syy, Ax, Ay) with
+ * S* = sum over contributing pixels of v*exp(-sigma) * moments of the pixel
+ * offset, A* = sum of |v*exp(-sigma)*(conic . d)|.  Zeroes `stats` first. */
+R2S_API int r2s_raster_splats_bwd_f32(const float* splats, const int32_t* tile_offsets,
+                              const int32_t* flatten_ids, const float* v_image, int64_t C,
+                              int64_t N, int64_t n_isects, uint32_t width, uint32_t height,
+                              uint32_t tile_size, uint32_t n_tiles_w, uint32_t n_tiles_h,
+                              int with_abs, float* stats, r2s_stream_t stream);
+
+/* Volume mapping + voxel splat records + brick rectangles
+ * (direct.py:289-314: world_to_volume_mapping_fwd and the first pass of
+ * isect_tiles_3d).  Writes means3d [N,3], conics [N,6], radii [N,3],
+ * vsplats [N,16] (x, y, z, c00, c01, c02, c11, c12, c22, w, ex, ey, ez, 0..),
+ * rects3 [N] (16 B), tiles_per_gauss [N] (nullable). */
+R2S_API int r2s_map_vsplats_f32(const float* means, const float* covars, const float* opacities,
+                        const float* ranges, const float* centers, int64_t N, uint32_t dim2,
+                        uint32_t dim1, uint32_t dim0, uint32_t tile_size, uint32_t nt2,
+                        uint32_t nt1, uint32_t nt0, double eps3d, double radius_clip,
+                        float* means3d, float* conics, int32_t* radii, float* vsplats,
+                        void* rects3, int32_t* tiles_per_gauss, r2s_stream_t stream);
+/* Voxelize bricks [z_begin/8 .. ) from voxel splat records; `volume` points
+ * at voxel row z_begin of a [dim0,dim1,dim2] grid (z-slab output). */
+R2S_API int r2s_voxel_splats_fwd_f32(const float* vsplats, const int32_t* tile_offsets,
+                             const int32_t* flatten_ids, int64_t N, int64_t n_isects,
+                             uint32_t dim2, uint32_t dim1, uint32_t dim0, uint32_t tile_size,
+                             uint32_t nt2, uint32_t nt1, uint32_t nt0, uint32_t layer_begin,
+                             uint32_t layer_end, float* volume, r2s_stream_t stream);
+/* Voxel backward statistics [N, 12] = (S0, Sx, Sy, Sz, Sxx, Sxy, Sxz, Syy,
+ * Syz, Szz, 0, 0), accumulated over bricks; zeroes `stats` first. */
+R2S_API int r2s_voxel_splats_bwd_f32(const float* vsplats, const int32_t* tile_offsets,
+                             const int32_t* flatten_ids, const float* v_volume, int64_t N,
+                             int64_t n_isects, uint32_t dim2, uint32_t dim1, uint32_t dim0,
+                             uint32_t tile_size, uint32_t nt2, uint32_t nt1, uint32_t nt0,
+                             uint32_t layer_begin, uint32_t layer_end, float* stats,
+                             r2s_stream_t stream);
+
+/* Whole explicit backward per Gaussian (explicit.py:233-385): converts the
+ * raster statistics of every view to the reference's per-view gradients
+ * (written to v_means2d / v_means2d_abs [C,N,2] when non-NULL), applies
+ * conics_mu_bwd and world_to_image_projection_bwd, sums over views, adds the
+ * voxel path (world_to_volume_mapping_bwd of the voxel statistics), then
+ * parameter_transform_bwd and the softplus chain for opacities.  Outputs
+ * v_means [N,3], v_quats [N,4], v_raw_scales [N,3], v_raw_opacities [N];
+ * with accumulate != 0 they are added to the existing contents.
+ * raster_stats / vox_stats may be NULL (that path had no upstream gradient). */
+R2S_API int r2s_explicit_backward_f32(
+    const float* means, const float* quats, const float* raw_scales,
+    const float* raw_opacities, double scale_min, double scale_max, const float* viewmats,
+    const float* Ks, int64_t C, int64_t N, uint32_t width, uint32_t height, double eps2d,
+    const float* raster_stats, float* v_means2d, float* v_means2d_abs, const float* ranges,
+    const float* centers, uint32_t dim2, uint32_t dim1, uint32_t dim0, double eps3d,
+    const float* vox_stats, int accumulate, float* v_means, float* v_quats,
+    float* v_raw_scales, float* v_raw_opacities, r2s_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* R2S_H */
