@@ -1,0 +1,572 @@
+"""Benchmark of the r2splat hot path on B200: projection fwd+bwd and voxelization fwd+bwd.
+
+Metric: Gaussian*views/s of projection forward+backward
+(``value``) and Mvoxels/s of voxelization forward+backward (``voxelize``), on
+benchmark config 2 by default: 500,000 Gaussians, 75 views over 360 degrees,
+512x512 detector, 256^3 grid (seeded synthetic inputs, r2s_workloads.py).
+
+One step of the projection path is the reference's explicit training step
+without the loss: prepare (parameter transform + softplus), explicit
+rasterize (projection, binning, rasterizer), then explicit backward with a
+seeded N(0,1) upstream image gradient, all through ``r2splat.ops``.  One
+voxel step is prepare, voxelize of the grid and the voxel VJP chain down to
+the raw parameters.
+
+Multi-GPU (torchrun, one process per GPU): every rank renders its own 75
+views of a 75*N-view orbit of the same Gaussians (weak scaling) and the
+per-Gaussian gradients are summed with one NCCL all-reduce per step; the
+voxel grid is split into N z-slabs (strong scaling of that secondary
+metric).  ``value`` is the whole job: N*75*500k Gaussian*views / max-over-
+ranks step time.
+
+``--impl reference`` times the reference implementation of the path -- the
+reference's own CUDA sources built for sm_100a (``oracle/_ref``) driven in
+the reference op layer's call order -- on rank 0 with the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (os.path.join(ROOT, "bt-3dgs_b200"), ROOT):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+
+import r2s_workloads as wl  # noqa: E402
+
+L2_FLUSH_BYTES = 256 << 20
+
+
+def _peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.idx = device_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def init_dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(local)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(world, value: float) -> float:
+    if world == 1:
+        return value
+    import torch.distributed as dist
+
+    t = torch.tensor([value], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# our implementation
+# ---------------------------------------------------------------------------
+class OursProjection:
+    def __init__(self, cfg, world, rank, dev):
+        from r2splat.ops import explicit as E
+
+        self.E = E
+        self.world = world
+        self.cfg = cfg
+        self.det = cfg.detector
+        m, q, s, o = wl.make_gaussians(cfg)
+        self.host = [t.pin_memory() for t in (m, q, s, o)]
+        self.params = [t.to(dev) for t in (m, q, s, o)]
+        vm, K = wl.make_cameras(cfg.n_views, cfg.detector, first=rank * cfg.n_views,
+                                count=cfg.n_views, total=cfg.n_views * world)
+        self.vm, self.K = vm.to(dev), K.to(dev)
+        self.host_cams = (vm.pin_memory(), K.pin_memory())
+        g = torch.Generator(device=dev).manual_seed(100 + rank)
+        self.v_img = torch.randn((cfg.n_views, self.det, self.det), generator=g, device=dev)
+        self.host_vimg = self.v_img.cpu().pin_memory()
+        self.flat = None
+
+    def step(self, params=None, vm=None, K=None, v_img=None):
+        E = self.E
+        params = self.params if params is None else params
+        vm = self.vm if vm is None else vm
+        K = self.K if K is None else K
+        v_img = self.v_img if v_img is None else v_img
+        for p in params:
+            p.grad = None
+            p.requires_grad_(True)
+        st = E.prepare_explicit_gaussians(params[1], params[2], params[3],
+                                          scale_min=wl.SCALE_MIN, scale_max=wl.SCALE_MAX)
+        res = E.explicit_rasterize(st, params[0], vm, K, img_w=self.det, img_h=self.det,
+                                   tile_size=wl.IMG_TILE, eps2d=wl.EPS2D,
+                                   radius_clip=wl.RADIUS_CLIP, absgrad=True)
+        res.image.grad = v_img
+        E.explicit_backward(st, *params)
+        if self.world > 1:
+            self._allreduce(params)
+        return res
+
+    def _allreduce(self, params):
+        import torch.distributed as dist
+
+        grads = [p.grad for p in params]
+        n = sum(g.numel() for g in grads)
+        if self.flat is None or self.flat.numel() != n:
+            self.flat = torch.empty(n, device=grads[0].device)
+        off = 0
+        for g in grads:
+            self.flat[off:off + g.numel()].copy_(g.reshape(-1))
+            off += g.numel()
+        dist.all_reduce(self.flat)
+        off = 0
+        for g in grads:
+            g.copy_(self.flat[off:off + g.numel()].view_as(g))
+            off += g.numel()
+
+    def step_e2e(self):
+        """Same step with host-resident inputs and outputs: H2D of the raw
+        parameters, cameras and upstream image gradient, D2H of the four
+        parameter gradients."""
+        dev = self.params[0].device
+        params = [h.to(dev, non_blocking=True) for h in self.host]
+        vm = self.host_cams[0].to(dev, non_blocking=True)
+        K = self.host_cams[1].to(dev, non_blocking=True)
+        v_img = self.host_vimg.to(dev, non_blocking=True)
+        self.step(params, vm, K, v_img)
+        outs = [p.grad.to("cpu", non_blocking=True) for p in params]
+        return outs
+
+    def bytes_e2e(self):
+        h2d = sum(t.numel() * t.element_size() for t in self.host) + sum(
+            t.numel() * t.element_size() for t in self.host_cams) + self.host_vimg.numel() * 4
+        d2h = sum(t.numel() * t.element_size() for t in self.host)
+        return h2d, d2h
+
+
+class OursVoxel:
+    def __init__(self, cfg, world, rank, dev, params):
+        from r2splat.cuda import _wrapper as W
+
+        self.W = W
+        self.world = world
+        self.G = cfg.grid
+        self.nt = (self.G + wl.VOL_TILE - 1) // wl.VOL_TILE
+        per = (self.nt + world - 1) // world
+        self.l0 = min(self.nt, rank * per)
+        self.l1 = min(self.nt, self.l0 + per)
+        self.params = params
+        rng, ctr = wl.unit_cube_box()
+        self.rng, self.ctr = rng.to(dev), ctr.to(dev)
+        z0 = self.l0 * wl.VOL_TILE
+        z1 = min(self.l1 * wl.VOL_TILE, self.G)
+        g = torch.Generator(device=dev).manual_seed(200 + rank)
+        self.v_vol = torch.randn((max(z1 - z0, 0), self.G, self.G), generator=g, device=dev)
+        self.flat = None
+
+    def step(self):
+        W = self.W
+        m, q, s, o = self.params
+        G, nt = self.G, self.nt
+        with torch.no_grad():
+            cov, ms, op = W.fused_prepare(q, s, o, wl.SCALE_MIN, wl.SCALE_MAX)
+            m3, c3, r3, vs, rects, _ = W.fused_map(m, cov, op, self.rng, self.ctr, G, G, G,
+                                                   wl.VOL_TILE, nt, nt, nt, wl.EPS3D,
+                                                   wl.RADIUS_CLIP)
+            S = self.l1 - self.l0
+            offs, fids, _ = W.fused_bin(rects, S, m.size(0), nt * nt, nt, 1, segment_base=self.l0)
+            vol = W.fused_voxel_fwd(vs, offs, fids, m.size(0), G, G, G, wl.VOL_TILE, nt, nt, nt,
+                                    self.l0, self.l1)
+            stats = W.fused_voxel_bwd(vs, offs, fids, self.v_vol, m.size(0), G, G, G,
+                                      wl.VOL_TILE, nt, nt, nt, self.l0, self.l1)
+            outs = [torch.empty_like(t) for t in (m, q, s, o)]
+            W.fused_explicit_backward(m, q, s, o, wl.SCALE_MIN, wl.SCALE_MAX, None, None, 0, 0,
+                                      wl.EPS2D, None, None, None, self.rng, self.ctr, G, G, G,
+                                      wl.EPS3D, stats, False, outs)
+            if self.world > 1:
+                import torch.distributed as dist
+
+                n = sum(t.numel() for t in outs)
+                if self.flat is None or self.flat.numel() != n:
+                    self.flat = torch.empty(n, device=m.device)
+                torch.cat([t.reshape(-1) for t in outs], out=self.flat)
+                dist.all_reduce(self.flat)
+        return vol
+
+
+# ---------------------------------------------------------------------------
+# reference implementation (the reference's CUDA build, reference call order)
+# ---------------------------------------------------------------------------
+class RefProjection:
+    def __init__(self, cfg, dev):
+        from oracle.ref_harness import ReferencePipeline
+
+        self.ref = ReferencePipeline()
+        self.cfg = cfg
+        self.det = cfg.detector
+        m, q, s, o = wl.make_gaussians(cfg)
+        self.params = [t.to(dev) for t in (m, q, s, o)]
+        vm, K = wl.make_cameras(cfg.n_views, cfg.detector)
+        self.vm, self.K = vm.to(dev), K.to(dev)
+        g = torch.Generator(device=dev).manual_seed(100)
+        self.v_img = torch.randn((cfg.n_views, self.det, self.det), generator=g, device=dev)
+
+    def step(self):
+        m, q, s, o = self.params
+        cov, ms, op = self.ref.prepare(q, s, o, wl.SCALE_MIN, wl.SCALE_MAX)
+        p = self.ref.rasterize_forward(m, cov, op, self.vm, self.K, self.det, self.det,
+                                       wl.IMG_TILE, wl.EPS2D, wl.RADIUS_CLIP)
+        self.ref.explicit_backward(p, self.v_img, None, None, m, q, s, o, cov, op, wl.SCALE_MIN,
+                                   wl.SCALE_MAX, absgrad=True)
+        return p
+
+
+class RefVoxel:
+    def __init__(self, cfg, dev, proj: RefProjection):
+        self.ref = proj.ref
+        self.params = proj.params
+        self.G = cfg.grid
+        rng, ctr = wl.unit_cube_box()
+        self.rng, self.ctr = rng.to(dev), ctr.to(dev)
+        g = torch.Generator(device=dev).manual_seed(200)
+        self.v_vol = torch.randn((self.G,) * 3, generator=g, device=dev)
+
+    def step(self):
+        m, q, s, o = self.params
+        G = self.G
+        cov, ms, op = self.ref.prepare(q, s, o, wl.SCALE_MIN, wl.SCALE_MAX)
+        v = self.ref.voxelize_forward(m, cov, ms, op, self.rng, self.ctr, G, G, G, wl.VOL_TILE,
+                                      wl.EPS3D, wl.RADIUS_CLIP)
+        self.ref.explicit_backward(None, None, v, self.v_vol, m, q, s, o, cov, op, wl.SCALE_MIN,
+                                   wl.SCALE_MAX)
+        return v
+
+
+# ---------------------------------------------------------------------------
+# timing helpers
+# ---------------------------------------------------------------------------
+def time_steps(fn, steps, warmup, world, flush):
+    for _ in range(warmup):
+        flush.zero_()
+        fn()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        flush.zero_()  # inputs and L2: 256 MiB write between steps
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = a.elapsed_time(b) / steps
+    return max_over_ranks(world, ms)
+
+
+def time_e2e(fn, steps, warmup, world, flush):
+    for _ in range(warmup):
+        flush.zero_()
+        outs = fn()
+        torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        flush.zero_()
+        outs = fn()
+    torch.cuda.synchronize()
+    dt = (time.perf_counter() - t0) * 1e3 / steps
+    barrier(world)
+    return max_over_ranks(world, dt)
+
+
+def kernel_time(fn, reps=3):
+    """Average duration of one launch sequence on the current stream."""
+    ts = []
+    for _ in range(reps):
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        ts.append(a.elapsed_time(b))
+    return sum(ts) / len(ts)
+
+
+def dominant_kernel_roofline(proj: OursProjection, hbm_peak, peak_kind):
+    """Raster backward (the largest share of the step) on its own launch.
+
+    Algorithmic bytes per launch (counted from the formulas): per
+    intersection record 4 B flatten id + 32 B splat record + 32 B statistics
+    reduction, plus the upstream image (4 B per pixel per view).  Pairs for
+    the FP32 view: n_isects * 256, 30 FP32 flops + 1 ex2 per pair."""
+    from r2splat.cuda import _wrapper as W
+
+    E = proj.E
+    m, q, s, o = proj.params
+    st = E.prepare_explicit_gaussians(q, s, o, scale_min=wl.SCALE_MIN, scale_max=wl.SCALE_MAX)
+    res = E.explicit_rasterize(st, m, proj.vm, proj.K, img_w=proj.det, img_h=proj.det,
+                               tile_size=wl.IMG_TILE, eps2d=wl.EPS2D, radius_clip=wl.RADIUS_CLIP,
+                               absgrad=True)
+    pb = st.projection.buffers
+    C, N = pb.means2d.shape[:2]
+    ntx, nty = pb.tile_offsets.size(2), pb.tile_offsets.size(1)
+    n_isects = pb.flatten_ids.numel()
+
+    def launch():
+        W.fused_raster_bwd(pb.splats, pb.tile_offsets, pb.flatten_ids, proj.v_img, C, N, proj.det,
+                           proj.det, wl.IMG_TILE, ntx, nty, True)
+
+    launch()
+    ms = kernel_time(launch)
+    alg_bytes = n_isects * (4 + 32 + 32) + C * proj.det * proj.det * 4
+    achieved = alg_bytes / (ms * 1e-3) / 1e9
+    pairs = n_isects * 256
+    flops = pairs * 30
+    fp32_peak = 148 * 128 * 2 * 1.965e9 / 1e12
+    tflops = flops / (ms * 1e-3) / 1e12
+    return {
+        "kernel": "raster_bwd_kernel<float,splats>",
+        "bound": "hbm",
+        "achieved": round(achieved, 1),
+        "peak": hbm_peak,
+        "unit": "GB/s",
+        "frac": round(achieved / hbm_peak, 4),
+        "peak_source": peak_kind,
+        "traffic": None,
+        "ms_per_launch": round(ms, 3),
+        "n_isects": n_isects,
+        "fp32": {"achieved_tflops": round(tflops, 2), "peak_tflops_nominal": round(fp32_peak, 1),
+                 "frac": round(tflops / fp32_peak, 4),
+                 "flops_per_pair": 30, "pairs": pairs},
+    }
+
+
+def cpu_baseline(cfg, seconds_budget=15.0):
+    """Dense PyTorch-on-CPU evaluation of the same formulas (the CPU oracle):
+    projection forward + autograd backward of a sample of Gaussians on one
+    full-size view; Gaussian*views/s of that sample."""
+    from oracle import r2s_oracle as O
+
+    threads = torch.get_num_threads()
+    vm, K = wl.make_cameras(1, cfg.detector, total=cfg.n_views)
+    n = 256
+    while True:
+        m, q, s, o = wl.make_gaussians(cfg, n=n)
+        params = [t.clone().requires_grad_(True) for t in (m, q, s, o)]
+        t0 = time.perf_counter()
+        img, *_ = O.projection_forward(*params, vm, K, width=cfg.detector, height=cfg.detector,
+                                       tile=wl.IMG_TILE, eps2d=wl.EPS2D, clip=wl.RADIUS_CLIP,
+                                       smin=wl.SCALE_MIN, smax=wl.SCALE_MAX, chunk=64)
+        img.backward(torch.ones_like(img))
+        dt = time.perf_counter() - t0
+        if dt * 2.2 > seconds_budget or n >= 16384:
+            break
+        n *= 2
+    return {"value": round(n / dt, 1), "unit": "Gaussian*views/s", "cores": threads,
+            "kind": "port",
+            "sample": f"{n} Gaussians of config-{2} distributions x 1 view at {cfg.detector}^2, "
+                      f"dense over all pixels with tile-membership mask, fwd+autograd bwd, "
+                      f"{dt:.1f} s"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--config", type=int, default=2)
+    ap.add_argument("--views", type=int, default=None,
+                    help="override the views per GPU (small profiling cases)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference" and int(os.environ.get("RANK", "0")) != 0:
+        return  # the reference arm runs on rank 0 only
+    if args.impl == "reference":
+        os.environ["WORLD_SIZE"] = "1"
+    world, rank, local = init_dist()
+    dev = torch.device("cuda", local)
+    cfg = wl.CONFIGS[args.config]
+    if args.views is not None:
+        import dataclasses
+
+        cfg = dataclasses.replace(cfg, n_views=args.views,
+                                  name=f"{cfg.name}-views{args.views}")
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    hbm_peak, peak_kind = _peaks()
+
+    if args.impl == "reference":
+        try:
+            from oracle.ref_harness import reference_available
+
+            if not reference_available():
+                print(json.dumps({"impl": "reference", "unavailable":
+                                  "reference sm_100a build oracle/_ref missing"}))
+                return
+            proj = RefProjection(cfg, dev)
+            vox = RefVoxel(cfg, dev, proj)
+        except Exception as exc:  # reference build cannot be loaded
+            print(json.dumps({"impl": "reference", "unavailable": f"{type(exc).__name__}: {exc}"}))
+            return
+        with ClockSampler(local) as clk:
+            ms = time_steps(proj.step, args.steps, args.warmup, 1, flush)
+            vms = time_steps(vox.step, args.steps, args.warmup, 1, flush)
+        value = cfg.n_gaussians * cfg.n_views / (ms * 1e-3)
+        line = {
+            "metric": "Gaussian*views/s projection fwd+bwd (and Mvoxels/s voxelize fwd+bwd)",
+            "impl": "reference", "value": round(value, 1), "unit": "Gaussian*views/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, r2s_workloads)",
+            "config": {"workload": cfg.name, "n_gaussians": cfg.n_gaussians,
+                       "views": cfg.n_views, "detector": cfg.detector, "grid": cfg.grid,
+                       "l2": "256MiB flush between steps"},
+            "voxelize": {"value": round(cfg.grid ** 3 / (vms * 1e-3) / 1e6, 2),
+                         "unit": "Mvoxels/s", "ms_per_step": round(vms, 3)},
+            "cpu_baseline": {"value": round(value, 1), "unit": "Gaussian*views/s", "cores": 0,
+                             "kind": "reference",
+                             "sample": "the reference's CUDA build (it ships no CPU "
+                                       "implementation), full workload on GPU 0"},
+            "e2e": {"value": round(value, 1), "unit": "Gaussian*views/s",
+                    "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line))
+        return
+
+    proj = OursProjection(cfg, world, rank, dev)
+    vox = OursVoxel(cfg, world, rank, dev, proj.params)
+    with ClockSampler(local) as clk:
+        ms = time_steps(proj.step, args.steps, args.warmup, world, flush)
+        vms = time_steps(vox.step, args.steps, args.warmup, world, flush)
+        e2e_ms = time_e2e(proj.step_e2e, args.steps, max(1, args.warmup // 2), world, flush)
+    value = world * cfg.n_gaussians * cfg.n_views / (ms * 1e-3)
+    e2e_value = world * cfg.n_gaussians * cfg.n_views / (e2e_ms * 1e-3)
+    h2d, d2h = proj.bytes_e2e()
+    roof = dominant_kernel_roofline(proj, hbm_peak, peak_kind) if rank == 0 else None
+    barrier(world)
+    # launches of our kernels per projection step (prepare 1, project 1,
+    # binning 4, rasterizer 1 + backward 2 statistics/finalize) and per voxel step
+    gpu_launches = args.steps * (1 + 1 + 4 + 1 + 2) + args.steps * (1 + 1 + 4 + 1 + 1 + 1)
+    if rank != 0:
+        return
+    line = {
+        "metric": "Gaussian*views/s projection fwd+bwd (and Mvoxels/s voxelize fwd+bwd)",
+        "value": round(value, 1), "unit": "Gaussian*views/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded, r2s_workloads)",
+        "config": {"workload": cfg.name, "n_gaussians": cfg.n_gaussians,
+                   "views_per_gpu": cfg.n_views, "detector": cfg.detector, "grid": cfg.grid,
+                   "parallelism": f"views x{world} (weak) + grad all-reduce; voxel z-slabs x{world}",
+                   "l2": "256MiB flush between steps"},
+        "voxelize": {"value": round(cfg.grid ** 3 / (vms * 1e-3) / 1e6, 2), "unit": "Mvoxels/s",
+                     "ms_per_step": round(vms, 3), "scaling": "strong (z-slabs)"},
+        "e2e": {"value": round(e2e_value, 1), "unit": "Gaussian*views/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": round(e2e_ms, 3)},
+        "roofline": roof,
+        "gpu_launches": gpu_launches,
+        "clocks": clk.summary(),
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(cfg)
+    print(json.dumps(line))
+
+
+def shutdown():
+    if torch.distributed.is_available() and torch.distributed.is_initialized():
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    try:
+        main()
+    finally:
+        shutdown()
