@@ -428,6 +428,280 @@ __global__ void raster_unpack_kernel(const S* __restrict__ stats, const S* __res
     }
 }
 
+// ===========================================================================
+// float32, 16x16 tiles: the fast kernels
+// ===========================================================================
+//
+// Validity test.  The reference keeps a pair when sigma >= 0 and
+// |w mu exp(-sigma)| >= 1e-5.  With s = sigma*log2(e) this is
+// 0 <= s <= s_thr, s_thr = log2(|w mu| * 1e5); for non-negative floats the
+// IEEE bit patterns are ordered like the values and every negative s (sign
+// bit set) compares above s_thr as an unsigned integer, so one integer
+// compare decides the pair.  Pairs within rounding of the alpha cut-off may
+// be decided differently from the reference's float test; each such pair
+// moves a pixel by at most ~1e-5.
+
+__device__ __forceinline__ bool s_valid(float s, uint32_t thr_bits) {
+    return __float_as_uint(s) <= thr_bits;
+}
+
+__device__ __forceinline__ float s_threshold(float wmu) {
+    const float a = fabsf(wmu) * 1e5f;
+    return a >= 1.0f ? log2f(a) : -1.0f;  // negative: nothing passes
+}
+
+constexpr int kFwd16Threads = 128;  // 4 warps, each an 8x8 pixel block, 2 pixels per lane
+constexpr int kFwd16Batch = 256;
+
+__global__ void __launch_bounds__(kFwd16Threads)
+raster_fwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict__ offsets,
+                    const int32_t* __restrict__ flatten_ids, int64_t n_keys, int64_t n_isects,
+                    uint32_t W, uint32_t H, uint32_t ntx, uint32_t nty, float* __restrict__ image) {
+    __shared__ float4 s_p[kFwd16Batch];  // mx, my, A = a/2 log2e, B = b log2e
+    __shared__ float4 s_q[kFwd16Batch];  // C = c/2 log2e, w*mu, s_thr, unused
+    __shared__ uint32_t s_mask[kFwd16Batch];
+    __shared__ uint16_t s_list[kFwd16Threads / 32][kFwd16Batch];  // per-warp work list
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int64_t cam = blockIdx.z;
+    const int X0 = blockIdx.x * 16, Y0 = blockIdx.y * 16;
+    const int64_t key = cam * (int64_t)ntx * nty + (int64_t)blockIdx.y * ntx + blockIdx.x;
+    const int start = offsets[key];
+    const int end = key + 1 < n_keys ? offsets[key + 1] : (int)n_isects;
+
+    const int ix = X0 + (warp & 1) * 8 + (lane & 7);
+    const int iy0 = Y0 + (warp >> 1) * 8 + (lane >> 3);
+    const float px = (float)ix + 0.5f;
+    const float py0 = (float)iy0 + 0.5f;
+    const float xmax = (float)W - 0.5f, ymax = (float)H - 0.5f;
+    float acc0 = 0.f, acc1 = 0.f;
+
+    for (int b0 = start; b0 < end; b0 += kFwd16Batch) {
+        const int n = min(kFwd16Batch, end - b0);
+        __syncthreads();
+        for (int j = tid; j < n; j += kFwd16Threads) {
+            const int64_t g = flatten_ids[b0 + j];
+            const float4 p = splats[2 * g];
+            const float4 q = splats[2 * g + 1];
+            // warp w covers pixel centres [X0+8(w&1)+0.5, +7.5] x [Y0+8(w>>1)+0.5, +7.5]
+            const float gx0 = p.x - q.z, gx1 = p.x + q.z, gy0 = p.y - q.w, gy1 = p.y + q.w;
+            uint32_t m = 0;
+#pragma unroll
+            for (int w = 0; w < 4; ++w) {
+                const float bx0 = (float)(X0 + (w & 1) * 8) + 0.5f;
+                const float by0 = (float)(Y0 + (w >> 1) * 8) + 0.5f;
+                const float bx1 = fminf(bx0 + 7.f, xmax), by1 = fminf(by0 + 7.f, ymax);
+                if (gx0 <= bx1 && gx1 >= bx0 && gy0 <= by1 && gy1 >= by0 && bx0 <= bx1 &&
+                    by0 <= by1)
+                    m |= 1u << w;
+            }
+            s_p[j] = make_float4(p.x, p.y, 0.5f * kLog2e * p.z, kLog2e * p.w);
+            s_q[j] = make_float4(0.5f * kLog2e * q.x, q.y, s_threshold(q.y), 0.f);
+            s_mask[j] = m;
+        }
+        __syncthreads();
+        // compact this warp's Gaussians of the batch into an index list
+        uint16_t* list = s_list[warp];
+        int cnt = 0;
+        for (int c0 = 0; c0 < n; c0 += 32) {
+            const int j = c0 + lane;
+            const bool mine = j < n && ((s_mask[j] >> warp) & 1u);
+            const unsigned bits = __ballot_sync(0xffffffffu, mine);
+            if (mine) list[cnt + __popc(bits & lanemask_lt())] = (uint16_t)j;
+            cnt += __popc(bits);
+        }
+        __syncwarp();
+        for (int i = 0; i < cnt; ++i) {
+            const int t = list[i];
+            const float4 P = s_p[t];
+            const float4 Q = s_q[t];
+            const uint32_t thr = __float_as_uint(Q.z);
+            const float dx = px - P.x;
+            const float xx = P.z * dx * dx;
+            const float xy = P.w * dx;
+            const float dy0 = py0 - P.y;
+            const float dy1 = dy0 + 4.0f;
+            const float s0 = fmaf(dy0, fmaf(Q.x, dy0, xy), xx);
+            const float s1 = fmaf(dy1, fmaf(Q.x, dy1, xy), xx);
+            const bool v0 = s_valid(s0, thr), v1 = s_valid(s1, thr);
+            if (!__any_sync(0xffffffffu, v0 | v1)) continue;
+            const float e0 = exp2f(-s0);
+            const float e1 = exp2f(-s1);
+            if (v0) acc0 = fmaf(Q.y, e0, acc0);
+            if (v1) acc1 = fmaf(Q.y, e1, acc1);
+        }
+    }
+    if (ix < (int)W) {
+        float* out = image + cam * (int64_t)H * W;
+        if (iy0 < (int)H) out[(int64_t)iy0 * W + ix] = acc0;
+        if (iy0 + 4 < (int)H) out[(int64_t)(iy0 + 4) * W + ix] = acc1;
+    }
+}
+
+// Eight-value warp sum by transposed butterflies: after the three halving
+// steps lane L holds the partial of value (L >> 2) & 7, finished by two
+// plain steps; 9 shuffles instead of 40.
+__device__ __forceinline__ float warp_sum8_transposed(float v[8]) {
+    const int lane = threadIdx.x & 31;
+    const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
+    float u[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const float send = b4 ? v[k] : v[k + 4];
+        const float keep = b4 ? v[k + 4] : v[k];
+        u[k] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+    }
+    float w[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        const float send = b3 ? u[k] : u[k + 2];
+        const float keep = b3 ? u[k + 2] : u[k];
+        w[k] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+    }
+    const float send = b2 ? w[0] : w[1];
+    const float keep = b2 ? w[1] : w[0];
+    float x = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+    x += __shfl_xor_sync(0xffffffffu, x, 2);
+    x += __shfl_xor_sync(0xffffffffu, x, 1);
+    return x;
+}
+
+constexpr int kBwd16Threads = 256;  // 8 warps, one Gaussian per warp at a time
+constexpr int kBwd16Batch = 256;
+
+template <bool WITH_ABS>
+__global__ void __launch_bounds__(kBwd16Threads)
+raster_bwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict__ offsets,
+                    const int32_t* __restrict__ flatten_ids, int64_t n_keys, int64_t n_isects,
+                    const float* __restrict__ v_image, uint32_t W, uint32_t H, uint32_t ntx,
+                    uint32_t nty, float* __restrict__ stats) {
+    __shared__ float s_v[16 * 17];
+    __shared__ float4 s_p[kBwd16Batch];  // mx, my, a, b
+    __shared__ float4 s_q[kBwd16Batch];  // c, w*mu, s_thr, unused
+    __shared__ int32_t s_g[kBwd16Batch];
+    __shared__ uint32_t s_box[kBwd16Batch];
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int64_t cam = blockIdx.z;
+    const int X0 = blockIdx.x * 16, Y0 = blockIdx.y * 16;
+    const int64_t key = cam * (int64_t)ntx * nty + (int64_t)blockIdx.y * ntx + blockIdx.x;
+    const int start = offsets[key];
+    const int end = key + 1 < n_keys ? offsets[key + 1] : (int)n_isects;
+    if (start >= end) return;
+    const int cmax = min(15, (int)W - 1 - X0), rmax = min(15, (int)H - 1 - Y0);
+    {
+        const float* vc = v_image + cam * (int64_t)H * W;
+        const int r = tid >> 4, c = tid & 15;
+        s_v[r * 17 + c] = (c <= cmax && r <= rmax) ? vc[(int64_t)(Y0 + r) * W + X0 + c] : 0.f;
+    }
+    for (int b0 = start; b0 < end; b0 += kBwd16Batch) {
+        const int n = min(kBwd16Batch, end - b0);
+        __syncthreads();
+        if (tid < n) {
+            const int64_t g = flatten_ids[b0 + tid];
+            const float4 p = splats[2 * g];
+            const float4 q = splats[2 * g + 1];
+            int c_lo, c_hi, r_lo, r_hi;
+            cull_range(p.x, q.z, (float)X0, cmax, c_lo, c_hi);
+            cull_range(p.y, q.w, (float)Y0, rmax, r_lo, r_hi);
+            uint32_t box = 0x000000ffu;  // empty: c_lo 255 > c_hi 0
+            if (c_lo <= c_hi && r_lo <= r_hi)
+                box = (uint32_t)c_lo | ((uint32_t)c_hi << 8) | ((uint32_t)r_lo << 16) |
+                      ((uint32_t)r_hi << 24);
+            s_p[tid] = p;
+            s_q[tid] = make_float4(q.x, q.y, s_threshold(q.y), 0.f);
+            s_g[tid] = (int32_t)g;
+            s_box[tid] = box;
+        }
+        __syncthreads();
+        for (int t = warp; t < n; t += kBwd16Threads / 32) {
+            const uint32_t bx = s_box[t];
+            const int c_lo = bx & 0xff, c_hi = (bx >> 8) & 0xff;
+            if (c_lo > c_hi) continue;
+            const int r_lo = (bx >> 16) & 0xff, r_hi = bx >> 24;
+            const float4 P = s_p[t];
+            const float4 Q = s_q[t];
+            const uint32_t thr = __float_as_uint(Q.z);
+            const float A = 0.5f * kLog2e * P.z, B = kLog2e * P.w, Cc = 0.5f * kLog2e * Q.x;
+            // Lanes take 4-pixel row segments of the footprint rectangle.  s is
+            // evaluated per pixel (two FMAs with the row terms B*dy and C*dy^2
+            // hoisted); the y moments of a row come from its sums
+            // R0 = sum ve, R1 = sum ve dx, R2 = sum ve dx^2; the absgrad terms
+            // |ve| |a dx + b dy| advance their linear factor by a (resp. b) per
+            // pixel, their sums have no cancellation.
+            const int w = c_hi - c_lo + 1;
+            const int spr = (w + 3) >> 2;
+            const int n_seg = spr * (r_hi - r_lo + 1);
+            const float inv_spr = 1.0f / (float)spr;
+            const float dxb = (float)(X0 + c_lo) + 0.5f - P.x;
+            const float dyb = (float)(Y0 + r_lo) + 0.5f - P.y;
+            const int vbase = r_lo * 17 + c_lo;
+            float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            for (int sg = lane; sg < n_seg; sg += 32) {
+                const float rf = truncf(((float)sg + 0.5f) * inv_spr);
+                const int row = (int)rf;
+                const int c0 = (sg - row * spr) * 4;
+                const int npx = min(4, w - c0);
+                const float dy = dyb + rf;
+                float dx = dxb + (float)c0;
+                const float by = B * dy;
+                const float cyy = Cc * dy * dy;
+                float qx = fmaf(P.z, dx, P.w * dy);  // a dx + b dy
+                float qy = fmaf(P.w, dx, Q.x * dy);  // b dx + c dy
+                const int vb = vbase + row * 17 + c0;
+                float R0 = 0.f, R1 = 0.f, R2 = 0.f, Ax = 0.f, Ay = 0.f;
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const bool in = k < npx;
+                    const float v = in ? s_v[vb + k] : 0.f;
+                    const float sv = fmaf(dx, fmaf(A, dx, by), cyy);
+                    const float e = exp2f(-sv);
+                    const float ve = s_valid(sv, thr) ? v * e : 0.f;
+                    const float vx = ve * dx;
+                    R0 += ve;
+                    R1 += vx;
+                    R2 = fmaf(vx, dx, R2);
+                    if constexpr (WITH_ABS) {
+                        Ax = fmaf(fabsf(ve), fabsf(qx), Ax);
+                        Ay = fmaf(fabsf(ve), fabsf(qy), Ay);
+                        qx += P.z;
+                        qy += P.w;
+                    }
+                    dx += 1.0f;
+                }
+                acc[0] += R0;
+                acc[1] += R1;
+                acc[2] = fmaf(dy, R0, acc[2]);
+                acc[3] += R2;
+                acc[4] = fmaf(dy, R1, acc[4]);
+                acc[5] = fmaf(dy * dy, R0, acc[5]);
+                if constexpr (WITH_ABS) {
+                    acc[6] += Ax;
+                    acc[7] += Ay;
+                }
+            }
+            const float sum = warp_sum8_transposed(acc);
+            if ((lane & 3) == 0 && (WITH_ABS || (lane >> 2) < 6))
+                atomicAdd(stats + (int64_t)s_g[t] * 8 + (lane >> 2), sum);
+        }
+    }
+}
+
+// Splat records from the reference-layout inputs (rasterizer wrappers).
+__global__ void pack_splats_kernel(const float* __restrict__ means2d,
+                                   const float* __restrict__ conics, const float* __restrict__ opac,
+                                   const float* __restrict__ mus, int64_t total,
+                                   float4* __restrict__ splats) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= total) return;
+    const float a = conics[3 * i], b = conics[3 * i + 1], c = conics[3 * i + 2];
+    const float wmu = opac[i] * mus[i];
+    float ex, ey;
+    conic_cull_extents(a, b, c, wmu, kAlphaMin2D, ex, ey);
+    splats[2 * i] = make_float4(means2d[2 * i], means2d[2 * i + 1], a, b);
+    splats[2 * i + 1] = make_float4(c, wmu, ex, ey);
+}
+
 // ---------------------------------------------------------------------------
 // launchers
 // ---------------------------------------------------------------------------
@@ -438,6 +712,33 @@ int check_tiles(int64_t C, uint32_t W, uint32_t H, uint32_t T, uint32_t ntx, uin
                 "rasterize: tile grid does not cover the image");
     R2S_REQUIRE(C <= 65535 && nty <= 65535, "rasterize: too many views or tile rows for one launch");
     return R2S_OK;
+}
+
+int launch_raster_fwd16(const float4* splats, const int32_t* offsets, const int32_t* flatten_ids,
+                        int64_t C, int64_t n_isects, uint32_t W, uint32_t H, uint32_t ntx,
+                        uint32_t nty, float* image, cudaStream_t stream) {
+    const dim3 grid(ntx, nty, (unsigned)C);
+    raster_fwd16_kernel<<<grid, kFwd16Threads, 0, stream>>>(
+        splats, offsets, flatten_ids, C * (int64_t)ntx * nty, n_isects, W, H, ntx, nty, image);
+    return check_launch("rasterize_to_pixels_fwd");
+}
+
+int launch_raster_bwd16(const float4* splats, const int32_t* offsets, const int32_t* flatten_ids,
+                        const float* v_image, int64_t C, int64_t N, int64_t n_isects, uint32_t W,
+                        uint32_t H, uint32_t ntx, uint32_t nty, int with_abs, float* stats,
+                        cudaStream_t stream) {
+    cudaMemsetAsync(stats, 0, (size_t)C * N * 8 * sizeof(float), stream);
+    if (n_isects == 0) return check_launch("rasterize_to_pixels_bwd");
+    const dim3 grid(ntx, nty, (unsigned)C);
+    if (with_abs)
+        raster_bwd16_kernel<true><<<grid, kBwd16Threads, 0, stream>>>(
+            splats, offsets, flatten_ids, C * (int64_t)ntx * nty, n_isects, v_image, W, H, ntx,
+            nty, stats);
+    else
+        raster_bwd16_kernel<false><<<grid, kBwd16Threads, 0, stream>>>(
+            splats, offsets, flatten_ids, C * (int64_t)ntx * nty, n_isects, v_image, W, H, ntx,
+            nty, stats);
+    return check_launch("rasterize_to_pixels_bwd");
 }
 
 template <typename S, bool SPLATS>
@@ -488,7 +789,8 @@ extern "C" int r2s_rasterize_to_pixels_fwd(int dtype, const void* means2d, const
                                            const int32_t* offsets, const int32_t* flatten_ids,
                                            int64_t C, int64_t N, int64_t n_isects, uint32_t W,
                                            uint32_t H, uint32_t T, uint32_t ntx, uint32_t nty,
-                                           void* image, r2s_stream_t stream) {
+                                           void* splat_scratch, void* image,
+                                           r2s_stream_t stream) {
     R2S_REQUIRE(C >= 0 && N >= 0 && n_isects >= 0, "rasterize_to_pixels_fwd: negative size");
     const size_t es = dtype == R2S_F64 ? 8 : 4;
     if (C == 0 || (int64_t)W * H == 0) return R2S_OK;
@@ -497,6 +799,13 @@ extern "C" int r2s_rasterize_to_pixels_fwd(int dtype, const void* means2d, const
         return check_launch("rasterize_to_pixels_fwd");
     }
     if (int rc = check_tiles(C, W, H, T, ntx, nty)) return rc;
+    if (dtype == R2S_F32 && T == 16 && splat_scratch != nullptr) {
+        pack_splats_kernel<<<grid_for(C * N), kThreads, 0, stream>>>(
+            (const float*)means2d, (const float*)conics, (const float*)opacities,
+            (const float*)mus, C * N, (float4*)splat_scratch);
+        return launch_raster_fwd16((const float4*)splat_scratch, offsets, flatten_ids, C, n_isects,
+                                   W, H, ntx, nty, (float*)image, stream);
+    }
     return R2S_DTYPE_DISPATCH(dtype, "rasterize_to_pixels_fwd", [&] {
         RasterSrc<scalar_t> src{nullptr, (const scalar_t*)means2d, (const scalar_t*)conics,
                                 (const scalar_t*)opacities, (const scalar_t*)mus};
@@ -511,8 +820,9 @@ extern "C" int r2s_rasterize_to_pixels_bwd(int dtype, int mode, const void* mean
                                            const int32_t* flatten_ids, const void* v_image,
                                            int64_t C, int64_t N, int64_t n_isects, uint32_t W,
                                            uint32_t H, uint32_t T, uint32_t ntx, uint32_t nty,
-                                           void* stats, void* v_abs, void* v_m2, void* v_con,
-                                           void* v_op, void* v_mu, r2s_stream_t stream) {
+                                           void* splat_scratch, void* stats, void* v_abs,
+                                           void* v_m2, void* v_con, void* v_op, void* v_mu,
+                                           r2s_stream_t stream) {
     R2S_REQUIRE(C >= 0 && N >= 0 && n_isects >= 0, "rasterize_to_pixels_bwd: negative size");
     R2S_REQUIRE(mode == 0 || mode == 1, "rasterize_to_pixels_bwd: mode must be 0 or 1");
     const int64_t total = C * N;
@@ -530,7 +840,15 @@ extern "C" int r2s_rasterize_to_pixels_bwd(int dtype, int mode, const void* mean
     return R2S_DTYPE_DISPATCH(dtype, "rasterize_to_pixels_bwd", [&] {
         RasterSrc<scalar_t> src{nullptr, (const scalar_t*)means2d, (const scalar_t*)conics,
                                 (const scalar_t*)opacities, (const scalar_t*)mus};
-        int rc = mode == 0
+        int rc;
+        if (std::is_same<scalar_t, float>::value && T == 16 && splat_scratch != nullptr) {
+            pack_splats_kernel<<<grid_for(total), kThreads, 0, stream>>>(
+                (const float*)means2d, (const float*)conics, (const float*)opacities,
+                (const float*)mus, total, (float4*)splat_scratch);
+            rc = launch_raster_bwd16((const float4*)splat_scratch, offsets, flatten_ids,
+                                     (const float*)v_image, C, N, n_isects, W, H, ntx, nty,
+                                     v_abs != nullptr, (float*)stats, stream);
+        } else rc = mode == 0
                      ? launch_raster_bwd<scalar_t, false, 0>(src, offsets, flatten_ids,
                                                              (const scalar_t*)v_image, C, N,
                                                              n_isects, W, H, T, ntx, nty,
@@ -562,6 +880,9 @@ extern "C" int r2s_raster_splats_fwd_f32(const float* splats, const int32_t* off
         return check_launch("raster_splats_fwd");
     }
     if (int rc = check_tiles(C, W, H, T, ntx, nty)) return rc;
+    if (T == 16)
+        return launch_raster_fwd16((const float4*)splats, offsets, flatten_ids, C, n_isects, W, H,
+                                   ntx, nty, image, stream);
     RasterSrc<float> src{(const float4*)splats, nullptr, nullptr, nullptr, nullptr};
     return launch_raster_fwd<float, true>(src, offsets, flatten_ids, C, n_isects, W, H, T, ntx,
                                           nty, image, stream);
@@ -579,6 +900,9 @@ extern "C" int r2s_raster_splats_bwd_f32(const float* splats, const int32_t* off
         return check_launch("raster_splats_bwd");
     }
     if (int rc = check_tiles(C, W, H, T, ntx, nty)) return rc;
+    if (T == 16)
+        return launch_raster_bwd16((const float4*)splats, offsets, flatten_ids, v_image, C, N,
+                                   n_isects, W, H, ntx, nty, with_abs, stats, stream);
     RasterSrc<float> src{(const float4*)splats, nullptr, nullptr, nullptr, nullptr};
     return launch_raster_bwd<float, true, 0>(src, offsets, flatten_ids, v_image, C, N, n_isects, W,
                                              H, T, ntx, nty, with_abs, stats, stream);

@@ -446,6 +446,13 @@ def _check_raster_inputs(means2d, conics, opacities, mus, tile_offsets, flatten_
     return C, N
 
 
+def _splat_scratch(means2d, C, N, tile):
+    """Packed splat records for the float32 16-pixel-tile kernels (else None)."""
+    if means2d.dtype == torch.float32 and int(tile) == 16:
+        return torch.empty((C * N * 8,), dtype=torch.float32, device=means2d.device)
+    return None
+
+
 def rasterize_to_pixels_fwd(means2d, conics, opacities, mus, tile_offsets, flatten_ids, dim1,
                             dim0, tile_size):
     C, N = _check_raster_inputs(means2d, conics, opacities, mus, tile_offsets, flatten_ids)
@@ -461,9 +468,10 @@ def rasterize_to_pixels_fwd(means2d, conics, opacities, mus, tile_offsets, flatt
         out.zero_()
         return out
     with torch.cuda.device(dev):
+        scratch = _splat_scratch(means2d, C, N, tile)
         _call("r2s_rasterize_to_pixels_fwd", code, _ptr(means2d), _ptr(conics), _ptr(opacities),
               _ptr(mus), _ptr(tile_offsets), _ptr(flatten_ids), C, N, n, W, H, tile, ntx, nty,
-              _ptr(out), _stream(dev))
+              _ptr(scratch), _ptr(out), _stream(dev))
     return out
 
 
@@ -491,9 +499,11 @@ def _raster_bwd(mode, means2d, conics, opacities, mus, tile_offsets, flatten_ids
     nty, ntx = tile_offsets.size(1), tile_offsets.size(2)
     with torch.cuda.device(dev):
         stats = torch.empty((C * N * 8,), dtype=means2d.dtype, device=dev)
+        scratch = _splat_scratch(means2d, C, N, tile)
         _call("r2s_rasterize_to_pixels_bwd", code, mode, _ptr(means2d), _ptr(conics),
               _ptr(opacities), _ptr(mus), _ptr(tile_offsets), _ptr(flatten_ids),
-              _ptr(v_render_output), C, N, n, W, H, tile, ntx, nty, _ptr(stats), _ptr(v_abs),
+              _ptr(v_render_output), C, N, n, W, H, tile, ntx, nty, _ptr(scratch), _ptr(stats),
+              _ptr(v_abs),
               _ptr(v_means2d), _ptr(v_conics), _ptr(v_opac), _ptr(v_mus), _stream(dev))
     return v_abs, v_means2d, v_conics, v_opac, v_mus
 

@@ -186,7 +186,9 @@ R2S_API int r2s_isect_offset_encode(const int64_t* isect_ids, int64_t n_isects, 
  * image[c,i,j] = sum over the tile's list of w*mu*exp(-sigma), skipping
  * sigma < 0 and |alpha| < 1e-5.  Inputs are [C,N,...] flattened
  * (means2d 2, conics 3, opacities 1, mus 1), tile_offsets [C,nty,ntx],
- * flatten_ids [n_isects]; output image [C,H,W].  Replaces
+ * flatten_ids [n_isects]; output image [C,H,W].  `splat_scratch` (nullable,
+ * C*N*32 bytes) lets float32 inputs with 16-pixel tiles take the packed-record
+ * kernel; without it a generic kernel runs.  Replaces
  * rasterize_to_pixels_fwd_tensor (Ops.h:50-53; csrc/RasterizeToPixels.cpp:25-115).
  */
 R2S_API int r2s_rasterize_to_pixels_fwd(int dtype, const void* means2d, const void* conics,
@@ -194,7 +196,8 @@ R2S_API int r2s_rasterize_to_pixels_fwd(int dtype, const void* means2d, const vo
                                 const int32_t* tile_offsets, const int32_t* flatten_ids,
                                 int64_t C, int64_t N, int64_t n_isects, uint32_t width,
                                 uint32_t height, uint32_t tile_size, uint32_t n_tiles_w,
-                                uint32_t n_tiles_h, void* image, r2s_stream_t stream);
+                                uint32_t n_tiles_h, void* splat_scratch, void* image,
+                                r2s_stream_t stream);
 /* VJP w.r.t. means2d, conics, opacities, mus (+ |d means2d| summed per
  * pixel when v_means2d_abs != NULL).  Both reference modes map here:
  * mode 0 = "pixel" (rasterize_to_pixels_bwd_tensor, Ops.h:54-58;
@@ -202,15 +205,16 @@ R2S_API int r2s_rasterize_to_pixels_fwd(int dtype, const void* means2d, const vo
  * (rasterize_to_pixels_bwd_per_gaussian_tensor, Ops.h:59-64;
  * RasterizeToPixels.cpp:225-317).  The modes differ only in the precision
  * of exp for float64 inputs, as in the reference.  `stats` is caller
- * scratch of C*N*8 elements of dtype. */
+ * scratch of C*N*8 elements of dtype; `splat_scratch` as for the forward. */
 R2S_API int r2s_rasterize_to_pixels_bwd(int dtype, int mode, const void* means2d,
                                 const void* conics, const void* opacities, const void* mus,
                                 const int32_t* tile_offsets, const int32_t* flatten_ids,
                                 const void* v_image, int64_t C, int64_t N, int64_t n_isects,
                                 uint32_t width, uint32_t height, uint32_t tile_size,
-                                uint32_t n_tiles_w, uint32_t n_tiles_h, void* stats,
-                                void* v_means2d_abs, void* v_means2d, void* v_conics,
-                                void* v_opacities, void* v_mus, r2s_stream_t stream);
+                                uint32_t n_tiles_w, uint32_t n_tiles_h, void* splat_scratch,
+                                void* stats, void* v_means2d_abs, void* v_means2d,
+                                void* v_conics, void* v_opacities, void* v_mus,
+                                r2s_stream_t stream);
 
 /* ------------------------------------------------------------------------
  * Voxelization: vol[z,y,x] = sum over the brick's list of w*exp(-sigma)

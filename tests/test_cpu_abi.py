@@ -82,7 +82,7 @@ def test_invalid_arguments_are_rejected_before_any_launch(lib):
     assert rc == 1
     # tile size beyond 32 (tile_size**2 > 1024)
     rc = lib.r2s_rasterize_to_pixels_fwd(0, None, None, None, None, None, None, 1, 1, 1, 64, 64, 33,
-                                         2, 2, None, None)
+                                         2, 2, None, None, None)
     assert rc == 1
     buf = ctypes.create_string_buffer(256)
     lib.r2s_last_error(buf, 256)
