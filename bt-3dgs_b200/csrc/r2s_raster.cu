@@ -907,3 +907,80 @@ extern "C" int r2s_raster_splats_bwd_f32(const float* splats, const int32_t* off
     return launch_raster_bwd<float, true, 0>(src, offsets, flatten_ids, v_image, C, N, n_isects, W,
                                              H, T, ntx, nty, with_abs, stats, stream);
 }
+
+// ===========================================================================
+// Backward without caller scratch
+// ===========================================================================
+//
+// Some host programs cannot give this library scratch memory: their device
+// memory belongs to an allocator the plugin may not call (a fixed arena sized
+// at start-up, or a framework that forbids cudaMalloc from inside its
+// operators), and their binding passes only the operator's inputs and
+// outputs.  For them the backward below keeps its scratch -- the
+// per-(view, Gaussian) statistics and the packed splat records, 64 bytes per
+// pair -- in one static device array of the library, so the call allocates
+// nothing.  The array is part of the library's device image: every GPU that
+// loads the library holds its 8 MiB until the process exits.
+#include <mutex>
+
+namespace r2s {
+namespace {
+
+constexpr int64_t kNoAllocMaxPairs = 131072;               // (view, Gaussian) pairs
+constexpr size_t kNoAllocFloats = (size_t)kNoAllocMaxPairs * 16;  // 8 stats + 8 splat floats
+constexpr int kNoAllocMaxDevices = 64;
+
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocFloats];
+
+std::mutex g_noalloc_mutex;
+float* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+// Device address of the static scratch on the current device.  The host-side
+// name g_noalloc_scratch is only a stand-in for the symbol, so the address is
+// looked up once per device with cudaGetSymbolAddress while that device is
+// current (the first call on each device does this) and cached.
+int noalloc_scratch(float** out) {
+    int dev = -1;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess)
+        return fail(R2S_ERR_CUDA, "noalloc: cudaGetDevice failed (%s)", cudaGetErrorString(err));
+    if (dev < 0 || dev >= kNoAllocMaxDevices)
+        return fail(R2S_ERR_UNSUPPORTED, "noalloc: device ordinal %d out of range", dev);
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (g_noalloc_ptr[dev] == nullptr) {
+        void* p = nullptr;
+        err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (err != cudaSuccess || p == nullptr)
+            return fail(R2S_ERR_CUDA, "noalloc: cudaGetSymbolAddress failed on device %d (%s)", dev,
+                        cudaGetErrorString(err));
+        g_noalloc_ptr[dev] = static_cast<float*>(p);
+    }
+    *out = g_noalloc_ptr[dev];
+    return R2S_OK;
+}
+
+}  // namespace
+}  // namespace r2s
+
+extern "C" int r2s_rasterize_to_pixels_bwd_noalloc_f32(
+    int mode, const float* means2d, const float* conics, const float* opacities, const float* mus,
+    const int32_t* offsets, const int32_t* flatten_ids, const float* v_image, int64_t C, int64_t N,
+    int64_t n_isects, uint32_t W, uint32_t H, uint32_t T, uint32_t ntx, uint32_t nty,
+    float* v_means2d_abs, float* v_means2d, float* v_conics, float* v_opacities, float* v_mus,
+    r2s_stream_t stream) {
+    R2S_REQUIRE(C >= 0 && N >= 0, "rasterize_to_pixels_bwd_noalloc: negative size");
+    if (C * N > r2s::kNoAllocMaxPairs)
+        return r2s::fail(R2S_ERR_UNSUPPORTED,
+                         "rasterize_to_pixels_bwd_noalloc: %lld (view, Gaussian) pairs exceed the "
+                         "static scratch of %lld pairs; use r2s_rasterize_to_pixels_bwd with "
+                         "caller scratch",
+                         (long long)(C * N), (long long)r2s::kNoAllocMaxPairs);
+    float* scratch = nullptr;
+    if (int rc = r2s::noalloc_scratch(&scratch)) return rc;
+    float* stats = scratch;
+    float* splats = scratch + (size_t)r2s::kNoAllocMaxPairs * 8;
+    return r2s_rasterize_to_pixels_bwd(R2S_F32, mode, means2d, conics, opacities, mus, offsets,
+                                       flatten_ids, v_image, C, N, n_isects, W, H, T, ntx, nty,
+                                       splats, stats, v_means2d_abs, v_means2d, v_conics,
+                                       v_opacities, v_mus, stream);
+}

@@ -59,6 +59,9 @@ _SIGNATURES = {
     "r2s_rasterize_to_pixels_bwd": (
         [_i32, _i32, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _u32, _u32, _u32, _u32, _u32,
          _p, _p, _p, _p, _p, _p, _p, _p], _i32),
+    "r2s_rasterize_to_pixels_bwd_noalloc_f32": (
+        [_i32, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _u32, _u32, _u32, _u32, _u32, _p, _p,
+         _p, _p, _p, _p], _i32),
     "r2s_voxelize_to_voxels_fwd": (
         [_i32, _p, _p, _p, _p, _p, _i64, _i64, _u32, _u32, _u32, _u32, _u32, _u32, _u32, _p, _p],
         _i32),

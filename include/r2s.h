@@ -216,6 +216,26 @@ R2S_API int r2s_rasterize_to_pixels_bwd(int dtype, int mode, const void* means2d
                                 void* v_conics, void* v_opacities, void* v_mus,
                                 r2s_stream_t stream);
 
+/* Rasterizer backward that allocates nothing and takes no scratch (float32).
+ * No counterpart in the reference.  For host programs that cannot hand this
+ * library scratch memory -- their device memory belongs to an allocator the
+ * plugin may not call (a fixed arena, or a framework that forbids cudaMalloc
+ * inside its operators) and their binding passes only inputs and outputs.
+ * Same arguments and results as r2s_rasterize_to_pixels_bwd without
+ * splat_scratch/stats; the scratch is a static 8 MiB device array of the
+ * library, so C*N is limited to 131072 (view, Gaussian) pairs (larger calls
+ * return R2S_ERR_UNSUPPORTED).  Works on the current device; its first call
+ * on each device looks the array up with cudaGetSymbolAddress and should come
+ * before any stream capture.  Every call reuses the same array: calls that
+ * overlap on the GPU (other streams, other threads) race and must be
+ * serialized by the caller. */
+R2S_API int r2s_rasterize_to_pixels_bwd_noalloc_f32(
+    int mode, const float* means2d, const float* conics, const float* opacities, const float* mus,
+    const int32_t* tile_offsets, const int32_t* flatten_ids, const float* v_image, int64_t C,
+    int64_t N, int64_t n_isects, uint32_t width, uint32_t height, uint32_t tile_size,
+    uint32_t n_tiles_w, uint32_t n_tiles_h, float* v_means2d_abs, float* v_means2d,
+    float* v_conics, float* v_opacities, float* v_mus, r2s_stream_t stream);
+
 /* ------------------------------------------------------------------------
  * Voxelization: vol[z,y,x] = sum over the brick's list of w*exp(-sigma)
  * (6-term quadratic), skipping sigma < 0 and |alpha| < 1e-6.  means3d [N,3],
