@@ -13,10 +13,11 @@
 //            then an exclusive scan of the per-tile totals -> tile offsets
 //            and n_isects (the reference's isect_offset_encode output falls
 //            out of this scan directly)
-//   phase 3  per (segment, chunk): one warp walks the chunk's items in order
-//            and writes each record to offsets[tile] + running count; records
-//            of up to 32 items are packed per step and ranked stably with
-//            __match_any_sync, so equal tiles keep item order
+//   phase 3  per (segment, chunk): one warp walks the chunk's items in order,
+//            one item per step with its records spread over the lanes, and
+//            writes each record to offsets[tile] + running count; an item's
+//            records cover distinct tiles, so lanes never share a counter and
+//            item order is kept without ranking
 //
 // The sorted keys (isect_ids) are a run-length expansion of the offsets and
 // are written by a separate coalesced kernel only when a caller asks for them.
@@ -171,7 +172,6 @@ __global__ void bin_place_kernel(const void* __restrict__ rects, int64_t S, int6
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     int32_t* cnt = smem + (int64_t)warp * T;
-    int32_t* stage = smem + (int64_t)warps * T + warp * 96;  // excl[32], rx[32], ry[32]
     const int64_t gw = (int64_t)blockIdx.x * warps + warp;
     if (gw >= S * n_chunks) return;
     const int64_t s = gw / n_chunks;
@@ -188,43 +188,31 @@ __global__ void bin_place_kernel(const void* __restrict__ rects, int64_t S, int6
         const int64_t i = base + lane;
         ItemRect r{0, 0, 0, 0, 0};
         if (i < i1) r = load_rect<LAYERED>(rects, s, i, N, seg_base + s);
-        const int incl = warp_inclusive_scan(r.n);
-        const int total = __shfl_sync(0xffffffffu, incl, 31);
-        if (total == 0) continue;
-        __syncwarp();
-        stage[lane] = incl - r.n;
-        stage[32 + lane] = (int32_t)pack16(r.x0, r.x1);
-        stage[64 + lane] = (int32_t)pack16(r.y0, r.y1);
-        __syncwarp();
-        for (int r0 = 0; r0 < total; r0 += 32) {
-            const int p = r0 + lane;
-            const bool active = p < total;
-            int tile = 0, src = 0;
-            if (active) {
-                // largest j with excl[j] <= p
-                int lo = 0, hi = 31;
-                while (lo < hi) {
-                    const int mid = (lo + hi + 1) >> 1;
-                    if (stage[mid] <= p) lo = mid; else hi = mid - 1;
-                }
-                src = lo;
-                const int local = p - stage[src];
-                const uint32_t qx = (uint32_t)stage[32 + src], qy = (uint32_t)stage[64 + src];
-                const int w = (int)(hi16(qx) - lo16(qx));
-                const int dy = local / w;
-                const int dx = local - dy * w;
-                tile = (int)(lo16(qy) + dy) * (int)tiles_x + (int)lo16(qx) + dx;
+        unsigned todo = __ballot_sync(0xffffffffu, r.n > 0);
+        const uint32_t px = pack16(r.x0, r.x1), py = pack16(r.y0, r.y1);
+        // One item at a time, in item order: its records cover distinct tiles,
+        // so every lane owns a different counter and no ranking is needed.
+        while (todo) {
+            const int j = __ffs(todo) - 1;
+            todo &= todo - 1;
+            const uint32_t qx = __shfl_sync(0xffffffffu, px, j);
+            const uint32_t qy = __shfl_sync(0xffffffffu, py, j);
+            const int x0 = (int)lo16(qx), w = (int)(hi16(qx) - lo16(qx));
+            const int y0 = (int)lo16(qy), h = (int)(hi16(qy) - lo16(qy));
+            const int n = w * h;
+            const int32_t id = (int32_t)(id_base + base + j);
+            int dy = lane / w;
+            int dx = lane - dy * w;
+            const int sdy = 32 / w, sdx = 32 - sdy * w;
+            for (int q = lane; q < n; q += 32) {
+                const int tile = (y0 + dy) * (int)tiles_x + x0 + dx;
+                const int pos = cnt[tile];
+                flatten_ids[pos] = id;
+                cnt[tile] = pos + 1;
+                dy += sdy;
+                dx += sdx;
+                if (dx >= w) { dx -= w; ++dy; }
             }
-            const unsigned am = __ballot_sync(0xffffffffu, active);
-            int pos = 0;
-            unsigned grp = 0;
-            if (active) {
-                grp = __match_any_sync(am, tile);
-                pos = cnt[tile] + __popc(grp & lanemask_lt());
-                flatten_ids[pos] = (int32_t)(id_base + base + src);
-            }
-            __syncwarp();
-            if (active && (grp >> lane) == 1u) cnt[tile] = pos + 1;
             __syncwarp();
         }
     }
@@ -362,7 +350,7 @@ int bin_place_impl(const void* rects, int64_t S, int64_t N, int64_t T, uint32_t 
     const BinPlan p = make_plan(S, N, T);
     R2S_REQUIRE(ws_bytes >= p.bytes, "binning: workspace too small");
     const WsView w = carve(const_cast<void*>(ws), p);
-    const int per_warp = (int)T * 4 + 96 * 4;
+    const int per_warp = (int)T * 4;
     int warps = kSmemLimit / per_warp;
     warps = warps > 8 ? 8 : (warps < 1 ? 1 : warps);
     const int64_t n_warps = S * p.n_chunks;

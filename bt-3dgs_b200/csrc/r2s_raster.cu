@@ -13,8 +13,10 @@
 //
 // Backward (reference: csrc/RasterizeToPixelsBwd.cu:76-265 "pixel" and
 // 349-480 "primitive"): one CTA per (view, tile) with the tile's upstream
-// gradient in shared memory; each warp takes whole Gaussians and walks only
-// the pixel rectangle that can contribute.  Per (Gaussian, tile) it reduces
+// gradient in shared memory.  The generic kernel gives each warp whole
+// Gaussians and walks only the pixel rectangle that can contribute; the
+// float32 16x16 kernel gives each thread one Gaussian record and walks the
+// rows of its culling box.  Per (Gaussian, tile) both reduce
 // six moments of the contributing pixels,
 //   S0 = sum v e,  Sx = sum v e dx,  Sy = sum v e dy,
 //   Sxx = sum v e dx^2,  Sxy = sum v e dx dy,  Syy = sum v e dy^2
@@ -538,50 +540,61 @@ raster_fwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict
     }
 }
 
-// Eight-value warp sum by transposed butterflies: after the three halving
-// steps lane L holds the partial of value (L >> 2) & 7, finished by two
-// plain steps; 9 shuffles instead of 40.
-__device__ __forceinline__ float warp_sum8_transposed(float v[8]) {
-    const int lane = threadIdx.x & 31;
-    const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
-    float u[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        const float send = b4 ? v[k] : v[k + 4];
-        const float keep = b4 ? v[k + 4] : v[k];
-        u[k] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
-    }
-    float w[2];
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-        const float send = b3 ? u[k] : u[k + 2];
-        const float keep = b3 ? u[k + 2] : u[k];
-        w[k] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
-    }
-    const float send = b2 ? w[0] : w[1];
-    const float keep = b2 ? w[1] : w[0];
-    float x = keep + __shfl_xor_sync(0xffffffffu, send, 4);
-    x += __shfl_xor_sync(0xffffffffu, x, 2);
-    x += __shfl_xor_sync(0xffffffffu, x, 1);
-    return x;
+// Packed float32 pairs (sm_100 f32x2 arithmetic): one instruction updates two
+// adjacent pixels; each lane of the pair is rounded exactly like the scalar
+// instruction.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+        "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
+}
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+        "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+        "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
 }
 
-constexpr int kBwd16Threads = 256;  // 8 warps, one Gaussian per warp at a time
-constexpr int kBwd16Batch = 256;
+constexpr int kBwd16Threads = 256;  // one (view, tile) per CTA, one Gaussian per thread
 
+// Backward statistics of 16x16 tiles, one Gaussian record per thread.
+//
+// The tile's upstream gradient sits in shared memory and every thread walks
+// the 16 columns of the rows its record can reach (rows outside the record's
+// culling box, and pixels failing the alpha cut-off, contribute nothing); a
+// warp executes the union of its lanes' row ranges.  Per pixel: sigma from the
+// column offset dx (exact per column) and the row terms B dy, C dy^2, one ex2,
+// and packed updates of the per-column sums Col_c = sum_rows v e and the row
+// sums sum_c v e, sum_c v e dx.  The moments follow without cancellation:
+//   S0 = sum_c Col_c, Sx = sum_c Col_c dx_c, Sxx = sum_c Col_c dx_c^2,
+//   Sy = sum_r dy_r R0_r, Syy = sum_r dy_r^2 R0_r, Sxy = sum_r dy_r R1_r.
+// No cross-lane reduction is needed; each record adds its eight values with
+// two vector reductions.
 template <bool WITH_ABS>
 __global__ void __launch_bounds__(kBwd16Threads)
 raster_bwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict__ offsets,
                     const int32_t* __restrict__ flatten_ids, int64_t n_keys, int64_t n_isects,
                     const float* __restrict__ v_image, uint32_t W, uint32_t H, uint32_t ntx,
                     uint32_t nty, float* __restrict__ stats) {
-    __shared__ float s_v[16 * 17];
-    __shared__ float4 s_p[kBwd16Batch];  // mx, my, a, b
-    __shared__ float4 s_q[kBwd16Batch];  // c, w*mu, s_thr, unused
-    __shared__ int32_t s_g[kBwd16Batch];
-    __shared__ uint32_t s_box[kBwd16Batch];
+    __shared__ __align__(16) float s_v[256];
 
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int tid = threadIdx.x;
     const int64_t cam = blockIdx.z;
     const int X0 = blockIdx.x * 16, Y0 = blockIdx.y * 16;
     const int64_t key = cam * (int64_t)ntx * nty + (int64_t)blockIdx.y * ntx + blockIdx.x;
@@ -592,98 +605,97 @@ raster_bwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict
     {
         const float* vc = v_image + cam * (int64_t)H * W;
         const int r = tid >> 4, c = tid & 15;
-        s_v[r * 17 + c] = (c <= cmax && r <= rmax) ? vc[(int64_t)(Y0 + r) * W + X0 + c] : 0.f;
+        s_v[tid] = (c <= cmax && r <= rmax) ? vc[(int64_t)(Y0 + r) * W + X0 + c] : 0.f;
     }
-    for (int b0 = start; b0 < end; b0 += kBwd16Batch) {
-        const int n = min(kBwd16Batch, end - b0);
-        __syncthreads();
-        if (tid < n) {
-            const int64_t g = flatten_ids[b0 + tid];
-            const float4 p = splats[2 * g];
-            const float4 q = splats[2 * g + 1];
-            int c_lo, c_hi, r_lo, r_hi;
-            cull_range(p.x, q.z, (float)X0, cmax, c_lo, c_hi);
-            cull_range(p.y, q.w, (float)Y0, rmax, r_lo, r_hi);
-            uint32_t box = 0x000000ffu;  // empty: c_lo 255 > c_hi 0
-            if (c_lo <= c_hi && r_lo <= r_hi)
-                box = (uint32_t)c_lo | ((uint32_t)c_hi << 8) | ((uint32_t)r_lo << 16) |
-                      ((uint32_t)r_hi << 24);
-            s_p[tid] = p;
-            s_q[tid] = make_float4(q.x, q.y, s_threshold(q.y), 0.f);
-            s_g[tid] = (int32_t)g;
-            s_box[tid] = box;
+    __syncthreads();
+    const float X0f = (float)X0, Y0f = (float)Y0;
+
+    // the trip count is the same for every thread: warp votes stay convergent
+    for (int base = start; base < end; base += kBwd16Threads) {
+        const int i = base + tid;
+        int64_t g = 0;
+        float4 p = make_float4(0.f, 0.f, 0.f, 0.f), q = p;
+        int c_lo = 1, c_hi = 0, r_lo = 1, r_hi = 0;
+        if (i < end) {
+            g = flatten_ids[i];
+            p = splats[2 * g];
+            q = splats[2 * g + 1];
+            cull_range(p.x, q.z, X0f, cmax, c_lo, c_hi);
+            cull_range(p.y, q.w, Y0f, rmax, r_lo, r_hi);
         }
-        __syncthreads();
-        for (int t = warp; t < n; t += kBwd16Threads / 32) {
-            const uint32_t bx = s_box[t];
-            const int c_lo = bx & 0xff, c_hi = (bx >> 8) & 0xff;
-            if (c_lo > c_hi) continue;
-            const int r_lo = (bx >> 16) & 0xff, r_hi = bx >> 24;
-            const float4 P = s_p[t];
-            const float4 Q = s_q[t];
-            const uint32_t thr = __float_as_uint(Q.z);
-            const float A = 0.5f * kLog2e * P.z, B = kLog2e * P.w, Cc = 0.5f * kLog2e * Q.x;
-            // Lanes take 4-pixel row segments of the footprint rectangle.  s is
-            // evaluated per pixel (two FMAs with the row terms B*dy and C*dy^2
-            // hoisted); the y moments of a row come from its sums
-            // R0 = sum ve, R1 = sum ve dx, R2 = sum ve dx^2; the absgrad terms
-            // |ve| |a dx + b dy| advance their linear factor by a (resp. b) per
-            // pixel, their sums have no cancellation.
-            const int w = c_hi - c_lo + 1;
-            const int spr = (w + 3) >> 2;
-            const int n_seg = spr * (r_hi - r_lo + 1);
-            const float inv_spr = 1.0f / (float)spr;
-            const float dxb = (float)(X0 + c_lo) + 0.5f - P.x;
-            const float dyb = (float)(Y0 + r_lo) + 0.5f - P.y;
-            const int vbase = r_lo * 17 + c_lo;
-            float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-            for (int sg = lane; sg < n_seg; sg += 32) {
-                const float rf = truncf(((float)sg + 0.5f) * inv_spr);
-                const int row = (int)rf;
-                const int c0 = (sg - row * spr) * 4;
-                const int npx = min(4, w - c0);
-                const float dy = dyb + rf;
-                float dx = dxb + (float)c0;
-                const float by = B * dy;
-                const float cyy = Cc * dy * dy;
-                float qx = fmaf(P.z, dx, P.w * dy);  // a dx + b dy
-                float qy = fmaf(P.w, dx, Q.x * dy);  // b dx + c dy
-                const int vb = vbase + row * 17 + c0;
-                float R0 = 0.f, R1 = 0.f, R2 = 0.f, Ax = 0.f, Ay = 0.f;
+        const bool live = c_lo <= c_hi && r_lo <= r_hi;
+        if (!live) r_lo = 16, r_hi = -1;
+        const int row0 = __reduce_min_sync(0xffffffffu, r_lo);
+        const int row1 = __reduce_max_sync(0xffffffffu, r_hi);
+        if (row0 > row1) continue;
+
+        const float A = 0.5f * kLog2e * p.z, B = kLog2e * p.w, Cc = 0.5f * kLog2e * q.x;
+        const uint32_t thr = __float_as_uint(s_threshold(q.y));
+        const float2 A2 = make_float2(A, A);
+        const float2 a2 = make_float2(p.z, p.z), b2 = make_float2(p.w, p.w);
+        float2 dx[8], col[8];
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    const bool in = k < npx;
-                    const float v = in ? s_v[vb + k] : 0.f;
-                    const float sv = fmaf(dx, fmaf(A, dx, by), cyy);
-                    const float e = exp2f(-sv);
-                    const float ve = s_valid(sv, thr) ? v * e : 0.f;
-                    const float vx = ve * dx;
-                    R0 += ve;
-                    R1 += vx;
-                    R2 = fmaf(vx, dx, R2);
+        for (int j = 0; j < 8; ++j) {
+            dx[j] = make_float2((X0f + (2 * j + 0.5f)) - p.x, (X0f + (2 * j + 1.5f)) - p.x);
+            col[j] = make_float2(0.f, 0.f);
+        }
+        float Sy = 0.f, Syy = 0.f, Sxy = 0.f, Ax = 0.f, Ay = 0.f;
+        for (int r = row0; r <= row1; ++r) {
+            const bool rin = r >= r_lo && r <= r_hi;
+            const float dy = (Y0f + ((float)r + 0.5f)) - p.y;
+            const float by = B * dy, cyy = Cc * dy * dy;
+            const float2 by2 = make_float2(by, by), cyy2 = make_float2(cyy, cyy);
+            const float bdy = p.w * dy, cdy = q.x * dy;
+            const float2 bdy2 = make_float2(bdy, bdy), cdy2 = make_float2(cdy, cdy);
+            const float4* vr = reinterpret_cast<const float4*>(s_v + r * 16);
+            float2 r0 = make_float2(0.f, 0.f), r1 = r0;
+#pragma unroll
+            for (int j4 = 0; j4 < 4; ++j4) {
+                const float4 v4 = vr[j4];
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int j = 2 * j4 + h;
+                    const float2 v2 = h ? make_float2(v4.z, v4.w) : make_float2(v4.x, v4.y);
+                    const float2 t = ffma2(A2, dx[j], by2);
+                    const float2 s = ffma2(dx[j], t, cyy2);
+                    float e0 = exp2f(-s.x), e1 = exp2f(-s.y);
+                    e0 = (rin && s_valid(s.x, thr)) ? e0 : 0.f;
+                    e1 = (rin && s_valid(s.y, thr)) ? e1 : 0.f;
+                    const float2 ve = fmul2(v2, make_float2(e0, e1));
+                    col[j] = fadd2(col[j], ve);
+                    r0 = fadd2(r0, ve);
+                    r1 = ffma2(ve, dx[j], r1);
                     if constexpr (WITH_ABS) {
-                        Ax = fmaf(fabsf(ve), fabsf(qx), Ax);
-                        Ay = fmaf(fabsf(ve), fabsf(qy), Ay);
-                        qx += P.z;
-                        qy += P.w;
+                        const float2 qx = ffma2(a2, dx[j], bdy2);  // a dx + b dy
+                        const float2 qy = ffma2(b2, dx[j], cdy2);  // b dx + c dy
+                        Ax = fmaf(fabsf(ve.x), fabsf(qx.x), Ax);
+                        Ax = fmaf(fabsf(ve.y), fabsf(qx.y), Ax);
+                        Ay = fmaf(fabsf(ve.x), fabsf(qy.x), Ay);
+                        Ay = fmaf(fabsf(ve.y), fabsf(qy.y), Ay);
                     }
-                    dx += 1.0f;
-                }
-                acc[0] += R0;
-                acc[1] += R1;
-                acc[2] = fmaf(dy, R0, acc[2]);
-                acc[3] += R2;
-                acc[4] = fmaf(dy, R1, acc[4]);
-                acc[5] = fmaf(dy * dy, R0, acc[5]);
-                if constexpr (WITH_ABS) {
-                    acc[6] += Ax;
-                    acc[7] += Ay;
                 }
             }
-            const float sum = warp_sum8_transposed(acc);
-            if ((lane & 3) == 0 && (WITH_ABS || (lane >> 2) < 6))
-                atomicAdd(stats + (int64_t)s_g[t] * 8 + (lane >> 2), sum);
+            const float R0 = r0.x + r0.y, R1 = r1.x + r1.y;
+            Sy = fmaf(dy, R0, Sy);
+            Syy = fmaf(dy * dy, R0, Syy);
+            Sxy = fmaf(dy, R1, Sxy);
         }
+        if (!live) continue;
+        float S0 = 0.f, Sx = 0.f, Sxx = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            S0 += col[j].x + col[j].y;
+            const float2 cx = fmul2(col[j], dx[j]);
+            Sx += cx.x + cx.y;
+            Sxx = fmaf(cx.x, dx[j].x, Sxx);
+            Sxx = fmaf(cx.y, dx[j].y, Sxx);
+        }
+        float* st = stats + g * 8;
+        red_add_v4(st, S0, Sx, Sy, Sxx);
+        if constexpr (WITH_ABS)
+            red_add_v4(st + 4, Sxy, Syy, Ax, Ay);
+        else
+            red_add_v2(st + 4, Sxy, Syy);
     }
 }
 

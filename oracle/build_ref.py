@@ -12,8 +12,9 @@ the reference's nvcc flags (``setup.py:23-48``: ``-O3 --use_fast_math
 to ``oracle/_ref/build``; the module is copied to
 ``oracle/_ref/r2splat_ref_csrc.so`` so it can travel without the sources.
 
-Usage: ``python oracle/build_ref.py [reference_root]`` (default
-``/root/reference``).  Takes ~6 minutes with 8 cores.
+Usage: ``python oracle/build_ref.py [reference_root]`` (default: the
+``BT3DGS_REFERENCE_ROOT`` environment variable, else ``oracle.REFERENCE_ROOT``).
+Takes ~6 minutes with 8 cores.
 """
 from __future__ import annotations
 
@@ -22,13 +23,16 @@ import os
 import shutil
 import sys
 
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+from oracle import REFERENCE_ROOT  # noqa: E402
+
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT_DIR = os.path.join(HERE, "_ref")
 MODULE_NAME = "r2splat_ref_csrc"
 SO_PATH = os.path.join(OUT_DIR, MODULE_NAME + ".so")
 
 
-def build(reference_root: str = "/root/reference") -> str:
+def build(reference_root: str = REFERENCE_ROOT) -> str:
     from torch.utils.cpp_extension import load
 
     csrc = os.path.join(reference_root, "r2splat", "cuda", "csrc")
@@ -59,5 +63,5 @@ def build(reference_root: str = "/root/reference") -> str:
 
 
 if __name__ == "__main__":
-    root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    root = sys.argv[1] if len(sys.argv) > 1 else REFERENCE_ROOT
     print(build(root))

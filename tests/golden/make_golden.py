@@ -1,6 +1,6 @@
 """Generate the golden known-answer fixtures under tests/golden/.
 
-Runs only where the reference checkout exists (default /root/reference).  It
+Runs only where the reference checkout exists (``oracle.REFERENCE_ROOT``).  It
 loads the dense PyTorch reference functions of the reference's own CUDA test
 suite -- ``_covars_from_quats_scales_reference``,
 ``_unpack_covariance_reference``, ``_raster_reference`` and
@@ -21,6 +21,9 @@ import os
 import sys
 
 import torch
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))))
+from oracle import REFERENCE_ROOT  # noqa: E402
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 HELPERS = (
@@ -44,7 +47,7 @@ def load_reference_helpers(ref_root: str) -> dict:
     return ns
 
 
-def main(ref_root: str = "/root/reference") -> str:
+def main(ref_root: str = REFERENCE_ROOT) -> str:
     h = load_reference_helpers(ref_root)
     out = {}
 
@@ -141,4 +144,4 @@ def main(ref_root: str = "/root/reference") -> str:
 
 
 if __name__ == "__main__":
-    print(main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference"))
+    print(main(sys.argv[1] if len(sys.argv) > 1 else REFERENCE_ROOT))
