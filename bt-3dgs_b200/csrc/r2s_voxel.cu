@@ -422,6 +422,256 @@ __global__ void voxel_bwd_kernel(VoxSrc<S> src, const int32_t* __restrict__ offs
     }
 }
 
+// ===========================================================================
+// float32, 8x8x8 bricks: the fast kernels
+// ===========================================================================
+//
+// Validity test as in the 16x16 rasterizer: with s = sigma*log2(e) the
+// reference's test (sigma >= 0 and |w exp(-sigma)| >= 1e-6) is
+// 0 <= s <= log2(|w| 1e6), decided by one unsigned compare of the bits of s.
+// Pairs within rounding of the cut-off may be decided differently from the
+// reference's float test; each such pair moves a voxel by at most ~1e-6.
+
+__device__ __forceinline__ bool s_valid_v(float s, uint32_t thr_bits) {
+    return __float_as_uint(s) <= thr_bits;
+}
+
+__device__ __forceinline__ float s_threshold_v(float w) {
+    const float a = fabsf(w) * 1e6f;
+    return a >= 1.0f ? log2f(a) : -1.0f;  // records with a < 1 have an empty box
+}
+
+struct VRecord {
+    float m[3];
+    float A, B, Cq, D, E, F;  // pre-scaled conic: sigma log2(e) = dx (A dx + B dy + Cq dz) + dy (D dy + E dz) + F dz^2
+    float w;
+    float e[3];
+};
+
+__device__ __forceinline__ VRecord load_vrecord(const float4* __restrict__ vsplats, int64_t g) {
+    const float4 a = vsplats[4 * g], b = vsplats[4 * g + 1], c = vsplats[4 * g + 2],
+                 d = vsplats[4 * g + 3];
+    VRecord r;
+    r.m[0] = a.x;
+    r.m[1] = a.y;
+    r.m[2] = a.z;
+    r.A = 0.5f * kLog2eV * a.w;
+    r.B = kLog2eV * b.x;
+    r.Cq = kLog2eV * b.y;
+    r.D = 0.5f * kLog2eV * b.z;
+    r.E = kLog2eV * b.w;
+    r.F = 0.5f * kLog2eV * c.x;
+    r.w = c.y;
+    r.e[0] = c.z;
+    r.e[1] = c.w;
+    r.e[2] = d.x;
+    return r;
+}
+
+constexpr int kVFwd8Threads = 128;  // 4 warps; a warp owns two z-slices, a thread 2x2 voxels (x, z)
+constexpr int kVFwd8Batch = 128;
+
+__global__ void __launch_bounds__(kVFwd8Threads)
+voxel_fwd8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict__ offsets,
+                  const int32_t* __restrict__ flatten_ids, int64_t n_keys, int64_t n_isects,
+                  uint32_t dim2, uint32_t dim1, uint32_t dim0, uint32_t nt2, uint32_t nt1,
+                  uint32_t layer_begin, float* __restrict__ vol) {
+    __shared__ float4 s_a[kVFwd8Batch];  // mx, my, mz, A
+    __shared__ float4 s_b[kVFwd8Batch];  // B, Cq, D, E
+    __shared__ float4 s_c[kVFwd8Batch];  // F, w, s threshold, warp mask (bits)
+
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const uint32_t bz = blockIdx.z + layer_begin;
+    const int64_t key = ((int64_t)blockIdx.z * nt1 + blockIdx.y) * nt2 + blockIdx.x;
+    const int X0 = blockIdx.x * 8, Y0 = blockIdx.y * 8, Z0 = bz * 8;
+    const int xmax = min(7, (int)dim2 - 1 - X0);
+    const int ymax = min(7, (int)dim1 - 1 - Y0);
+    const int zmax = min(7, (int)dim0 - 1 - Z0);
+    const int lx = (tid & 3) * 2, ly = (tid >> 2) & 7, lz = warp * 2;
+    const float2 px = make_float2((float)(X0 + lx) + 0.5f, (float)(X0 + lx) + 1.5f);
+    const float py = (float)(Y0 + ly) + 0.5f;
+    const float pz0 = (float)(Z0 + lz) + 0.5f, pz1 = (float)(Z0 + lz) + 1.5f;
+    const int start = offsets[key];
+    const int end = key + 1 < n_keys ? offsets[key + 1] : (int)n_isects;
+    float a00 = 0.f, a01 = 0.f, a10 = 0.f, a11 = 0.f;  // (z, x) offsets
+
+    for (int b0 = start; b0 < end; b0 += kVFwd8Batch) {
+        const int n = min(kVFwd8Batch, end - b0);
+        __syncthreads();
+        if (tid < n) {
+            const int64_t g = flatten_ids[b0 + tid];
+            const VRecord r = load_vrecord(vsplats, g);
+            int xl, xh, yl, yh, zl, zh;
+            cull_range_v(r.m[0], r.e[0], (float)X0, xmax, xl, xh);
+            cull_range_v(r.m[1], r.e[1], (float)Y0, ymax, yl, yh);
+            cull_range_v(r.m[2], r.e[2], (float)Z0, zmax, zl, zh);
+            uint32_t msk = 0;
+            if (xl <= xh && yl <= yh && zl <= zh) {
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    if (zl <= 2 * k + 1 && zh >= 2 * k) msk |= 1u << k;
+            }
+            s_a[tid] = make_float4(r.m[0], r.m[1], r.m[2], r.A);
+            s_b[tid] = make_float4(r.B, r.Cq, r.D, r.E);
+            s_c[tid] = make_float4(r.F, r.w, s_threshold_v(r.w), __uint_as_float(msk));
+        }
+        __syncthreads();
+        for (int t = 0; t < n; ++t) {
+            const float4 c = s_c[t];
+            if (!((__float_as_uint(c.w) >> warp) & 1u)) continue;  // warp-uniform
+            const float4 a = s_a[t], b = s_b[t];
+            const uint32_t thr = __float_as_uint(c.z);
+            const float2 dx = make_float2(px.x - a.x, px.y - a.x);
+            const float dy = py - a.y;
+            const float dz0 = pz0 - a.z, dz1 = pz1 - a.z;
+            const float bdy = b.x * dy, ddy = b.z * dy;
+            const float u0 = fmaf(b.y, dz0, bdy), u1 = fmaf(b.y, dz1, bdy);
+            const float q0 = fmaf(dy, fmaf(b.w, dz0, ddy), c.x * dz0 * dz0);
+            const float q1 = fmaf(dy, fmaf(b.w, dz1, ddy), c.x * dz1 * dz1);
+            const float2 A2 = make_float2(a.w, a.w);
+            const float2 s0 = ffma2(dx, ffma2(A2, dx, make_float2(u0, u0)), make_float2(q0, q0));
+            const float2 s1 = ffma2(dx, ffma2(A2, dx, make_float2(u1, u1)), make_float2(q1, q1));
+            const float e00 = exp2f(-s0.x), e01 = exp2f(-s0.y);
+            const float e10 = exp2f(-s1.x), e11 = exp2f(-s1.y);
+            if (s_valid_v(s0.x, thr)) a00 = fmaf(c.y, e00, a00);
+            if (s_valid_v(s0.y, thr)) a01 = fmaf(c.y, e01, a01);
+            if (s_valid_v(s1.x, thr)) a10 = fmaf(c.y, e10, a10);
+            if (s_valid_v(s1.y, thr)) a11 = fmaf(c.y, e11, a11);
+        }
+    }
+    if (ly > ymax) return;
+    const int64_t zoff = (int64_t)layer_begin * 8;
+    float* row0 = vol + ((Z0 + lz - zoff) * (int64_t)dim1 + (Y0 + ly)) * dim2 + X0 + lx;
+    float* row1 = row0 + (int64_t)dim1 * dim2;
+    if (lz <= zmax) {
+        if (lx <= xmax) row0[0] = a00;
+        if (lx + 1 <= xmax) row0[1] = a01;
+    }
+    if (lz + 1 <= zmax) {
+        if (lx <= xmax) row1[0] = a10;
+        if (lx + 1 <= xmax) row1[1] = a11;
+    }
+}
+
+constexpr int kVBwd8Threads = 256;  // one brick per CTA, one Gaussian record per thread
+
+// Backward statistics of 8x8x8 bricks, one record per thread: the thread walks
+// the (y, z) rows of its culling box (a warp executes the union of its
+// lanes' rows) and the 8 voxels of each row in packed pairs.  Per-column sums
+// Col_x = sum v e over rows give S0, Sx, Sxx; per-row sums R0 = sum_x v e and
+// R1 = sum_x v e dx give the y/z moments, so every moment is a direct sum.
+__global__ void __launch_bounds__(kVBwd8Threads)
+voxel_bwd8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict__ offsets,
+                  const int32_t* __restrict__ flatten_ids, int64_t n_keys, int64_t n_isects,
+                  const float* __restrict__ v_vol, uint32_t dim2, uint32_t dim1, uint32_t dim0,
+                  uint32_t nt2, uint32_t nt1, uint32_t layer_begin, float* __restrict__ stats) {
+    __shared__ __align__(16) float s_v[512];
+
+    const int tid = threadIdx.x;
+    const uint32_t bz = blockIdx.z + layer_begin;
+    const int64_t key = ((int64_t)blockIdx.z * nt1 + blockIdx.y) * nt2 + blockIdx.x;
+    const int X0 = blockIdx.x * 8, Y0 = blockIdx.y * 8, Z0 = bz * 8;
+    const int xmax = min(7, (int)dim2 - 1 - X0);
+    const int ymax = min(7, (int)dim1 - 1 - Y0);
+    const int zmax = min(7, (int)dim0 - 1 - Z0);
+    const int start = offsets[key];
+    const int end = key + 1 < n_keys ? offsets[key + 1] : (int)n_isects;
+    if (start >= end) return;
+    const int64_t zoff = (int64_t)layer_begin * 8;
+    for (int p = tid; p < 512; p += kVBwd8Threads) {
+        const int z = p >> 6, y = (p >> 3) & 7, x = p & 7;
+        s_v[p] = (x <= xmax && y <= ymax && z <= zmax)
+                     ? v_vol[((Z0 + z - zoff) * (int64_t)dim1 + (Y0 + y)) * dim2 + X0 + x]
+                     : 0.f;
+    }
+    __syncthreads();
+    const float X0f = (float)X0, Y0f = (float)Y0, Z0f = (float)Z0;
+
+    // the trip count is the same for every thread: warp votes stay convergent
+    for (int base = start; base < end; base += kVBwd8Threads) {
+        const int i = base + tid;
+        int64_t g = 0;
+        VRecord r{};
+        int xl = 1, xh = 0, yl = 1, yh = 0, zl = 1, zh = 0;
+        if (i < end) {
+            g = flatten_ids[i];
+            r = load_vrecord(vsplats, g);
+            cull_range_v(r.m[0], r.e[0], X0f, xmax, xl, xh);
+            cull_range_v(r.m[1], r.e[1], Y0f, ymax, yl, yh);
+            cull_range_v(r.m[2], r.e[2], Z0f, zmax, zl, zh);
+        }
+        const bool live = xl <= xh && yl <= yh && zl <= zh;
+        if (!live) yl = zl = 8, yh = zh = -1;
+        const int z0 = __reduce_min_sync(0xffffffffu, zl);
+        const int z1 = __reduce_max_sync(0xffffffffu, zh);
+        const int y0 = __reduce_min_sync(0xffffffffu, yl);
+        const int y1 = __reduce_max_sync(0xffffffffu, yh);
+        if (z0 > z1) continue;
+
+        const uint32_t thr = __float_as_uint(s_threshold_v(r.w));
+        const float2 A2 = make_float2(r.A, r.A);
+        float2 dx[4], col[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            dx[j] = make_float2((X0f + (2 * j + 0.5f)) - r.m[0], (X0f + (2 * j + 1.5f)) - r.m[0]);
+            col[j] = make_float2(0.f, 0.f);
+        }
+        float Sy = 0.f, Sz = 0.f, Syy = 0.f, Syz = 0.f, Szz = 0.f, Sxy = 0.f, Sxz = 0.f;
+        for (int z = z0; z <= z1; ++z) {
+            const bool zin = z >= zl && z <= zh;
+            const float dz = (Z0f + ((float)z + 0.5f)) - r.m[2];
+            const float cdz = r.Cq * dz, edz = r.E * dz, fzz = r.F * dz * dz;
+            for (int y = y0; y <= y1; ++y) {
+                const bool rin = zin && y >= yl && y <= yh;
+                const float dy = (Y0f + ((float)y + 0.5f)) - r.m[1];
+                const float by = fmaf(r.B, dy, cdz);
+                const float rest = fmaf(dy, fmaf(r.D, dy, edz), fzz);
+                const float2 by2 = make_float2(by, by), rest2 = make_float2(rest, rest);
+                const float4* vr = reinterpret_cast<const float4*>(s_v + z * 64 + y * 8);
+                const float4 va = vr[0], vb = vr[1];
+                float2 r0 = make_float2(0.f, 0.f), r1 = r0;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float2 v2 = j == 0   ? make_float2(va.x, va.y)
+                                      : j == 1 ? make_float2(va.z, va.w)
+                                      : j == 2 ? make_float2(vb.x, vb.y)
+                                               : make_float2(vb.z, vb.w);
+                    const float2 s = ffma2(dx[j], ffma2(A2, dx[j], by2), rest2);
+                    float e0 = exp2f(-s.x), e1 = exp2f(-s.y);
+                    e0 = (rin && s_valid_v(s.x, thr)) ? e0 : 0.f;
+                    e1 = (rin && s_valid_v(s.y, thr)) ? e1 : 0.f;
+                    const float2 ve = fmul2(v2, make_float2(e0, e1));
+                    col[j] = fadd2(col[j], ve);
+                    r0 = fadd2(r0, ve);
+                    r1 = ffma2(ve, dx[j], r1);
+                }
+                const float R0 = r0.x + r0.y, R1 = r1.x + r1.y;
+                Sy = fmaf(dy, R0, Sy);
+                Sz = fmaf(dz, R0, Sz);
+                Syy = fmaf(dy * dy, R0, Syy);
+                Syz = fmaf(dy * dz, R0, Syz);
+                Szz = fmaf(dz * dz, R0, Szz);
+                Sxy = fmaf(dy, R1, Sxy);
+                Sxz = fmaf(dz, R1, Sxz);
+            }
+        }
+        if (!live) continue;
+        float S0 = 0.f, Sx = 0.f, Sxx = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            S0 += col[j].x + col[j].y;
+            const float2 cx = fmul2(col[j], dx[j]);
+            Sx += cx.x + cx.y;
+            Sxx = fmaf(cx.x, dx[j].x, Sxx);
+            Sxx = fmaf(cx.y, dx[j].y, Sxx);
+        }
+        float* st = stats + g * 12;
+        red_add_v4(st, S0, Sx, Sy, Sz);
+        red_add_v4(st + 4, Sxx, Sxy, Sxz, Syy);
+        red_add_v2(st + 8, Syz, Szz);
+    }
+}
+
 template <typename S>
 __global__ void voxel_unpack_kernel(const S* __restrict__ stats, const S* __restrict__ conics,
                                     const S* __restrict__ opac, int64_t N, S* __restrict__ v_m3,
@@ -577,6 +827,14 @@ extern "C" int r2s_voxel_splats_fwd_f32(const float* vsplats, const int32_t* off
         cudaMemsetAsync(volume, 0, (size_t)(ze - zb) * dim1 * dim2 * 4, stream);
         return check_launch("voxel_splats_fwd");
     }
+    if (T == 8) {
+        const dim3 grid(nt2, nt1, layer_end - layer_begin);
+        voxel_fwd8_kernel<<<grid, kVFwd8Threads, 0, stream>>>(
+            (const float4*)vsplats, offsets, flatten_ids,
+            (int64_t)(layer_end - layer_begin) * nt1 * nt2, n_isects, dim2, dim1, dim0, nt2, nt1,
+            layer_begin, volume);
+        return check_launch("voxel_splats_fwd");
+    }
     VoxSrc<float> src{(const float4*)vsplats, nullptr, nullptr, nullptr};
     return launch_voxel_fwd<float, true>(src, offsets, flatten_ids, n_isects, dim2, dim1, dim0, T,
                                          nt2, nt1, layer_begin, layer_end, volume, stream);
@@ -592,6 +850,17 @@ extern "C" int r2s_voxel_splats_bwd_f32(const float* vsplats, const int32_t* off
     R2S_REQUIRE(layer_begin <= layer_end && layer_end <= nt0, "voxel_splats_bwd: bad layer range");
     if (int rc = check_bricks(T, nt2, nt1, nt0)) return rc;
     if (N == 0) return R2S_OK;
+    if (T == 8) {
+        cudaMemsetAsync(stats, 0, (size_t)N * 12 * sizeof(float), stream);
+        if (n_isects > 0 && layer_end > layer_begin) {
+            const dim3 grid(nt2, nt1, layer_end - layer_begin);
+            voxel_bwd8_kernel<<<grid, kVBwd8Threads, 0, stream>>>(
+                (const float4*)vsplats, offsets, flatten_ids,
+                (int64_t)(layer_end - layer_begin) * nt1 * nt2, n_isects, v_volume, dim2, dim1,
+                dim0, nt2, nt1, layer_begin, stats);
+        }
+        return check_launch("voxel_splats_bwd");
+    }
     VoxSrc<float> src{(const float4*)vsplats, nullptr, nullptr, nullptr};
     return launch_voxel_bwd<float, true, 0>(src, offsets, flatten_ids, v_volume, N, n_isects, dim2,
                                             dim1, dim0, T, nt2, nt1, layer_begin, layer_end, stats,

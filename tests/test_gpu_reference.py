@@ -4,8 +4,8 @@ CUDA sources compiled for sm_100a by oracle/build_ref.py).
 Integer outputs (radii, tiles per Gaussian, sorted keys, flatten ids, tile
 offsets) must be identical; floating-point outputs within rel-L2 1e-5
 (float32).  Inputs are seeded synthetic workloads with the shapes of
-benchmark configs 0 and 1 (config 1 reduced in views to keep the test
-short).
+benchmark configs 0, 1 and 2 (configs 1 and 2 reduced in views to keep the
+test short; config 2 keeps its 500k Gaussians, 512^2 detector and 256^3 grid).
 """
 import os
 
@@ -49,6 +49,7 @@ def _workload(cfg_id, n=None, views=None, det=None, grid=None):
 CASES = {
     "cfg0": dict(cfg_id=0),
     "cfg1-8views": dict(cfg_id=1, views=8),
+    "cfg2-4views": dict(cfg_id=2, views=4),
 }
 
 
@@ -257,3 +258,37 @@ def test_fused_op_layer_accumulates_existing_grads(case):
         grads.append({k: t.grad.clone() for k, t in params.items()})
     for k in grads[0]:
         torch.testing.assert_close(grads[1][k], grads[0][k] + 1.0, rtol=1e-5, atol=1e-6)
+
+
+def test_fused_voxel_gradients_alone_match_reference(ref, case):
+    """Volume-only upstream gradient: the voxel backward chain is compared on
+    its own (the projection's upstream gradient is zero)."""
+    name, d = case
+    import r2s_workloads as wl
+    from r2splat.ops import explicit as E
+
+    det, G = d["det"], d["grid"]
+    params = {k: d[k].clone().requires_grad_(True) for k in ("means", "quats", "scales", "opac")}
+    state = E.prepare_explicit_gaussians(params["quats"], params["scales"], params["opac"],
+                                         scale_min=wl.SCALE_MIN, scale_max=wl.SCALE_MAX)
+    res = E.explicit_rasterize(state, params["means"], d["viewmats"], d["Ks"], img_w=det, img_h=det,
+                               tile_size=wl.IMG_TILE, eps2d=wl.EPS2D, radius_clip=wl.RADIUS_CLIP,
+                               absgrad=False)
+    vres = E.explicit_voxelize(state, params["means"], d["ranges"], d["centers"], dim2=G, dim1=G,
+                               dim0=G, tile_size=wl.VOL_TILE, eps3d=wl.EPS3D,
+                               radius_clip=wl.RADIUS_CLIP)
+    g = torch.Generator(device="cuda").manual_seed(11)
+    v_vol = torch.randn(vres.volume.shape, generator=g, device="cuda")
+    (res.image * 0).sum().backward()
+    (vres.volume * v_vol).sum().backward()
+    E.explicit_backward(state, params["means"], params["quats"], params["scales"], params["opac"])
+    covars, max_s, opac = ref.prepare(d["quats"], d["scales"], d["opac"], wl.SCALE_MIN, wl.SCALE_MAX)
+    v = ref.voxelize_forward(d["means"], covars, max_s, opac, d["ranges"], d["centers"], G, G, G,
+                             wl.VOL_TILE, wl.EPS3D, wl.RADIUS_CLIP)
+    assert rel_l2(vres.volume, v["output"]) < REL_L2_F32
+    theirs = ref.explicit_backward(None, None, v, v_vol, d["means"], d["quats"], d["scales"],
+                                   d["opac"], covars, opac, wl.SCALE_MIN, wl.SCALE_MAX)
+    for key, pk in (("means", "means"), ("quats", "quats"), ("scales", "scales"),
+                    ("opac", "opacities")):
+        e = rel_l2(params[key].grad, theirs[pk])
+        assert e < REL_L2_F32, f"{name}: voxel-only grad {key} rel-L2 {e:.3e}"
