@@ -218,6 +218,157 @@ __global__ void bin_place_kernel(const void* __restrict__ rects, int64_t S, int6
     }
 }
 
+// Warp walk over items [w0, w1) in item order: for every record (item, tile)
+// calls emit(tile, item - i_base) on one lane.  One item per step, its records
+// spread over the lanes; an item's records cover distinct tiles, so lanes of
+// one step never share a tile.
+template <bool LAYERED, typename Emit>
+__device__ __forceinline__ void walk_items(const void* __restrict__ rects, int64_t s, int64_t N,
+                                           int64_t layer, int64_t w0, int64_t w1, int64_t i_base,
+                                           uint32_t tiles_x, Emit&& emit) {
+    const int lane = threadIdx.x & 31;
+    for (int64_t base = w0; base < w1; base += 32) {
+        const int64_t i = base + lane;
+        ItemRect r{0, 0, 0, 0, 0};
+        if (i < w1) r = load_rect<LAYERED>(rects, s, i, N, layer);
+        unsigned todo = __ballot_sync(0xffffffffu, r.n > 0);
+        const uint32_t px = pack16(r.x0, r.x1), py = pack16(r.y0, r.y1);
+        const int local0 = (int)(base - i_base);
+        while (todo) {
+            const int j = __ffs(todo) - 1;
+            todo &= todo - 1;
+            const uint32_t qx = __shfl_sync(0xffffffffu, px, j);
+            const uint32_t qy = __shfl_sync(0xffffffffu, py, j);
+            const int x0 = (int)lo16(qx), w = (int)(hi16(qx) - lo16(qx));
+            const int y0 = (int)lo16(qy), h = (int)(hi16(qy) - lo16(qy));
+            const int n = w * h;
+            // q / w for q < 2^21 records by a float reciprocal: (q + 0.5) / w
+            // lies at least 0.5 / w from an integer, far above the rounding
+            const float rw = 1.0f / (float)w;
+            int dy = (int)(((float)lane + 0.5f) * rw);
+            int dx = lane - dy * w;
+            const int sdy = (int)(32.5f * rw), sdx = 32 - sdy * w;
+            for (int q = lane; q < n; q += 32) {
+                emit((y0 + dy) * (int)tiles_x + x0 + dx, local0 + j);
+                dy += sdy;
+                dx += sdx;
+                if (dx >= w) {
+                    dx -= w;
+                    ++dy;
+                }
+            }
+            __syncwarp();
+        }
+    }
+}
+
+// Exclusive scan of v[0, n) into out[0, n) by one CTA; returns the total to
+// every thread.  scratch holds 33 ints (one per warp, <= 32 warps, and the total).
+__device__ __forceinline__ int block_exclusive_scan(const int32_t* v, int32_t* out, int n,
+                                                    int32_t* scratch) {
+    const int tid = threadIdx.x, nthr = blockDim.x, lane = tid & 31, warp = tid >> 5;
+    const int per = (n + nthr - 1) / nthr;
+    const int b = min(n, tid * per), e = min(n, b + per);
+    int local = 0;
+    for (int j = b; j < e; ++j) local += v[j];
+    const int incl = warp_inclusive_scan(local);
+    if (lane == 31) scratch[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        const int nw = nthr >> 5;
+        const int x = lane < nw ? scratch[lane] : 0;
+        const int xi = warp_inclusive_scan(x);
+        if (lane < nw) scratch[lane] = xi - x;
+        if (lane == nw - 1) scratch[32] = xi;
+    }
+    __syncthreads();
+    int run = scratch[warp] + incl - local;
+    for (int j = b; j < e; ++j) {
+        const int c = v[j];
+        out[j] = run;
+        run += c;
+    }
+    const int total = scratch[32];
+    __syncthreads();
+    return total;
+}
+
+constexpr int kStagedWarps = 8;
+
+// Phase 3, staged: one CTA per (segment, chunk).  Warps take consecutive
+// sub-chunks; a counting walk gives per-(warp, tile) counts, whose prefix over
+// warps and tiles places every record of the chunk in a tile-major staging
+// buffer in shared memory (16-bit item offsets), in item order per tile.  The
+// buffer is then written out one tile run at a time, so each tile's records
+// of the chunk reach global memory as one contiguous store sequence.  A chunk
+// with more records than the buffer holds writes its records directly.
+template <bool LAYERED>
+__global__ void __launch_bounds__(kStagedWarps * 32)
+bin_place_staged_kernel(const void* __restrict__ rects, int64_t N, int T, uint32_t tiles_x,
+                        int64_t seg_base, int64_t chunk, int64_t n_chunks,
+                        const int32_t* __restrict__ hist, const int32_t* __restrict__ offsets,
+                        int32_t* __restrict__ flatten_ids, int cap) {
+    extern __shared__ __align__(16) int32_t smem[];
+    __shared__ int32_t s_scan[33];
+    const int tid = threadIdx.x, nthr = blockDim.x, warp = tid >> 5, lane = tid & 31;
+    int32_t* wc = smem;                  // [warps][T]: counts, then running positions
+    int32_t* gpos = wc + kStagedWarps * T;  // [T] first global position of the chunk's run
+    int32_t* tot = gpos + T;             // [T] records of the chunk per tile
+    int32_t* lofs = tot + T;             // [T] first staging slot per tile
+    uint16_t* stage = reinterpret_cast<uint16_t*>(lofs + T);
+
+    const int64_t s = blockIdx.x / n_chunks;
+    const int64_t k = blockIdx.x - s * n_chunks;
+    const int64_t i0 = k * chunk;
+    const int64_t i1 = min(N, i0 + chunk);
+    const int64_t layer = seg_base + s;
+    const int64_t id0 = (LAYERED ? 0 : s * N) + i0;
+    const int64_t per = (((i1 - i0) + kStagedWarps * 32 - 1) / (kStagedWarps * 32)) * 32;
+    const int64_t w0 = min(i1, i0 + warp * per), w1 = min(i1, w0 + per);
+    const int32_t* hrow = hist + (s * n_chunks + k) * (int64_t)T;
+    const int32_t* orow = offsets + s * (int64_t)T;
+    for (int t = tid; t < kStagedWarps * T; t += nthr) wc[t] = 0;
+    for (int t = tid; t < T; t += nthr) gpos[t] = orow[t] + hrow[t];
+    __syncthreads();
+
+    int32_t* mine = wc + warp * T;
+    walk_items<LAYERED>(rects, s, N, layer, w0, w1, i0, tiles_x,
+                        [&](int tile, int) { mine[tile] += 1; });
+    __syncthreads();
+    for (int t = tid; t < T; t += nthr) {
+        int run = 0;
+#pragma unroll
+        for (int w = 0; w < kStagedWarps; ++w) {
+            const int c = wc[w * T + t];
+            wc[w * T + t] = run;
+            run += c;
+        }
+        tot[t] = run;
+    }
+    __syncthreads();
+    const int total = block_exclusive_scan(tot, lofs, T, s_scan);
+    if (total <= cap) {
+        walk_items<LAYERED>(rects, s, N, layer, w0, w1, i0, tiles_x, [&](int tile, int local) {
+            const int p = mine[tile];
+            mine[tile] = p + 1;
+            stage[lofs[tile] + p] = (uint16_t)local;
+        });
+        __syncthreads();
+        for (int t = warp; t < T; t += kStagedWarps) {
+            const int n = tot[t];
+            const uint16_t* src = stage + lofs[t];
+            int32_t* dst = flatten_ids + gpos[t];
+            for (int j = lane; j < n; j += 32) dst[j] = (int32_t)(id0 + src[j]);
+        }
+    } else {
+        walk_items<LAYERED>(rects, s, N, layer, w0, w1, i0, tiles_x, [&](int tile, int local) {
+            const int p = mine[tile];
+            mine[tile] = p + 1;
+            flatten_ids[gpos[tile] + p] = (int32_t)(id0 + local);
+        });
+    }
+}
+
 // Run-length expansion of the offsets into sorted int64 keys: one warp per key.
 __global__ void decode_keys_kernel(const int32_t* __restrict__ offsets, int64_t n_keys,
                                    int64_t n_isects, int64_t key_base,
@@ -350,6 +501,34 @@ int bin_place_impl(const void* rects, int64_t S, int64_t N, int64_t T, uint32_t 
     const BinPlan p = make_plan(S, N, T);
     R2S_REQUIRE(ws_bytes >= p.bytes, "binning: workspace too small");
     const WsView w = carve(const_cast<void*>(ws), p);
+    // staged placement when the per-(warp, tile) counters leave room for a
+    // staging buffer of at least 4096 records in ~104 KB (two CTAs per SM)
+    constexpr int kStagedSmem = 104 * 1024;
+    const int64_t fixed = (int64_t)(kStagedWarps + 3) * T * 4;
+    const int64_t cap = ((kStagedSmem - fixed) / 2) & ~int64_t(7);
+    if (cap >= 4096 && p.chunk <= 65536) {
+        const size_t smem = (size_t)(fixed + cap * 2);
+        const unsigned blocks = (unsigned)(S * p.n_chunks);
+        if (layered) {
+            cudaFuncSetAttribute(bin_place_staged_kernel<true>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            bin_place_staged_kernel<true><<<blocks, kStagedWarps * 32, smem, stream>>>(
+                rects, N, (int)T, tiles_x, seg_base, p.chunk, p.n_chunks, w.hist, offsets,
+                flatten_ids, (int)cap);
+        } else {
+            cudaFuncSetAttribute(bin_place_staged_kernel<false>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            bin_place_staged_kernel<false><<<blocks, kStagedWarps * 32, smem, stream>>>(
+                rects, N, (int)T, tiles_x, seg_base, p.chunk, p.n_chunks, w.hist, offsets,
+                flatten_ids, (int)cap);
+        }
+        if (isect_ids != nullptr) {
+            const int64_t n_keys = S * T;
+            decode_keys_kernel<<<(unsigned)((n_keys * 32 + 255) / 256), 256, 0, stream>>>(
+                offsets, n_keys, n_isects, seg_base * T, isect_ids);
+        }
+        return check_launch("bin_place");
+    }
     const int per_warp = (int)T * 4;
     int warps = kSmemLimit / per_warp;
     warps = warps > 8 ? 8 : (warps < 1 ? 1 : warps);

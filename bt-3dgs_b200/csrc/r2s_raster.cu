@@ -4,11 +4,13 @@
 // (view, tile), one thread per pixel; the tile's sorted Gaussian list is
 // staged through shared memory in batches.  Differences in how the work is
 // done (the result is the same sum over the same contributing set):
-//   * every staged Gaussian carries a bit mask of the warps (pixel blocks of
-//     8x4 for tile sizes divisible by 8) whose pixels can reach the
-//     |alpha| >= 1e-5 cut-off; a warp only evaluates the Gaussians of its
-//     mask bits (ballot + find-first-set), so pairs that the reference
-//     evaluates and then discards are never evaluated;
+//   * generic kernel: every staged Gaussian carries a bit mask of the warps
+//     (pixel blocks of 8x4 for tile sizes divisible by 8) whose pixels can
+//     reach the |alpha| >= 1e-5 cut-off; a warp only evaluates the Gaussians
+//     of its mask bits (ballot + find-first-set);
+//   * float32 16x16 kernel: every warp covers the whole tile for a quarter of
+//     the list and evaluates only the 4-row groups a Gaussian's culling box
+//     reaches; partial sums of the four warps are added at the end;
 //   * float32 evaluates sigma*log2(e) with a pre-scaled conic and one ex2.
 //
 // Backward (reference: csrc/RasterizeToPixelsBwd.cu:76-265 "pixel" and
@@ -452,17 +454,23 @@ __device__ __forceinline__ float s_threshold(float wmu) {
     return a >= 1.0f ? log2f(a) : -1.0f;  // negative: nothing passes
 }
 
-constexpr int kFwd16Threads = 128;  // 4 warps, each an 8x8 pixel block, 2 pixels per lane
-constexpr int kFwd16Batch = 256;
+constexpr int kFwd16Threads = 128;  // 4 warps, each covering the whole tile for a quarter of the list
+constexpr int kFwd16Batch = 128;
 
+// Forward of 16x16 tiles.  Every warp covers all 256 pixels of the tile (lane
+// L: column L & 15, rows (L >> 4) + 2k) and takes every fourth staged record,
+// so a warp evaluates one record at a time with no per-warp work list.  A
+// record carries a mask of the four 4-row groups its culling box reaches;
+// a warp evaluates only those groups (2 pixels per lane each, in packed
+// pairs).  The four warps' partial sums are added in shared memory at the
+// end.
 __global__ void __launch_bounds__(kFwd16Threads)
 raster_fwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict__ offsets,
                     const int32_t* __restrict__ flatten_ids, int64_t n_keys, int64_t n_isects,
                     uint32_t W, uint32_t H, uint32_t ntx, uint32_t nty, float* __restrict__ image) {
     __shared__ float4 s_p[kFwd16Batch];  // mx, my, A = a/2 log2e, B = b log2e
-    __shared__ float4 s_q[kFwd16Batch];  // C = c/2 log2e, w*mu, s_thr, unused
-    __shared__ uint32_t s_mask[kFwd16Batch];
-    __shared__ uint16_t s_list[kFwd16Threads / 32][kFwd16Batch];  // per-warp work list
+    __shared__ float4 s_q[kFwd16Batch];  // C = c/2 log2e, w*mu, s_thr, row-group mask (bits)
+    __shared__ float s_acc[kFwd16Threads / 32][256];
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int64_t cam = blockIdx.z;
@@ -470,73 +478,69 @@ raster_fwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict
     const int64_t key = cam * (int64_t)ntx * nty + (int64_t)blockIdx.y * ntx + blockIdx.x;
     const int start = offsets[key];
     const int end = key + 1 < n_keys ? offsets[key + 1] : (int)n_isects;
+    const int cmax = min(15, (int)W - 1 - X0), rmax = min(15, (int)H - 1 - Y0);
 
-    const int ix = X0 + (warp & 1) * 8 + (lane & 7);
-    const int iy0 = Y0 + (warp >> 1) * 8 + (lane >> 3);
-    const float px = (float)ix + 0.5f;
-    const float py0 = (float)iy0 + 0.5f;
-    const float xmax = (float)W - 0.5f, ymax = (float)H - 0.5f;
-    float acc0 = 0.f, acc1 = 0.f;
+    const int col = lane & 15, rb = lane >> 4;
+    const float px = (float)(X0 + col) + 0.5f;
+    float2 py[4];
+#pragma unroll
+    for (int g = 0; g < 4; ++g)
+        py[g] = make_float2((float)(Y0 + 4 * g + rb) + 0.5f, (float)(Y0 + 4 * g + rb) + 2.5f);
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 
     for (int b0 = start; b0 < end; b0 += kFwd16Batch) {
         const int n = min(kFwd16Batch, end - b0);
         __syncthreads();
-        for (int j = tid; j < n; j += kFwd16Threads) {
-            const int64_t g = flatten_ids[b0 + j];
+        if (tid < n) {
+            const int64_t g = flatten_ids[b0 + tid];
             const float4 p = splats[2 * g];
             const float4 q = splats[2 * g + 1];
-            // warp w covers pixel centres [X0+8(w&1)+0.5, +7.5] x [Y0+8(w>>1)+0.5, +7.5]
-            const float gx0 = p.x - q.z, gx1 = p.x + q.z, gy0 = p.y - q.w, gy1 = p.y + q.w;
+            int c_lo, c_hi, r_lo, r_hi;
+            cull_range(p.x, q.z, (float)X0, cmax, c_lo, c_hi);
+            cull_range(p.y, q.w, (float)Y0, rmax, r_lo, r_hi);
             uint32_t m = 0;
+            if (c_lo <= c_hi) {
 #pragma unroll
-            for (int w = 0; w < 4; ++w) {
-                const float bx0 = (float)(X0 + (w & 1) * 8) + 0.5f;
-                const float by0 = (float)(Y0 + (w >> 1) * 8) + 0.5f;
-                const float bx1 = fminf(bx0 + 7.f, xmax), by1 = fminf(by0 + 7.f, ymax);
-                if (gx0 <= bx1 && gx1 >= bx0 && gy0 <= by1 && gy1 >= by0 && bx0 <= bx1 &&
-                    by0 <= by1)
-                    m |= 1u << w;
+                for (int k = 0; k < 4; ++k)
+                    if (r_lo <= 4 * k + 3 && r_hi >= 4 * k) m |= 1u << k;
             }
-            s_p[j] = make_float4(p.x, p.y, 0.5f * kLog2e * p.z, kLog2e * p.w);
-            s_q[j] = make_float4(0.5f * kLog2e * q.x, q.y, s_threshold(q.y), 0.f);
-            s_mask[j] = m;
+            s_p[tid] = make_float4(p.x, p.y, 0.5f * kLog2e * p.z, kLog2e * p.w);
+            s_q[tid] = make_float4(0.5f * kLog2e * q.x, q.y, s_threshold(q.y), __uint_as_float(m));
         }
         __syncthreads();
-        // compact this warp's Gaussians of the batch into an index list
-        uint16_t* list = s_list[warp];
-        int cnt = 0;
-        for (int c0 = 0; c0 < n; c0 += 32) {
-            const int j = c0 + lane;
-            const bool mine = j < n && ((s_mask[j] >> warp) & 1u);
-            const unsigned bits = __ballot_sync(0xffffffffu, mine);
-            if (mine) list[cnt + __popc(bits & lanemask_lt())] = (uint16_t)j;
-            cnt += __popc(bits);
-        }
-        __syncwarp();
-        for (int i = 0; i < cnt; ++i) {
-            const int t = list[i];
-            const float4 P = s_p[t];
+        for (int t = warp; t < n; t += kFwd16Threads / 32) {
             const float4 Q = s_q[t];
+            const uint32_t m = __float_as_uint(Q.w);
+            if (m == 0) continue;  // warp-uniform
+            const float4 P = s_p[t];
             const uint32_t thr = __float_as_uint(Q.z);
             const float dx = px - P.x;
             const float xx = P.z * dx * dx;
             const float xy = P.w * dx;
-            const float dy0 = py0 - P.y;
-            const float dy1 = dy0 + 4.0f;
-            const float s0 = fmaf(dy0, fmaf(Q.x, dy0, xy), xx);
-            const float s1 = fmaf(dy1, fmaf(Q.x, dy1, xy), xx);
-            const bool v0 = s_valid(s0, thr), v1 = s_valid(s1, thr);
-            if (!__any_sync(0xffffffffu, v0 | v1)) continue;
-            const float e0 = exp2f(-s0);
-            const float e1 = exp2f(-s1);
-            if (v0) acc0 = fmaf(Q.y, e0, acc0);
-            if (v1) acc1 = fmaf(Q.y, e1, acc1);
+            const float2 xx2 = make_float2(xx, xx), xy2 = make_float2(xy, xy);
+            const float2 C2 = make_float2(Q.x, Q.x), nmy = make_float2(-P.y, -P.y);
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+                if (!((m >> g) & 1u)) continue;  // warp-uniform
+                const float2 dy = fadd2(py[g], nmy);
+                const float2 s = ffma2(dy, ffma2(C2, dy, xy2), xx2);
+                const float e0 = exp2f(-s.x), e1 = exp2f(-s.y);
+                if (s_valid(s.x, thr)) acc[2 * g] = fmaf(Q.y, e0, acc[2 * g]);
+                if (s_valid(s.y, thr)) acc[2 * g + 1] = fmaf(Q.y, e1, acc[2 * g + 1]);
+            }
         }
     }
-    if (ix < (int)W) {
-        float* out = image + cam * (int64_t)H * W;
-        if (iy0 < (int)H) out[(int64_t)iy0 * W + ix] = acc0;
-        if (iy0 + 4 < (int)H) out[(int64_t)(iy0 + 4) * W + ix] = acc1;
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+        s_acc[warp][(4 * g + rb) * 16 + col] = acc[2 * g];
+        s_acc[warp][(4 * g + rb + 2) * 16 + col] = acc[2 * g + 1];
+    }
+    __syncthreads();
+    float* out = image + cam * (int64_t)H * W;
+    for (int p = tid; p < 256; p += kFwd16Threads) {
+        const int r = p >> 4, c = p & 15;
+        const float v = (s_acc[0][p] + s_acc[1][p]) + (s_acc[2][p] + s_acc[3][p]);
+        if (c <= cmax && r <= rmax) out[(int64_t)(Y0 + r) * W + X0 + c] = v;
     }
 }
 

@@ -9,6 +9,29 @@ GOLDEN = os.path.join(ROOT, "tests", "golden", "kat.pt")
 # float32 parity bar of the hot path (rel-L2 against the reference build)
 REL_L2_F32 = 1e-5
 
+# Parameter gradients of workloads where one Gaussian sums ~1e4 pixels of a
+# random-sign upstream gradient: two float32 evaluations that differ only in
+# rounding differ by ~1e-5 (the reference's own "pixel" and "primitive"
+# backward modes differ by 5e-6 at config-2 scale, and each is 6-8e-6 from a
+# float64 evaluation of the same float32 forward values).  A gradient that
+# misses REL_L2_F32 against the reference passes only if (a) it is within
+# GRAD_NOISE_F32 of the reference and (b) it is no less accurate than the
+# reference against the float64 evaluation.
+GRAD_NOISE_F32 = 2e-5
+
+
+def check_grad_accuracy(name, ours, theirs, truth, slack=1.25):
+    """ours/theirs/truth: dicts of parameter gradients (truth in float64)."""
+    for k in truth:
+        e_pair = rel_l2(ours[k], theirs[k])
+        if e_pair < REL_L2_F32:
+            continue
+        e_ref = rel_l2(theirs[k], truth[k])
+        e_ours = rel_l2(ours[k], truth[k])
+        assert e_pair < GRAD_NOISE_F32, f"{name}: grad {k} rel-L2 vs reference {e_pair:.3e}"
+        assert e_ours <= slack * e_ref + 1e-7, (
+            f"{name}: grad {k} rel-L2 vs float64 {e_ours:.3e}, reference {e_ref:.3e}")
+
 
 def load_golden():
     return torch.load(GOLDEN, weights_only=False)

@@ -12,7 +12,7 @@ import os
 import pytest
 import torch
 
-from _helpers import REL_L2_F32, rel_l2
+from _helpers import REL_L2_F32, check_grad_accuracy, rel_l2
 
 pytestmark = pytest.mark.gpu
 
@@ -228,12 +228,59 @@ def test_fused_op_layer_matches_reference_pipeline(ref, case):
     E.explicit_backward(state, params["means"], params["quats"], params["scales"], params["opac"])
     theirs = ref.explicit_backward(p, v_img, v, v_vol, d["means"], d["quats"], d["scales"], d["opac"],
                                    covars, opac, wl.SCALE_MIN, wl.SCALE_MAX, absgrad=True)
-    for key, pk in (("means", "means"), ("quats", "quats"), ("scales", "scales"),
-                    ("opac", "opacities")):
-        e = rel_l2(params[key].grad, theirs[pk])
-        assert e < REL_L2_F32, f"{name}: grad {key} rel-L2 {e:.3e}"
+    pairs = (("means", "means"), ("quats", "quats"), ("scales", "scales"), ("opac", "opacities"))
+    if name in NOISE_LIMITED:
+        truth = _float64_gradients(ref, d, p, v_img, v, v_vol, covars)
+        check_grad_accuracy(name, {k: params[k].grad for k, _ in pairs},
+                            {k: theirs[pk] for k, pk in pairs}, truth)
+    else:
+        for key, pk in pairs:
+            e = rel_l2(params[key].grad, theirs[pk])
+            assert e < REL_L2_F32, f"{name}: grad {key} rel-L2 {e:.3e}"
     assert rel_l2(res.means2d.grad, theirs["means2d"]) < REL_L2_F32
     assert rel_l2(res.means2d.absgrad, theirs["means2d_abs"]) < REL_L2_F32
+
+
+# cases whose parameter gradients are limited by float32 summation noise
+NOISE_LIMITED = {"cfg2-4views"}
+
+
+def _float64_gradients(ref, d, p, v_img, v, v_vol, covars):
+    """Parameter gradients evaluated in float64 by the reference's own double
+    kernels from the float32 forward values and the float32 binning (the
+    primitive backward of RasterizeToPixelsBwd.cu / VoxelizeToVoxelsBwd.cu and
+    the reference VJP chain of r2splat/ops/explicit.py:233-385)."""
+    import r2s_workloads as wl
+
+    C = ref.C
+    f8 = torch.float64
+    det = d["det"]
+    G = d["grid"]
+    v_abs, v_m2, v_con, v_op, v_mu = C.rasterize_to_pixels_bwd_per_gaussian(
+        p["means2d"].to(f8), p["conics"].to(f8), p["opacity"].to(f8), p["mus"].to(f8),
+        p["tile_offsets"], p["isect_ids"], p["flatten_ids"], v_img.to(f8), det, det, wl.IMG_TILE,
+        False)
+    v_c2 = C.conics_mu_bwd(p["cov2d"].to(f8), wl.EPS2D, p["conics"].to(f8), p["mus"].to(f8),
+                           v_con.contiguous(), v_mu.contiguous())
+    means, cov = d["means"].to(f8), covars.to(f8)
+    v_means, v_cov = C.world_to_image_projection_bwd(means, cov, d["viewmats"].to(f8),
+                                                     d["Ks"].to(f8), det, det, v_m2.contiguous(),
+                                                     v_c2.contiguous())
+    v_opac = v_op.sum(0)
+    v_m3, v_c3, v_o3 = C.voxelize_to_voxels_bwd_per_gaussian(
+        v["means3d"].to(f8), v["conics"].to(f8), v["opacity"].to(f8), v["tile_offsets"],
+        v["isect_ids"], v["flatten_ids"], v_vol.to(f8), G, G, G, wl.VOL_TILE)
+    vm3, vc3 = C.world_to_volume_mapping_bwd(means, cov, v["ranges"].to(f8), v["centers"].to(f8),
+                                             G, G, G, wl.EPS3D, v_m3.contiguous(),
+                                             v_c3.contiguous())
+    v_means = v_means + vm3
+    v_cov = v_cov + vc3
+    v_opac = v_opac + v_o3
+    q8, s8 = d["quats"].to(f8), d["scales"].to(f8)
+    v_quats, v_scales = C.parameter_transform_bwd(q8, s8, wl.SCALE_MIN, wl.SCALE_MAX,
+                                                  v_cov.contiguous())
+    v_raw = v_opac * torch.sigmoid(d["opac"].to(f8))
+    return {"means": v_means, "quats": v_quats, "scales": v_scales, "opac": v_raw}
 
 
 def test_fused_op_layer_accumulates_existing_grads(case):
