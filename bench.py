@@ -378,21 +378,31 @@ def kernel_time(fn, reps=3):
     return sum(ts) / len(ts)
 
 
-def dominant_kernel_roofline(proj: OursProjection, hbm_peak, peak_kind):
+# DRAM traffic of one raster_bwd16_kernel launch per view, from the ncu
+# capture of `bench.py --views 8` (dram__bytes_read.sum + dram__bytes_write.sum
+# = 439.3 MB + 101.7 MB for 8 views; traffic grows with the views).
+BWD16_DRAM_BYTES_PER_VIEW = (439.278336e6 + 101.730048e6) / 8
+
+
+def dominant_kernel_roofline(proj: OursProjection, hbm_peak, peak_kind, clock_mhz):
     """Raster backward (the largest share of the step) on its own launch.
 
-    Algorithmic bytes per launch (counted from the formulas): per
-    intersection record 4 B flatten id + 32 B splat record + 32 B statistics
-    reduction, plus the upstream image (4 B per pixel per view).  Pairs for
-    the FP32 view: n_isects * 256, 30 FP32 flops + 1 ex2 per pair."""
+    Algorithmic (compulsory) bytes per launch: the flatten ids (4 B per
+    intersection record), every (view, Gaussian) splat record once (32 B) and
+    its statistics once (32 B), the upstream image (4 B per pixel) and the
+    tile offsets (4 B per tile).  The kernel is bound by the SM pipes, not by
+    HBM: every pixel of every record's tile needs one exponential (the
+    reference evaluates all tile_size^2 pixels per record), so `sfu` reports
+    pairs/s against 16 ex2 per clock per SM at the sampled SM clock, and
+    `fp32` the same pairs at 30 FP32 flops each against the FP32 peak."""
     from r2splat.cuda import _wrapper as W
 
     E = proj.E
     m, q, s, o = proj.params
     st = E.prepare_explicit_gaussians(q, s, o, scale_min=wl.SCALE_MIN, scale_max=wl.SCALE_MAX)
-    res = E.explicit_rasterize(st, m, proj.vm, proj.K, img_w=proj.det, img_h=proj.det,
-                               tile_size=wl.IMG_TILE, eps2d=wl.EPS2D, radius_clip=wl.RADIUS_CLIP,
-                               absgrad=True)
+    E.explicit_rasterize(st, m, proj.vm, proj.K, img_w=proj.det, img_h=proj.det,
+                         tile_size=wl.IMG_TILE, eps2d=wl.EPS2D, radius_clip=wl.RADIUS_CLIP,
+                         absgrad=True)
     pb = st.projection.buffers
     C, N = pb.means2d.shape[:2]
     ntx, nty = pb.tile_offsets.size(2), pb.tile_offsets.size(1)
@@ -404,26 +414,32 @@ def dominant_kernel_roofline(proj: OursProjection, hbm_peak, peak_kind):
 
     launch()
     ms = kernel_time(launch)
-    alg_bytes = n_isects * (4 + 32 + 32) + C * proj.det * proj.det * 4
+    alg_bytes = (n_isects * 4 + C * N * (32 + 32) + C * proj.det * proj.det * 4
+                 + C * ntx * nty * 4)
     achieved = alg_bytes / (ms * 1e-3) / 1e9
-    pairs = n_isects * 256
-    flops = pairs * 30
-    fp32_peak = 148 * 128 * 2 * 1.965e9 / 1e12
-    tflops = flops / (ms * 1e-3) / 1e12
+    pairs = n_isects * wl.IMG_TILE * wl.IMG_TILE
+    mhz = clock_mhz or 1965.0
+    sfu_peak = 148 * 16 * mhz * 1e6
+    fp32_peak = 148 * 128 * 2 * mhz * 1e6 / 1e12
+    tflops = pairs * 30 / (ms * 1e-3) / 1e12
     return {
-        "kernel": "raster_bwd_kernel<float,splats>",
+        "kernel": "raster_bwd16_kernel<true>",
         "bound": "hbm",
         "achieved": round(achieved, 1),
         "peak": hbm_peak,
         "unit": "GB/s",
         "frac": round(achieved / hbm_peak, 4),
         "peak_source": peak_kind,
-        "traffic": None,
+        "traffic": round(BWD16_DRAM_BYTES_PER_VIEW * C),
+        "alg_bytes": alg_bytes,
+        "traffic_source": "ncu capture at 8 views, scaled by views",
         "ms_per_launch": round(ms, 3),
         "n_isects": n_isects,
+        "sfu": {"achieved_ex2_per_s": round(pairs / (ms * 1e-3), -6),
+                "peak_ex2_per_s": round(sfu_peak, -6), "frac": round(pairs / (ms * 1e-3) / sfu_peak, 4),
+                "pairs": pairs, "clock_mhz": mhz},
         "fp32": {"achieved_tflops": round(tflops, 2), "peak_tflops_nominal": round(fp32_peak, 1),
-                 "frac": round(tflops / fp32_peak, 4),
-                 "flops_per_pair": 30, "pairs": pairs},
+                 "frac": round(tflops / fp32_peak, 4), "flops_per_pair": 30},
     }
 
 
@@ -521,19 +537,24 @@ def main():
         return
 
     proj = OursProjection(cfg, world, rank, dev)
-    vox = OursVoxel(cfg, world, rank, dev, proj.params)
     with ClockSampler(local) as clk:
         ms = time_steps(proj.step, args.steps, args.warmup, world, flush)
-        vms = time_steps(vox.step, args.steps, args.warmup, world, flush)
         e2e_ms = time_e2e(proj.step_e2e, args.steps, max(1, args.warmup // 2), world, flush)
+        roof = dominant_kernel_roofline(proj, hbm_peak, peak_kind, clk.summary()["sm_mhz"]) \
+            if rank == 0 else None
+        vox = OursVoxel(cfg, world, rank, dev, proj.params)
+        torch.cuda.empty_cache()
+        vms = time_steps(vox.step, args.steps, args.warmup, world, flush)
     value = world * cfg.n_gaussians * cfg.n_views / (ms * 1e-3)
     e2e_value = world * cfg.n_gaussians * cfg.n_views / (e2e_ms * 1e-3)
     h2d, d2h = proj.bytes_e2e()
-    roof = dominant_kernel_roofline(proj, hbm_peak, peak_kind) if rank == 0 else None
     barrier(world)
-    # launches of our kernels per projection step (prepare 1, project 1,
-    # binning 4, rasterizer 1 + backward 2 statistics/finalize) and per voxel step
-    gpu_launches = args.steps * (1 + 1 + 4 + 1 + 2) + args.steps * (1 + 1 + 4 + 1 + 1 + 1)
+    # our kernels per timed step: projection = prepare, project_splats, binning
+    # (count, column scan, scan, place), raster forward, raster backward,
+    # explicit backward; voxel = prepare, map, binning (4), voxel forward,
+    # voxel backward, explicit backward
+    gpu_launches = args.steps * 9
+    vox_launches = args.steps * 9
     if rank != 0:
         return
     line = {
@@ -547,7 +568,8 @@ def main():
                    "parallelism": f"views x{world} (weak) + grad all-reduce; voxel z-slabs x{world}",
                    "l2": "256MiB flush between steps"},
         "voxelize": {"value": round(cfg.grid ** 3 / (vms * 1e-3) / 1e6, 2), "unit": "Mvoxels/s",
-                     "ms_per_step": round(vms, 3), "scaling": "strong (z-slabs)"},
+                     "ms_per_step": round(vms, 3), "scaling": "strong (z-slabs)",
+                     "gpu_launches": vox_launches},
         "e2e": {"value": round(e2e_value, 1), "unit": "Gaussian*views/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": round(e2e_ms, 3)},
