@@ -41,6 +41,7 @@ for _p in (os.path.join(ROOT, "bt-3dgs_b200"), ROOT):
 
 import torch  # noqa: E402
 
+import r2s_shard as shard  # noqa: E402
 import r2s_workloads as wl  # noqa: E402
 
 L2_FLUSH_BYTES = 256 << 20
@@ -159,14 +160,14 @@ class OursProjection:
         m, q, s, o = wl.make_gaussians(cfg)
         self.host = [t.pin_memory() for t in (m, q, s, o)]
         self.params = [t.to(dev) for t in (m, q, s, o)]
-        vm, K = wl.make_cameras(cfg.n_views, cfg.detector, first=rank * cfg.n_views,
-                                count=cfg.n_views, total=cfg.n_views * world)
+        first, count, total = shard.view_shard(cfg.n_views, rank, world)
+        vm, K = wl.make_cameras(count, cfg.detector, first=first, count=count, total=total)
         self.vm, self.K = vm.to(dev), K.to(dev)
         self.host_cams = (vm.pin_memory(), K.pin_memory())
         g = torch.Generator(device=dev).manual_seed(100 + rank)
         self.v_img = torch.randn((cfg.n_views, self.det, self.det), generator=g, device=dev)
         self.host_vimg = self.v_img.cpu().pin_memory()
-        self.flat = None
+        self.allreduce = shard.GradientAllReduce()
 
     def step(self, params=None, vm=None, K=None, v_img=None):
         E = self.E
@@ -185,25 +186,8 @@ class OursProjection:
         res.image.grad = v_img
         E.explicit_backward(st, *params)
         if self.world > 1:
-            self._allreduce(params)
+            self.allreduce([p.grad for p in params])
         return res
-
-    def _allreduce(self, params):
-        import torch.distributed as dist
-
-        grads = [p.grad for p in params]
-        n = sum(g.numel() for g in grads)
-        if self.flat is None or self.flat.numel() != n:
-            self.flat = torch.empty(n, device=grads[0].device)
-        off = 0
-        for g in grads:
-            self.flat[off:off + g.numel()].copy_(g.reshape(-1))
-            off += g.numel()
-        dist.all_reduce(self.flat)
-        off = 0
-        for g in grads:
-            g.copy_(self.flat[off:off + g.numel()].view_as(g))
-            off += g.numel()
 
     def step_e2e(self):
         """Same step with host-resident inputs and outputs: H2D of the raw
@@ -233,17 +217,14 @@ class OursVoxel:
         self.world = world
         self.G = cfg.grid
         self.nt = (self.G + wl.VOL_TILE - 1) // wl.VOL_TILE
-        per = (self.nt + world - 1) // world
-        self.l0 = min(self.nt, rank * per)
-        self.l1 = min(self.nt, self.l0 + per)
+        self.l0, self.l1 = shard.layer_range(self.nt, rank, world)
         self.params = params
         rng, ctr = wl.unit_cube_box()
         self.rng, self.ctr = rng.to(dev), ctr.to(dev)
-        z0 = self.l0 * wl.VOL_TILE
-        z1 = min(self.l1 * wl.VOL_TILE, self.G)
+        z0, z1 = shard.slab_rows(self.l0, self.l1, wl.VOL_TILE, self.G)
         g = torch.Generator(device=dev).manual_seed(200 + rank)
-        self.v_vol = torch.randn((max(z1 - z0, 0), self.G, self.G), generator=g, device=dev)
-        self.flat = None
+        self.v_vol = torch.randn((z1 - z0, self.G, self.G), generator=g, device=dev)
+        self.allreduce = shard.GradientAllReduce()
 
     def step(self):
         W = self.W
@@ -265,13 +246,7 @@ class OursVoxel:
                                       wl.EPS2D, None, None, None, self.rng, self.ctr, G, G, G,
                                       wl.EPS3D, stats, False, outs)
             if self.world > 1:
-                import torch.distributed as dist
-
-                n = sum(t.numel() for t in outs)
-                if self.flat is None or self.flat.numel() != n:
-                    self.flat = torch.empty(n, device=m.device)
-                torch.cat([t.reshape(-1) for t in outs], out=self.flat)
-                dist.all_reduce(self.flat)
+                self.allreduce(outs)
         return vol
 
 

@@ -1,0 +1,175 @@
+"""Multi-process sharding of the path on CPU (gloo, world size 2): views per
+rank with a gradient all-reduce equal the single-process gradient over all
+views; the z-slabs of the voxel grid tile the full volume and their gradient
+sum equals the full gradient.  The per-rank compute is the CPU oracle; the
+sharding and the collective are the ones bench.py runs over NCCL."""
+import os
+import socket
+import sys
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from _helpers import ROOT
+
+WORLD = 2
+VIEWS_PER_RANK = 2
+DET = 32
+GRID = 32
+TILE3 = 8
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _setup_paths():
+    for p in (os.path.join(ROOT, "bt-3dgs_b200"), ROOT):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+
+
+def _params():
+    import r2s_workloads as wl
+
+    m, q, s, o = wl.make_gaussians(wl.CONFIGS[0], n=48)
+    return [t.double().requires_grad_(True) for t in (m, q, s, o)]
+
+
+def _projection_grads(params, first, count, total):
+    import r2s_workloads as wl
+    from oracle import r2s_oracle as O
+
+    vm, K = wl.make_cameras(count, DET, first=first, count=count, total=total)
+    img, *_ = O.projection_forward(*params, vm.double(), K.double(), width=DET, height=DET,
+                                   tile=wl.IMG_TILE, eps2d=wl.EPS2D, clip=wl.RADIUS_CLIP,
+                                   smin=wl.SCALE_MIN, smax=wl.SCALE_MAX)
+    g = torch.Generator().manual_seed(5)
+    v = torch.randn((total, DET, DET), generator=g, dtype=torch.float64)[first:first + count]
+    return torch.autograd.grad((img * v).sum(), params)
+
+
+def _voxel_slab(params, l0, l1):
+    import r2s_workloads as wl
+    from oracle import r2s_oracle as O
+
+    m, q, s, o = params
+    cov, _ = O.parameter_transform(q, s, wl.SCALE_MIN, wl.SCALE_MAX)
+    opac = O.softplus(o)
+    rng, ctr = wl.unit_cube_box()
+    m3, c3, r3 = O.volume_mapping(m, cov, rng.double(), ctr.double(), GRID, GRID, GRID, wl.EPS3D,
+                                  wl.RADIUS_CLIP)
+    nt = GRID // TILE3
+    rects, valid, _ = O.brick_rects_3d(m3.detach().numpy(), r3.numpy(), TILE3, nt, nt, nt)
+    return O.voxelize_slab(m3, c3, opac, rects, valid, GRID, GRID, GRID, TILE3, l0, l1)
+
+
+def _worker(rank, port, out_path):
+    _setup_paths()
+    import torch.distributed as dist
+
+    import r2s_shard as shard
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=WORLD)
+    try:
+        params = _params()
+        first, count, total = shard.view_shard(VIEWS_PER_RANK, rank, WORLD)
+        grads = [g.clone() for g in _projection_grads(params, first, count, total)]
+        shard.GradientAllReduce()(grads)
+
+        l0, l1 = shard.layer_range(GRID // TILE3, rank, WORLD)
+        slab = _voxel_slab(params, l0, l1)
+        g = torch.Generator().manual_seed(9)
+        v_full = torch.randn((GRID, GRID, GRID), generator=g, dtype=torch.float64)
+        z0, z1 = shard.slab_rows(l0, l1, TILE3, GRID)
+        vgrads = [t.clone() for t in torch.autograd.grad((slab * v_full[z0:z1]).sum(), params)]
+        shard.GradientAllReduce()(vgrads)
+        sizes = [torch.zeros(1, dtype=torch.int64) for _ in range(WORLD)]
+        dist.all_gather(sizes, torch.tensor([slab.shape[0]]))
+        slabs = [torch.zeros((int(n), GRID, GRID), dtype=torch.float64) for n in sizes]
+        dist.all_gather(slabs, slab.detach().contiguous())
+        if rank == 0:
+            torch.save({"grads": grads, "vgrads": vgrads, "volume": torch.cat(slabs)}, out_path)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.fixture(scope="module")
+def sharded(tmp_path_factory):
+    out = str(tmp_path_factory.mktemp("multirank") / "rank0.pt")
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=_worker, args=(r, _free_port_once(), out)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    return torch.load(out)
+
+
+_PORT = []
+
+
+def _free_port_once():
+    if not _PORT:
+        _PORT.append(_free_port())
+    return _PORT[0]
+
+
+def test_layer_ranges_tile_the_grid():
+    _setup_paths()
+    import r2s_shard as shard
+
+    for n_layers in (1, 4, 7, 32):
+        for world in (1, 2, 3, 8):
+            rows = []
+            for r in range(world):
+                l0, l1 = shard.layer_range(n_layers, r, world)
+                assert 0 <= l0 <= l1 <= n_layers
+                rows.extend(range(l0, l1))
+            assert rows == list(range(n_layers))
+    assert shard.slab_rows(3, 4, 8, 30) == (24, 30)
+    assert shard.slab_rows(4, 4, 8, 30) == (32, 32)
+    with pytest.raises(ValueError):
+        shard.layer_range(4, 2, 2)
+
+
+def test_view_shards_cover_the_orbit():
+    _setup_paths()
+    import r2s_shard as shard
+
+    seen = []
+    for r in range(4):
+        first, count, total = shard.view_shard(75, r, 4)
+        assert total == 300 and count == 75
+        seen.extend(range(first, first + count))
+    assert seen == list(range(300))
+
+
+def test_projection_gradient_allreduce_equals_single_process(sharded):
+    _setup_paths()
+    params = _params()
+    full = _projection_grads(params, 0, VIEWS_PER_RANK * WORLD, VIEWS_PER_RANK * WORLD)
+    for a, b in zip(sharded["grads"], full):
+        torch.testing.assert_close(a, b, rtol=1e-10, atol=1e-12)
+
+
+def test_voxel_slabs_equal_the_full_volume_and_gradient(sharded):
+    _setup_paths()
+    params = _params()
+    nt = GRID // TILE3
+    full = _voxel_slab(params, 0, nt)
+    torch.testing.assert_close(sharded["volume"], full.detach(), rtol=1e-12, atol=1e-14)
+    g = torch.Generator().manual_seed(9)
+    v_full = torch.randn((GRID, GRID, GRID), generator=g, dtype=torch.float64)
+    ref = torch.autograd.grad((full * v_full).sum(), params)
+    for a, b in zip(sharded["vgrads"], ref):
+        torch.testing.assert_close(a, b, rtol=1e-10, atol=1e-12)
