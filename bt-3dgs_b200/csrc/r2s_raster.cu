@@ -544,17 +544,21 @@ raster_fwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict
     }
 }
 
-constexpr int kBwd16Threads = 256;  // one (view, tile) per CTA, one Gaussian per thread
+constexpr int kBwd16Threads = 256;  // one (view, tile) per CTA, one Gaussian record per thread
+constexpr int kBwd16Batch = 1024;   // records staged and sorted per batch (32 groups of 32)
 
 // Backward statistics of 16x16 tiles, one Gaussian record per thread.
 //
-// The tile's upstream gradient sits in shared memory and every thread walks
-// the 16 columns of the rows its record can reach (rows outside the record's
-// culling box, and pixels failing the alpha cut-off, contribute nothing); a
-// warp executes the union of its lanes' row ranges.  Per pixel: sigma from the
-// column offset dx (exact per column) and the row terms B dy, C dy^2, one ex2,
-// and packed updates of the per-column sums Col_c = sum_rows v e and the row
-// sums sum_c v e, sum_c v e dx.  The moments follow without cancellation:
+// The tile's upstream gradient sits in shared memory.  The CTA stages the
+// tile's list in batches of 1024 records and orders each batch with a
+// counting sort on the record's row range (first row, last row of the
+// culling box), so that each group of 32 lanes walks similar rows: a warp
+// executes the union of its lanes' rows.  Warp w takes the sorted groups
+// w, w+8, w+16, w+24, which spreads short and long row ranges evenly over the
+// warps.  Per pixel: sigma from the column offset dx (exact per column) and
+// the row terms B dy, C dy^2, one ex2, and packed updates of the per-column
+// sums Col_c = sum_rows v e and the row sums sum_c v e, sum_c v e dx.  The
+// moments follow without cancellation:
 //   S0 = sum_c Col_c, Sx = sum_c Col_c dx_c, Sxx = sum_c Col_c dx_c^2,
 //   Sy = sum_r dy_r R0_r, Syy = sum_r dy_r^2 R0_r, Sxy = sum_r dy_r R1_r.
 // No cross-lane reduction is needed; each record adds its eight values with
@@ -566,8 +570,15 @@ raster_bwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict
                     const float* __restrict__ v_image, uint32_t W, uint32_t H, uint32_t ntx,
                     uint32_t nty, float* __restrict__ stats) {
     __shared__ __align__(16) float s_v[256];
+    __shared__ float4 s_p[kBwd16Batch];
+    __shared__ float4 s_q[kBwd16Batch];
+    __shared__ int32_t s_g[kBwd16Batch];
+    __shared__ uint8_t s_rows[kBwd16Batch];  // first row | last row << 4
+    __shared__ uint16_t s_perm[kBwd16Batch];
+    __shared__ int32_t s_cnt[257];
+    __shared__ int32_t s_wsum[kBwd16Threads / 32];
 
-    const int tid = threadIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int64_t cam = blockIdx.z;
     const int X0 = blockIdx.x * 16, Y0 = blockIdx.y * 16;
     const int64_t key = cam * (int64_t)ntx * nty + (int64_t)blockIdx.y * ntx + blockIdx.x;
@@ -580,95 +591,140 @@ raster_bwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict
         const int r = tid >> 4, c = tid & 15;
         s_v[tid] = (c <= cmax && r <= rmax) ? vc[(int64_t)(Y0 + r) * W + X0 + c] : 0.f;
     }
-    __syncthreads();
     const float X0f = (float)X0, Y0f = (float)Y0;
 
-    // the trip count is the same for every thread: warp votes stay convergent
-    for (int base = start; base < end; base += kBwd16Threads) {
-        const int i = base + tid;
-        int64_t g = 0;
-        float4 p = make_float4(0.f, 0.f, 0.f, 0.f), q = p;
-        int c_lo = 1, c_hi = 0, r_lo = 1, r_hi = 0;
-        if (i < end) {
-            g = flatten_ids[i];
-            p = splats[2 * g];
-            q = splats[2 * g + 1];
-            cull_range(p.x, q.z, X0f, cmax, c_lo, c_hi);
-            cull_range(p.y, q.w, Y0f, rmax, r_lo, r_hi);
-        }
-        const bool live = c_lo <= c_hi && r_lo <= r_hi;
-        if (!live) r_lo = 16, r_hi = -1;
-        const int row0 = __reduce_min_sync(0xffffffffu, r_lo);
-        const int row1 = __reduce_max_sync(0xffffffffu, r_hi);
-        if (row0 > row1) continue;
-
-        const float A = 0.5f * kLog2e * p.z, B = kLog2e * p.w, Cc = 0.5f * kLog2e * q.x;
-        const uint32_t thr = __float_as_uint(s_threshold(q.y));
-        const float2 A2 = make_float2(A, A);
-        const float2 a2 = make_float2(p.z, p.z), b2 = make_float2(p.w, p.w);
-        float2 dx[8], col[8];
+    for (int base = start; base < end; base += kBwd16Batch) {
+        // stage the batch; bucket 256 holds records that reach no pixel
+        s_cnt[tid] = 0;
+        if (tid == 0) s_cnt[256] = 0;
+        __syncthreads();
+        constexpr int kPer = kBwd16Batch / kBwd16Threads;
+        int bucket[kPer], rank[kPer];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            dx[j] = make_float2((X0f + (2 * j + 0.5f)) - p.x, (X0f + (2 * j + 1.5f)) - p.x);
-            col[j] = make_float2(0.f, 0.f);
-        }
-        float Sy = 0.f, Syy = 0.f, Sxy = 0.f, Ax = 0.f, Ay = 0.f;
-        for (int r = row0; r <= row1; ++r) {
-            const bool rin = r >= r_lo && r <= r_hi;
-            const float dy = (Y0f + ((float)r + 0.5f)) - p.y;
-            const float by = B * dy, cyy = Cc * dy * dy;
-            const float2 by2 = make_float2(by, by), cyy2 = make_float2(cyy, cyy);
-            const float bdy = p.w * dy, cdy = q.x * dy;
-            const float2 bdy2 = make_float2(bdy, bdy), cdy2 = make_float2(cdy, cdy);
-            const float4* vr = reinterpret_cast<const float4*>(s_v + r * 16);
-            float2 r0 = make_float2(0.f, 0.f), r1 = r0;
-#pragma unroll
-            for (int j4 = 0; j4 < 4; ++j4) {
-                const float4 v4 = vr[j4];
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int j = 2 * j4 + h;
-                    const float2 v2 = h ? make_float2(v4.z, v4.w) : make_float2(v4.x, v4.y);
-                    const float2 t = ffma2(A2, dx[j], by2);
-                    const float2 s = ffma2(dx[j], t, cyy2);
-                    float e0 = exp2f(-s.x), e1 = exp2f(-s.y);
-                    e0 = (rin && s_valid(s.x, thr)) ? e0 : 0.f;
-                    e1 = (rin && s_valid(s.y, thr)) ? e1 : 0.f;
-                    const float2 ve = fmul2(v2, make_float2(e0, e1));
-                    col[j] = fadd2(col[j], ve);
-                    r0 = fadd2(r0, ve);
-                    r1 = ffma2(ve, dx[j], r1);
-                    if constexpr (WITH_ABS) {
-                        const float2 qx = ffma2(a2, dx[j], bdy2);  // a dx + b dy
-                        const float2 qy = ffma2(b2, dx[j], cdy2);  // b dx + c dy
-                        Ax = fmaf(fabsf(ve.x), fabsf(qx.x), Ax);
-                        Ax = fmaf(fabsf(ve.y), fabsf(qx.y), Ax);
-                        Ay = fmaf(fabsf(ve.x), fabsf(qy.x), Ay);
-                        Ay = fmaf(fabsf(ve.y), fabsf(qy.y), Ay);
-                    }
+        for (int k = 0; k < kPer; ++k) {
+            const int idx = k * kBwd16Threads + tid;
+            const int i = base + idx;
+            int32_t g = 0;
+            float4 p = make_float4(0.f, 0.f, 0.f, 0.f), q = p;
+            int rows = 0x0f;  // empty: first row 15 > last row 0
+            bucket[k] = 256;
+            if (i < end) {
+                g = flatten_ids[i];
+                p = splats[2 * (int64_t)g];
+                q = splats[2 * (int64_t)g + 1];
+                int c_lo, c_hi, r_lo, r_hi;
+                cull_range(p.x, q.z, X0f, cmax, c_lo, c_hi);
+                cull_range(p.y, q.w, Y0f, rmax, r_lo, r_hi);
+                if (c_lo <= c_hi && r_lo <= r_hi) {
+                    bucket[k] = r_lo * 16 + r_hi;
+                    rows = r_lo | (r_hi << 4);
                 }
             }
-            const float R0 = r0.x + r0.y, R1 = r1.x + r1.y;
-            Sy = fmaf(dy, R0, Sy);
-            Syy = fmaf(dy * dy, R0, Syy);
-            Sxy = fmaf(dy, R1, Sxy);
+            s_g[idx] = g;
+            s_p[idx] = p;
+            s_q[idx] = q;
+            s_rows[idx] = (uint8_t)rows;
+            rank[k] = atomicAdd(&s_cnt[bucket[k]], 1);
         }
-        if (!live) continue;
-        float S0 = 0.f, Sx = 0.f, Sxx = 0.f;
+        __syncthreads();
+        {
+            const int c = s_cnt[tid];
+            const int incl = warp_inclusive_scan(c);
+            if (lane == 31) s_wsum[warp] = incl;
+            __syncthreads();
+            int wbase = 0;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            S0 += col[j].x + col[j].y;
-            const float2 cx = fmul2(col[j], dx[j]);
-            Sx += cx.x + cx.y;
-            Sxx = fmaf(cx.x, dx[j].x, Sxx);
-            Sxx = fmaf(cx.y, dx[j].y, Sxx);
+            for (int w = 0; w < kBwd16Threads / 32; ++w) wbase += w < warp ? s_wsum[w] : 0;
+            s_cnt[tid] = wbase + incl - c;
+            if (tid == kBwd16Threads - 1) s_cnt[256] = wbase + incl;  // after every live record
         }
-        float* st = stats + g * 8;
-        red_add_v4(st, S0, Sx, Sy, Sxx);
-        if constexpr (WITH_ABS)
-            red_add_v4(st + 4, Sxy, Syy, Ax, Ay);
-        else
-            red_add_v2(st + 4, Sxy, Syy);
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < kPer; ++k)
+            s_perm[s_cnt[bucket[k]] + rank[k]] = (uint16_t)(k * kBwd16Threads + tid);
+        __syncthreads();
+        const int n_groups = (min(kBwd16Batch, end - base) + 31) >> 5;
+
+        for (int grp = warp; grp < n_groups; grp += kBwd16Threads / 32) {
+            const int idx = s_perm[grp * 32 + lane];
+            int r_lo = s_rows[idx] & 15, r_hi = s_rows[idx] >> 4;
+            const bool live = r_lo <= r_hi;
+            if (!live) r_lo = 16, r_hi = -1;
+            const int row0 = __reduce_min_sync(0xffffffffu, r_lo);
+            const int row1 = __reduce_max_sync(0xffffffffu, r_hi);
+            if (row0 > row1) continue;  // warp-uniform
+            const int64_t g = s_g[idx];
+            const float4 p = s_p[idx], q = s_q[idx];
+
+            const float A = 0.5f * kLog2e * p.z, B = kLog2e * p.w, Cc = 0.5f * kLog2e * q.x;
+            const uint32_t thr = __float_as_uint(s_threshold(q.y));
+            const float2 A2 = make_float2(A, A);
+            const float2 a2 = make_float2(p.z, p.z), b2 = make_float2(p.w, p.w);
+            float2 dx[8], col[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                dx[j] = make_float2((X0f + (2 * j + 0.5f)) - p.x, (X0f + (2 * j + 1.5f)) - p.x);
+                col[j] = make_float2(0.f, 0.f);
+            }
+            float Sy = 0.f, Syy = 0.f, Sxy = 0.f, Ax = 0.f, Ay = 0.f;
+            for (int r = row0; r <= row1; ++r) {
+                const bool rin = r >= r_lo && r <= r_hi;
+                const float dy = (Y0f + ((float)r + 0.5f)) - p.y;
+                const float by = B * dy, cyy = Cc * dy * dy;
+                const float2 by2 = make_float2(by, by), cyy2 = make_float2(cyy, cyy);
+                const float bdy = p.w * dy, cdy = q.x * dy;
+                const float2 bdy2 = make_float2(bdy, bdy), cdy2 = make_float2(cdy, cdy);
+                const float4* vr = reinterpret_cast<const float4*>(s_v + r * 16);
+                float2 r0 = make_float2(0.f, 0.f), r1 = r0;
+#pragma unroll
+                for (int j4 = 0; j4 < 4; ++j4) {
+                    const float4 v4 = vr[j4];
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const int j = 2 * j4 + h;
+                        const float2 v2 = h ? make_float2(v4.z, v4.w) : make_float2(v4.x, v4.y);
+                        const float2 t = ffma2(A2, dx[j], by2);
+                        const float2 s = ffma2(dx[j], t, cyy2);
+                        float e0 = exp2f(-s.x), e1 = exp2f(-s.y);
+                        e0 = (rin && s_valid(s.x, thr)) ? e0 : 0.f;
+                        e1 = (rin && s_valid(s.y, thr)) ? e1 : 0.f;
+                        const float2 ve = fmul2(v2, make_float2(e0, e1));
+                        col[j] = fadd2(col[j], ve);
+                        r0 = fadd2(r0, ve);
+                        r1 = ffma2(ve, dx[j], r1);
+                        if constexpr (WITH_ABS) {
+                            const float2 qx = ffma2(a2, dx[j], bdy2);  // a dx + b dy
+                            const float2 qy = ffma2(b2, dx[j], cdy2);  // b dx + c dy
+                            Ax = fmaf(fabsf(ve.x), fabsf(qx.x), Ax);
+                            Ax = fmaf(fabsf(ve.y), fabsf(qx.y), Ax);
+                            Ay = fmaf(fabsf(ve.x), fabsf(qy.x), Ay);
+                            Ay = fmaf(fabsf(ve.y), fabsf(qy.y), Ay);
+                        }
+                    }
+                }
+                const float R0 = r0.x + r0.y, R1 = r1.x + r1.y;
+                Sy = fmaf(dy, R0, Sy);
+                Syy = fmaf(dy * dy, R0, Syy);
+                Sxy = fmaf(dy, R1, Sxy);
+            }
+            if (!live) continue;
+            float S0 = 0.f, Sx = 0.f, Sxx = 0.f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                S0 += col[j].x + col[j].y;
+                const float2 cx = fmul2(col[j], dx[j]);
+                Sx += cx.x + cx.y;
+                Sxx = fmaf(cx.x, dx[j].x, Sxx);
+                Sxx = fmaf(cx.y, dx[j].y, Sxx);
+            }
+            float* st = stats + g * 8;
+            red_add_v4(st, S0, Sx, Sy, Sxx);
+            if constexpr (WITH_ABS)
+                red_add_v4(st + 4, Sxy, Syy, Ax, Ay);
+            else
+                red_add_v2(st + 4, Sxy, Syy);
+        }
+        __syncthreads();
     }
 }
 

@@ -468,7 +468,7 @@ __device__ __forceinline__ VRecord load_vrecord(const float4* __restrict__ vspla
     return r;
 }
 
-constexpr int kVFwd8Threads = 128;  // 4 warps; a warp owns two z-slices, a thread 2x2 voxels (x, z)
+constexpr int kVFwd8Threads = 64;  // 2 warps; a warp owns four z-slices, a thread 4x2 voxels (x, z)
 constexpr int kVFwd8Batch = 128;
 
 __global__ void __launch_bounds__(kVFwd8Threads)
@@ -487,19 +487,20 @@ voxel_fwd8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict_
     const int xmax = min(7, (int)dim2 - 1 - X0);
     const int ymax = min(7, (int)dim1 - 1 - Y0);
     const int zmax = min(7, (int)dim0 - 1 - Z0);
-    const int lx = (tid & 3) * 2, ly = (tid >> 2) & 7, lz = warp * 2;
-    const float2 px = make_float2((float)(X0 + lx) + 0.5f, (float)(X0 + lx) + 1.5f);
+    const int lx = (tid & 1) * 4, ly = (tid >> 1) & 7, lz = (tid >> 4) * 2;
+    const float2 px01 = make_float2((float)(X0 + lx) + 0.5f, (float)(X0 + lx) + 1.5f);
+    const float2 px23 = make_float2((float)(X0 + lx) + 2.5f, (float)(X0 + lx) + 3.5f);
     const float py = (float)(Y0 + ly) + 0.5f;
     const float pz0 = (float)(Z0 + lz) + 0.5f, pz1 = (float)(Z0 + lz) + 1.5f;
     const int start = offsets[key];
     const int end = key + 1 < n_keys ? offsets[key + 1] : (int)n_isects;
-    float a00 = 0.f, a01 = 0.f, a10 = 0.f, a11 = 0.f;  // (z, x) offsets
+    float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};  // [z][x]
 
     for (int b0 = start; b0 < end; b0 += kVFwd8Batch) {
         const int n = min(kVFwd8Batch, end - b0);
         __syncthreads();
-        if (tid < n) {
-            const int64_t g = flatten_ids[b0 + tid];
+        for (int j = tid; j < n; j += kVFwd8Threads) {
+            const int64_t g = flatten_ids[b0 + j];
             const VRecord r = load_vrecord(vsplats, g);
             int xl, xh, yl, yh, zl, zh;
             cull_range_v(r.m[0], r.e[0], (float)X0, xmax, xl, xh);
@@ -508,12 +509,12 @@ voxel_fwd8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict_
             uint32_t msk = 0;
             if (xl <= xh && yl <= yh && zl <= zh) {
 #pragma unroll
-                for (int k = 0; k < 4; ++k)
-                    if (zl <= 2 * k + 1 && zh >= 2 * k) msk |= 1u << k;
+                for (int k = 0; k < 2; ++k)
+                    if (zl <= 4 * k + 3 && zh >= 4 * k) msk |= 1u << k;
             }
-            s_a[tid] = make_float4(r.m[0], r.m[1], r.m[2], r.A);
-            s_b[tid] = make_float4(r.B, r.Cq, r.D, r.E);
-            s_c[tid] = make_float4(r.F, r.w, s_threshold_v(r.w), __uint_as_float(msk));
+            s_a[j] = make_float4(r.m[0], r.m[1], r.m[2], r.A);
+            s_b[j] = make_float4(r.B, r.Cq, r.D, r.E);
+            s_c[j] = make_float4(r.F, r.w, s_threshold_v(r.w), __uint_as_float(msk));
         }
         __syncthreads();
         for (int t = 0; t < n; ++t) {
@@ -521,35 +522,43 @@ voxel_fwd8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict_
             if (!((__float_as_uint(c.w) >> warp) & 1u)) continue;  // warp-uniform
             const float4 a = s_a[t], b = s_b[t];
             const uint32_t thr = __float_as_uint(c.z);
-            const float2 dx = make_float2(px.x - a.x, px.y - a.x);
+            const float2 nmx = make_float2(-a.x, -a.x);
+            const float2 dx01 = fadd2(px01, nmx), dx23 = fadd2(px23, nmx);
             const float dy = py - a.y;
-            const float dz0 = pz0 - a.z, dz1 = pz1 - a.z;
             const float bdy = b.x * dy, ddy = b.z * dy;
-            const float u0 = fmaf(b.y, dz0, bdy), u1 = fmaf(b.y, dz1, bdy);
-            const float q0 = fmaf(dy, fmaf(b.w, dz0, ddy), c.x * dz0 * dz0);
-            const float q1 = fmaf(dy, fmaf(b.w, dz1, ddy), c.x * dz1 * dz1);
             const float2 A2 = make_float2(a.w, a.w);
-            const float2 s0 = ffma2(dx, ffma2(A2, dx, make_float2(u0, u0)), make_float2(q0, q0));
-            const float2 s1 = ffma2(dx, ffma2(A2, dx, make_float2(u1, u1)), make_float2(q1, q1));
-            const float e00 = exp2f(-s0.x), e01 = exp2f(-s0.y);
-            const float e10 = exp2f(-s1.x), e11 = exp2f(-s1.y);
-            if (s_valid_v(s0.x, thr)) a00 = fmaf(c.y, e00, a00);
-            if (s_valid_v(s0.y, thr)) a01 = fmaf(c.y, e01, a01);
-            if (s_valid_v(s1.x, thr)) a10 = fmaf(c.y, e10, a10);
-            if (s_valid_v(s1.y, thr)) a11 = fmaf(c.y, e11, a11);
+#pragma unroll
+            for (int zz = 0; zz < 2; ++zz) {
+                const float dz = (zz ? pz1 : pz0) - a.z;
+                const float u = fmaf(b.y, dz, bdy);
+                const float q = fmaf(dy, fmaf(b.w, dz, ddy), c.x * dz * dz);
+                const float2 u2 = make_float2(u, u), q2 = make_float2(q, q);
+                // s = dx (A dx + u) + q
+                const float2 s01 = ffma2(dx01, ffma2(A2, dx01, u2), q2);
+                const float2 s23 = ffma2(dx23, ffma2(A2, dx23, u2), q2);
+                const float e0 = exp2f(-s01.x), e1 = exp2f(-s01.y);
+                const float e2 = exp2f(-s23.x), e3 = exp2f(-s23.y);
+                if (s_valid_v(s01.x, thr)) acc[zz][0] = fmaf(c.y, e0, acc[zz][0]);
+                if (s_valid_v(s01.y, thr)) acc[zz][1] = fmaf(c.y, e1, acc[zz][1]);
+                if (s_valid_v(s23.x, thr)) acc[zz][2] = fmaf(c.y, e2, acc[zz][2]);
+                if (s_valid_v(s23.y, thr)) acc[zz][3] = fmaf(c.y, e3, acc[zz][3]);
+            }
         }
     }
     if (ly > ymax) return;
     const int64_t zoff = (int64_t)layer_begin * 8;
-    float* row0 = vol + ((Z0 + lz - zoff) * (int64_t)dim1 + (Y0 + ly)) * dim2 + X0 + lx;
-    float* row1 = row0 + (int64_t)dim1 * dim2;
-    if (lz <= zmax) {
-        if (lx <= xmax) row0[0] = a00;
-        if (lx + 1 <= xmax) row0[1] = a01;
-    }
-    if (lz + 1 <= zmax) {
-        if (lx <= xmax) row1[0] = a10;
-        if (lx + 1 <= xmax) row1[1] = a11;
+#pragma unroll
+    for (int zz = 0; zz < 2; ++zz) {
+        if (lz + zz > zmax) continue;
+        float* row = vol + ((Z0 + lz + zz - zoff) * (int64_t)dim1 + (Y0 + ly)) * dim2 + X0 + lx;
+        if (lx + 3 <= xmax && (dim2 & 3) == 0) {
+            *reinterpret_cast<float4*>(row) =
+                make_float4(acc[zz][0], acc[zz][1], acc[zz][2], acc[zz][3]);
+        } else {
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                if (lx + k <= xmax) row[k] = acc[zz][k];
+        }
     }
 }
 

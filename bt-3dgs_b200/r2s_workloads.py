@@ -11,8 +11,8 @@ at (DSO cos theta, DSO sin theta, 0); the view matrix is the rigid inverse
 scales through the bounded sigmoid (src/models/gaussian_model.py:266-274)
 and densities through softplus (gaussian_model.py:680-684).
 
-Everything is generated on the CPU with torch.Generator and moved by the
-caller.
+Everything is generated on the CPU (numpy PCG64, float64, then float32) and
+moved by the caller.
 """
 from __future__ import annotations
 
@@ -20,6 +20,7 @@ import math
 from dataclasses import dataclass
 from typing import Dict, Optional
 
+import numpy as np
 import torch
 
 SCALE_MIN = 5e-4  # configs/model/binary_tree.yaml:6
@@ -74,39 +75,42 @@ def inverse_softplus(rho: torch.Tensor) -> torch.Tensor:
     return torch.where(rho > 20, rho, torch.log(torch.expm1(rho)))
 
 
-def _means(cfg: WorkloadConfig, n: int, g: torch.Generator) -> torch.Tensor:
+def _means(cfg: WorkloadConfig, n: int, g: np.random.Generator) -> np.ndarray:
     if cfg.means == "uniform":
-        return torch.rand(n, 3, generator=g) - 0.5
+        return g.random((n, 3)) - 0.5
     if cfg.means == "clusters":
-        centers = (torch.rand(8, 3, generator=g) - 0.5) * 0.7
-        which = torch.randint(0, 8, (n,), generator=g)
-        m = centers[which] + 0.12 * torch.randn(n, 3, generator=g)
-        return m.clamp(-0.5, 0.5)
+        centers = (g.random((8, 3)) - 0.5) * 0.7
+        which = g.integers(0, 8, n)
+        m = centers[which] + 0.12 * g.standard_normal((n, 3))
+        return np.clip(m, -0.5, 0.5)
     if cfg.means == "shell":
         n_shell = int(round(0.3 * n))
-        cube = torch.rand(n - n_shell, 3, generator=g) - 0.5
-        d = torch.randn(n_shell, 3, generator=g)
-        d = d / d.norm(dim=-1, keepdim=True).clamp_min(1e-12)
-        r = 0.39 + 0.02 * torch.rand(n_shell, 1, generator=g)
-        m = torch.cat((cube, d * r), 0)
-        return m[torch.randperm(n, generator=g)]
+        cube = g.random((n - n_shell, 3)) - 0.5
+        d = g.standard_normal((n_shell, 3))
+        d = d / np.maximum(np.linalg.norm(d, axis=-1, keepdims=True), 1e-12)
+        r = 0.39 + 0.02 * g.random((n_shell, 1))
+        m = np.concatenate((cube, d * r), 0)
+        return m[g.permutation(n)]
     raise ValueError(cfg.means)
 
 
 def make_gaussians(cfg: WorkloadConfig, n: Optional[int] = None, seed: Optional[int] = None):
-    """Raw parameters (means, quats, raw_scales, raw_opacities), float32 CPU."""
+    """Raw parameters (means, quats, raw_scales, raw_opacities), float32 CPU.
+
+    Drawn with numpy's PCG64 generator in float64 (the same values on every
+    machine), activations inverted in float64, then rounded to float32."""
     n = cfg.n_gaussians if n is None else int(n)
-    g = torch.Generator().manual_seed(cfg.seed if seed is None else seed)
+    g = np.random.default_rng(cfg.seed if seed is None else seed)
     means = _means(cfg, n, g)
-    log_s = cfg.log_scale_lo + (cfg.log_scale_hi - cfg.log_scale_lo) * torch.rand(n, 3, generator=g)
-    scales = torch.exp(log_s)
-    quats = torch.randn(n, 4, generator=g)
-    quats = quats / quats.norm(dim=-1, keepdim=True).clamp_min(1e-12)
+    log_s = cfg.log_scale_lo + (cfg.log_scale_hi - cfg.log_scale_lo) * g.random((n, 3))
+    scales = torch.from_numpy(np.exp(log_s))
+    quats = g.standard_normal((n, 4))
+    quats = quats / np.maximum(np.linalg.norm(quats, axis=-1, keepdims=True), 1e-12)
     if cfg.density == "uniform":
-        rho = torch.rand(n, generator=g)
+        rho = torch.from_numpy(g.random(n))
     else:
-        rho = torch.exp(-2.0 + 1.0 * torch.randn(n, generator=g))
-    return (means.float().contiguous(), quats.float().contiguous(),
+        rho = torch.from_numpy(np.exp(-2.0 + 1.0 * g.standard_normal(n)))
+    return (torch.from_numpy(means).float().contiguous(), torch.from_numpy(quats).float().contiguous(),
             inverse_scale(scales).float().contiguous(), inverse_softplus(rho).float().contiguous())
 
 
