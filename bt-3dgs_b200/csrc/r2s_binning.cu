@@ -231,34 +231,57 @@ __device__ __forceinline__ void walk_items(const void* __restrict__ rects, int64
         const int64_t i = base + lane;
         ItemRect r{0, 0, 0, 0, 0};
         if (i < w1) r = load_rect<LAYERED>(rects, s, i, N, layer);
+        // the owner lane decodes its item once: (x0 | w << 16), (y0 | n << 16), 1 / w
+        const uint32_t w = r.x1 - r.x0;
+        const uint32_t pa = r.x0 | (w << 16), pb = r.y0 | ((uint32_t)r.n << 16);
+        const float prw = r.n > 0 ? 1.0f / (float)w : 0.f;
         unsigned todo = __ballot_sync(0xffffffffu, r.n > 0);
-        const uint32_t px = pack16(r.x0, r.x1), py = pack16(r.y0, r.y1);
         const int local0 = (int)(base - i_base);
+        int j = todo ? __ffs(todo) - 1 : 0;
+        uint32_t qa = __shfl_sync(0xffffffffu, pa, j), qb = __shfl_sync(0xffffffffu, pb, j);
+        float qr = __shfl_sync(0xffffffffu, prw, j);
         while (todo) {
-            const int j = __ffs(todo) - 1;
             todo &= todo - 1;
-            const uint32_t qx = __shfl_sync(0xffffffffu, px, j);
-            const uint32_t qy = __shfl_sync(0xffffffffu, py, j);
-            const int x0 = (int)lo16(qx), w = (int)(hi16(qx) - lo16(qx));
-            const int y0 = (int)lo16(qy), h = (int)(hi16(qy) - lo16(qy));
-            const int n = w * h;
+            // fetch the next item while this one is placed
+            const int jn = todo ? __ffs(todo) - 1 : 0;
+            const uint32_t na = __shfl_sync(0xffffffffu, pa, jn);
+            const uint32_t nb = __shfl_sync(0xffffffffu, pb, jn);
+            const float nr = __shfl_sync(0xffffffffu, prw, jn);
+            const int x0 = (int)(qa & 0xffffu), iw = (int)(qa >> 16);
+            const int y0 = (int)(qb & 0xffffu), n = (int)(qb >> 16);
             // q / w for q < 2^21 records by a float reciprocal: (q + 0.5) / w
             // lies at least 0.5 / w from an integer, far above the rounding
-            const float rw = 1.0f / (float)w;
-            int dy = (int)(((float)lane + 0.5f) * rw);
-            int dx = lane - dy * w;
-            const int sdy = (int)(32.5f * rw), sdx = 32 - sdy * w;
+            int dy = (int)(((float)lane + 0.5f) * qr);
+            int dx = lane - dy * iw;
+            const int sdy = (int)(32.5f * qr), sdx = 32 - sdy * iw;
             for (int q = lane; q < n; q += 32) {
                 emit((y0 + dy) * (int)tiles_x + x0 + dx, local0 + j);
                 dy += sdy;
                 dx += sdx;
-                if (dx >= w) {
-                    dx -= w;
+                if (dx >= iw) {
+                    dx -= iw;
                     ++dy;
                 }
             }
             __syncwarp();
+            j = jn;
+            qa = na;
+            qb = nb;
+            qr = nr;
         }
+    }
+}
+
+// Per-tile record counts of items [w0, w1), one item per lane (order-free).
+template <bool LAYERED>
+__device__ __forceinline__ void count_items(const void* __restrict__ rects, int64_t s, int64_t N,
+                                            int64_t layer, int64_t w0, int64_t w1,
+                                            uint32_t tiles_x, int32_t* counts) {
+    for (int64_t i = w0 + (threadIdx.x & 31); i < w1; i += 32) {
+        const ItemRect r = load_rect<LAYERED>(rects, s, i, N, layer);
+        if (r.n == 0) continue;
+        for (uint32_t y = r.y0; y < r.y1; ++y)
+            for (uint32_t x = r.x0; x < r.x1; ++x) atomicAdd(&counts[y * tiles_x + x], 1);
     }
 }
 
@@ -296,7 +319,7 @@ __device__ __forceinline__ int block_exclusive_scan(const int32_t* v, int32_t* o
 constexpr int kStagedWarps = 8;
 
 // Phase 3, staged: one CTA per (segment, chunk).  Warps take consecutive
-// sub-chunks; a counting walk gives per-(warp, tile) counts, whose prefix over
+// sub-chunks; shared-memory atomics give per-(warp, tile) counts, whose prefix over
 // warps and tiles places every record of the chunk in a tile-major staging
 // buffer in shared memory (16-bit item offsets), in item order per tile.  The
 // buffer is then written out one tile run at a time, so each tile's records
@@ -332,8 +355,7 @@ bin_place_staged_kernel(const void* __restrict__ rects, int64_t N, int T, uint32
     __syncthreads();
 
     int32_t* mine = wc + warp * T;
-    walk_items<LAYERED>(rects, s, N, layer, w0, w1, i0, tiles_x,
-                        [&](int tile, int) { mine[tile] += 1; });
+    count_items<LAYERED>(rects, s, N, layer, w0, w1, tiles_x, mine);
     __syncthreads();
     for (int t = tid; t < T; t += nthr) {
         int run = 0;
