@@ -443,7 +443,11 @@ __global__ void raster_unpack_kernel(const S* __restrict__ stats, const S* __res
 // bit set) compares above s_thr as an unsigned integer, so one integer
 // compare decides the pair.  Pairs within rounding of the alpha cut-off may
 // be decided differently from the reference's float test; each such pair
-// moves a pixel by at most ~1e-5.
+// moves a pixel by at most ~1e-5.  The 16x16 kernels evaluate -s with negated
+// coefficients (exact: negation commutes with rounding) and compare the bits
+// of -s as signed integers with INT_MIN + bits(s_thr); the one value decided
+// differently from "0 <= s <= s_thr" is s = -0.0, which needs a conic that is
+// not positive definite and a pixel centre on the mean, and counts as s < 0.
 
 __device__ __forceinline__ bool s_valid(float s, uint32_t thr_bits) {
     return __float_as_uint(s) <= thr_bits;
@@ -504,8 +508,13 @@ raster_fwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict
                 for (int k = 0; k < 4; ++k)
                     if (r_lo <= 4 * k + 3 && r_hi >= 4 * k) m |= 1u << k;
             }
-            s_p[tid] = make_float4(p.x, p.y, 0.5f * kLog2e * p.z, kLog2e * p.w);
-            s_q[tid] = make_float4(0.5f * kLog2e * q.x, q.y, s_threshold(q.y), __uint_as_float(m));
+            // negated coefficients: the packed chain yields -s exactly, so ex2
+            // takes it as is; the cut-off test compares the bits of -s as
+            // signed integers against INT_MIN + bits(s_thr)
+            s_p[tid] = make_float4(p.x, p.y, -0.5f * kLog2e * p.z, -kLog2e * p.w);
+            s_q[tid] = make_float4(-0.5f * kLog2e * q.x, q.y,
+                                   __uint_as_float(__float_as_uint(s_threshold(q.y)) ^ 0x80000000u),
+                                   __uint_as_float(m));
         }
         __syncthreads();
         for (int t = warp; t < n; t += kFwd16Threads / 32) {
@@ -513,7 +522,7 @@ raster_fwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict
             const uint32_t m = __float_as_uint(Q.w);
             if (m == 0) continue;  // warp-uniform
             const float4 P = s_p[t];
-            const uint32_t thr = __float_as_uint(Q.z);
+            const int thr_n = __float_as_int(Q.z);
             const float dx = px - P.x;
             const float xx = P.z * dx * dx;
             const float xy = P.w * dx;
@@ -523,10 +532,10 @@ raster_fwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict
             for (int g = 0; g < 4; ++g) {
                 if (!((m >> g) & 1u)) continue;  // warp-uniform
                 const float2 dy = fadd2(py[g], nmy);
-                const float2 s = ffma2(dy, ffma2(C2, dy, xy2), xx2);
-                const float e0 = exp2f(-s.x), e1 = exp2f(-s.y);
-                if (s_valid(s.x, thr)) acc[2 * g] = fmaf(Q.y, e0, acc[2 * g]);
-                if (s_valid(s.y, thr)) acc[2 * g + 1] = fmaf(Q.y, e1, acc[2 * g + 1]);
+                const float2 sn = ffma2(dy, ffma2(C2, dy, xy2), xx2);  // -s
+                const float e0 = exp2f(sn.x), e1 = exp2f(sn.y);
+                if (__float_as_int(sn.x) <= thr_n) acc[2 * g] = fmaf(Q.y, e0, acc[2 * g]);
+                if (__float_as_int(sn.y) <= thr_n) acc[2 * g + 1] = fmaf(Q.y, e1, acc[2 * g + 1]);
             }
         }
     }
@@ -656,8 +665,10 @@ raster_bwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict
             const int64_t g = s_g[idx];
             const float4 p = s_p[idx], q = s_q[idx];
 
-            const float A = 0.5f * kLog2e * p.z, B = kLog2e * p.w, Cc = 0.5f * kLog2e * q.x;
-            const uint32_t thr = __float_as_uint(s_threshold(q.y));
+            // negated coefficients: the packed chain yields -s exactly (see the
+            // forward kernel for the cut-off test on the bits of -s)
+            const float A = -0.5f * kLog2e * p.z, B = -kLog2e * p.w, Cc = -0.5f * kLog2e * q.x;
+            const int thr_n = (int)(__float_as_uint(s_threshold(q.y)) ^ 0x80000000u);
             const float2 A2 = make_float2(A, A);
             const float2 a2 = make_float2(p.z, p.z), b2 = make_float2(p.w, p.w);
             float2 dx[8], col[8];
@@ -684,10 +695,10 @@ raster_bwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict
                         const int j = 2 * j4 + h;
                         const float2 v2 = h ? make_float2(v4.z, v4.w) : make_float2(v4.x, v4.y);
                         const float2 t = ffma2(A2, dx[j], by2);
-                        const float2 s = ffma2(dx[j], t, cyy2);
-                        float e0 = exp2f(-s.x), e1 = exp2f(-s.y);
-                        e0 = (rin && s_valid(s.x, thr)) ? e0 : 0.f;
-                        e1 = (rin && s_valid(s.y, thr)) ? e1 : 0.f;
+                        const float2 sn = ffma2(dx[j], t, cyy2);  // -s
+                        float e0 = exp2f(sn.x), e1 = exp2f(sn.y);
+                        e0 = (rin && __float_as_int(sn.x) <= thr_n) ? e0 : 0.f;
+                        e1 = (rin && __float_as_int(sn.y) <= thr_n) ? e1 : 0.f;
                         const float2 ve = fmul2(v2, make_float2(e0, e1));
                         col[j] = fadd2(col[j], ve);
                         r0 = fadd2(r0, ve);

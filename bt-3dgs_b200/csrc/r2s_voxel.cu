@@ -432,8 +432,15 @@ __global__ void voxel_bwd_kernel(VoxSrc<S> src, const int32_t* __restrict__ offs
 // Pairs within rounding of the cut-off may be decided differently from the
 // reference's float test; each such pair moves a voxel by at most ~1e-6.
 
-__device__ __forceinline__ bool s_valid_v(float s, uint32_t thr_bits) {
-    return __float_as_uint(s) <= thr_bits;
+// The kernels evaluate -s (negated coefficients, exact) and compare its bits as
+// signed integers with INT_MIN + bits(s_thr); s = -0.0 (a conic that is not
+// positive definite, voxel centre on the mean) counts as s < 0.
+__device__ __forceinline__ bool sn_valid_v(float sn, int thr_n) {
+    return __float_as_int(sn) <= thr_n;
+}
+
+__device__ __forceinline__ int thr_neg_v(float thr) {
+    return (int)(__float_as_uint(thr) ^ 0x80000000u);
 }
 
 __device__ __forceinline__ float s_threshold_v(float w) {
@@ -443,7 +450,8 @@ __device__ __forceinline__ float s_threshold_v(float w) {
 
 struct VRecord {
     float m[3];
-    float A, B, Cq, D, E, F;  // pre-scaled conic: sigma log2(e) = dx (A dx + B dy + Cq dz) + dy (D dy + E dz) + F dz^2
+    // negated pre-scaled conic: -sigma log2(e) = dx (A dx + B dy + Cq dz) + dy (D dy + E dz) + F dz^2
+    float A, B, Cq, D, E, F;
     float w;
     float e[3];
 };
@@ -455,12 +463,12 @@ __device__ __forceinline__ VRecord load_vrecord(const float4* __restrict__ vspla
     r.m[0] = a.x;
     r.m[1] = a.y;
     r.m[2] = a.z;
-    r.A = 0.5f * kLog2eV * a.w;
-    r.B = kLog2eV * b.x;
-    r.Cq = kLog2eV * b.y;
-    r.D = 0.5f * kLog2eV * b.z;
-    r.E = kLog2eV * b.w;
-    r.F = 0.5f * kLog2eV * c.x;
+    r.A = -0.5f * kLog2eV * a.w;
+    r.B = -kLog2eV * b.x;
+    r.Cq = -kLog2eV * b.y;
+    r.D = -0.5f * kLog2eV * b.z;
+    r.E = -kLog2eV * b.w;
+    r.F = -0.5f * kLog2eV * c.x;
     r.w = c.y;
     r.e[0] = c.z;
     r.e[1] = c.w;
@@ -514,14 +522,15 @@ voxel_fwd8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict_
             }
             s_a[j] = make_float4(r.m[0], r.m[1], r.m[2], r.A);
             s_b[j] = make_float4(r.B, r.Cq, r.D, r.E);
-            s_c[j] = make_float4(r.F, r.w, s_threshold_v(r.w), __uint_as_float(msk));
+            s_c[j] = make_float4(r.F, r.w, __int_as_float(thr_neg_v(s_threshold_v(r.w))),
+                                 __uint_as_float(msk));
         }
         __syncthreads();
         for (int t = 0; t < n; ++t) {
             const float4 c = s_c[t];
             if (!((__float_as_uint(c.w) >> warp) & 1u)) continue;  // warp-uniform
             const float4 a = s_a[t], b = s_b[t];
-            const uint32_t thr = __float_as_uint(c.z);
+            const int thr_n = __float_as_int(c.z);
             const float2 nmx = make_float2(-a.x, -a.x);
             const float2 dx01 = fadd2(px01, nmx), dx23 = fadd2(px23, nmx);
             const float dy = py - a.y;
@@ -533,15 +542,15 @@ voxel_fwd8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict_
                 const float u = fmaf(b.y, dz, bdy);
                 const float q = fmaf(dy, fmaf(b.w, dz, ddy), c.x * dz * dz);
                 const float2 u2 = make_float2(u, u), q2 = make_float2(q, q);
-                // s = dx (A dx + u) + q
+                // -s = dx (A dx + u) + q
                 const float2 s01 = ffma2(dx01, ffma2(A2, dx01, u2), q2);
                 const float2 s23 = ffma2(dx23, ffma2(A2, dx23, u2), q2);
-                const float e0 = exp2f(-s01.x), e1 = exp2f(-s01.y);
-                const float e2 = exp2f(-s23.x), e3 = exp2f(-s23.y);
-                if (s_valid_v(s01.x, thr)) acc[zz][0] = fmaf(c.y, e0, acc[zz][0]);
-                if (s_valid_v(s01.y, thr)) acc[zz][1] = fmaf(c.y, e1, acc[zz][1]);
-                if (s_valid_v(s23.x, thr)) acc[zz][2] = fmaf(c.y, e2, acc[zz][2]);
-                if (s_valid_v(s23.y, thr)) acc[zz][3] = fmaf(c.y, e3, acc[zz][3]);
+                const float e0 = exp2f(s01.x), e1 = exp2f(s01.y);
+                const float e2 = exp2f(s23.x), e3 = exp2f(s23.y);
+                if (sn_valid_v(s01.x, thr_n)) acc[zz][0] = fmaf(c.y, e0, acc[zz][0]);
+                if (sn_valid_v(s01.y, thr_n)) acc[zz][1] = fmaf(c.y, e1, acc[zz][1]);
+                if (sn_valid_v(s23.x, thr_n)) acc[zz][2] = fmaf(c.y, e2, acc[zz][2]);
+                if (sn_valid_v(s23.y, thr_n)) acc[zz][3] = fmaf(c.y, e3, acc[zz][3]);
             }
         }
     }
@@ -617,7 +626,7 @@ voxel_bwd8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict_
         const int y1 = __reduce_max_sync(0xffffffffu, yh);
         if (z0 > z1) continue;
 
-        const uint32_t thr = __float_as_uint(s_threshold_v(r.w));
+        const int thr_n = thr_neg_v(s_threshold_v(r.w));
         const float2 A2 = make_float2(r.A, r.A);
         float2 dx[4], col[4];
 #pragma unroll
@@ -645,10 +654,10 @@ voxel_bwd8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict_
                                       : j == 1 ? make_float2(va.z, va.w)
                                       : j == 2 ? make_float2(vb.x, vb.y)
                                                : make_float2(vb.z, vb.w);
-                    const float2 s = ffma2(dx[j], ffma2(A2, dx[j], by2), rest2);
-                    float e0 = exp2f(-s.x), e1 = exp2f(-s.y);
-                    e0 = (rin && s_valid_v(s.x, thr)) ? e0 : 0.f;
-                    e1 = (rin && s_valid_v(s.y, thr)) ? e1 : 0.f;
+                    const float2 sn = ffma2(dx[j], ffma2(A2, dx[j], by2), rest2);  // -s
+                    float e0 = exp2f(sn.x), e1 = exp2f(sn.y);
+                    e0 = (rin && sn_valid_v(sn.x, thr_n)) ? e0 : 0.f;
+                    e1 = (rin && sn_valid_v(sn.y, thr_n)) ? e1 : 0.f;
                     const float2 ve = fmul2(v2, make_float2(e0, e1));
                     col[j] = fadd2(col[j], ve);
                     r0 = fadd2(r0, ve);
