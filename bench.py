@@ -355,8 +355,8 @@ def kernel_time(fn, reps=3):
 
 # DRAM traffic of one raster_bwd16_kernel launch per view, from the ncu
 # capture of `bench.py --views 8` (dram__bytes_read.sum + dram__bytes_write.sum
-# = 439.3 MB + 101.7 MB for 8 views; traffic grows with the views).
-BWD16_DRAM_BYTES_PER_VIEW = (439.278336e6 + 101.730048e6) / 8
+# = 441.2 MB + 103.9 MB for 8 views; traffic grows with the views).
+BWD16_DRAM_BYTES_PER_VIEW = (441.213952e6 + 103.907328e6) / 8
 
 
 def dominant_kernel_roofline(proj: OursProjection, hbm_peak, peak_kind, clock_mhz):
