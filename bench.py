@@ -418,6 +418,62 @@ def dominant_kernel_roofline(proj: OursProjection, hbm_peak, peak_kind, clock_mh
     }
 
 
+def _training_inputs(cfg, dev):
+    """Config-sized inputs of the training rows after the backward: the four
+    parameter groups with gradients and Adam optimizers (eps 1e-15 and the
+    per-group learning rates of the reference's model config), and one step's
+    screen-space gradients and radii for the densification statistics."""
+    N, C = cfg.n_gaussians, cfg.n_views
+    g = torch.Generator(device=dev).manual_seed(300)
+    shapes = {"means": (N, 3), "quats": (N, 4), "scales": (N, 3), "opacities": (N,)}
+    lrs = {"means": 1.6e-4, "quats": 1e-3, "scales": 5e-3, "opacities": 5e-2}
+    params = {k: torch.nn.Parameter(torch.randn(v, generator=g, device=dev)) for k, v in shapes.items()}
+    for p in params.values():
+        p.grad = torch.randn(p.shape, generator=g, device=dev) * 1e-3
+    opts = {k: torch.optim.Adam([{"params": p, "name": k}], lr=lrs[k], eps=1e-15)
+            for k, p in params.items()}
+    grads2d = torch.rand((C, N, 2), generator=g, device=dev) * 1e-3
+    radii = torch.randint(0, 40, (C, N), generator=g, device=dev, dtype=torch.int32)
+    return opts, grads2d, radii
+
+
+def training_rows(cfg, dev, reference: bool, reps: int = 10):
+    """Device time of one Adam step over all parameter groups and of one
+    step's densification statistics (config-sized), ours or the reference's
+    PyTorch code (torch.optim.Adam; the strategy's _update_state)."""
+    opts, grads2d, radii = _training_inputs(cfg, dev)
+    C, N = radii.shape
+    state = {"grad2d": None, "count": None, "radii": None}
+    if reference:
+        from oracle import r2s_oracle as O
+
+        def adam():
+            for o in opts.values():
+                o.step()
+
+        def densify():
+            O.densify_state_update(state, grads2d, radii, cfg.detector, cfg.detector, C,
+                                   track_radii=True)
+    else:
+        from r2splat.ops import training as T
+
+        def adam():
+            T.adam_step(opts)
+
+        info = {"means2d": torch.zeros(1), "radii": radii, "width": cfg.detector,
+                "height": cfg.detector, "n_cameras": C}
+        info["means2d"].absgrad = grads2d
+
+        def densify():
+            T.update_densify_state(state, info, track_radii=True)
+    out = {}
+    for name, fn in (("adam", adam), ("densify", densify)):
+        fn()
+        out[name + "_ms"] = round(kernel_time(fn, reps), 4)
+    out["groups"] = "means [N,3], quats [N,4], scales [N,3], opacities [N]; densify [C,N] pairs"
+    return out
+
+
 def cpu_baseline(cfg, seconds_budget=15.0):
     """Dense PyTorch-on-CPU evaluation of the same formulas (the CPU oracle):
     projection forward + autograd backward of a sample of Gaussians on one
@@ -488,6 +544,9 @@ def main():
         with ClockSampler(local) as clk:
             ms = time_steps(proj.step, args.steps, args.warmup, 1, flush)
             vms = time_steps(vox.step, args.steps, args.warmup, 1, flush)
+        del proj, vox
+        torch.cuda.empty_cache()
+        train = training_rows(cfg, dev, reference=True)
         value = cfg.n_gaussians * cfg.n_views / (ms * 1e-3)
         line = {
             "metric": "Gaussian*views/s projection fwd+bwd (and Mvoxels/s voxelize fwd+bwd)",
@@ -506,6 +565,7 @@ def main():
                                        "implementation), full workload on GPU 0"},
             "e2e": {"value": round(value, 1), "unit": "Gaussian*views/s",
                     "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "training": train,
             "clocks": clk.summary(),
         }
         print(json.dumps(line))
@@ -520,6 +580,9 @@ def main():
         vox = OursVoxel(cfg, world, rank, dev, proj.params)
         torch.cuda.empty_cache()
         vms = time_steps(vox.step, args.steps, args.warmup, world, flush)
+    del vox
+    torch.cuda.empty_cache()
+    train = training_rows(cfg, dev, reference=False) if rank == 0 else None
     value = world * cfg.n_gaussians * cfg.n_views / (ms * 1e-3)
     e2e_value = world * cfg.n_gaussians * cfg.n_views / (e2e_ms * 1e-3)
     h2d, d2h = proj.bytes_e2e()
@@ -549,6 +612,7 @@ def main():
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": round(e2e_ms, 3)},
         "roofline": roof,
+        "training": train,
         "gpu_launches": gpu_launches,
         "clocks": clk.summary(),
     }

@@ -28,9 +28,19 @@ _u32 = ctypes.c_uint32
 _f64 = ctypes.c_double
 _p = ctypes.c_void_p
 
+class AdamGroup(ctypes.Structure):
+    """r2s_adam_group of include/r2s.h."""
+
+    _fields_ = [("param", ctypes.c_void_p), ("grad", ctypes.c_void_p),
+                ("exp_avg", ctypes.c_void_p), ("exp_avg_sq", ctypes.c_void_p),
+                ("numel", ctypes.c_int64), ("lr", ctypes.c_double), ("step", ctypes.c_int64)]
+
+
 # argument type lists of every exported function (include/r2s.h)
 _SIGNATURES = {
     "r2s_version": ([], ctypes.c_char_p),
+    "r2s_adam_step_f32": ([ctypes.POINTER(AdamGroup), _i32, _f64, _f64, _f64, _p], _i32),
+    "r2s_densify_stats_f32": ([_p, _p, _i64, _i64, _f64, _f64, _f64, _p, _p, _p, _p], _i32),
     "r2s_last_error": ([ctypes.c_char_p, ctypes.c_size_t], ctypes.c_size_t),
     "r2s_parameter_transform_fwd": ([_i32, _p, _p, _f64, _f64, _p, _p, _i64, _p], _i32),
     "r2s_parameter_transform_bwd": ([_i32, _p, _p, _f64, _f64, _p, _p, _p, _i64, _p], _i32),

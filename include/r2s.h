@@ -51,6 +51,43 @@ enum {
     R2S_ERR_UNSUPPORTED = 4  /* shape outside what this build supports */
 };
 
+/* ------------------------------------------------------------------------
+ * Training-step rows (after the rasterizer backward)
+ * ---------------------------------------------------------------------- */
+
+/* One Adam parameter group: float32 parameter, gradient and the two moment
+ * buffers (same numel), its learning rate and the step count after this
+ * update (torch.optim.Adam's state["step"] + 1). */
+typedef struct r2s_adam_group {
+    float* param;
+    const float* grad;
+    float* exp_avg;
+    float* exp_avg_sq;
+    int64_t numel;
+    double lr;
+    int64_t step;
+} r2s_adam_group;
+
+/* Adam update of up to 8 parameter groups in one launch, with
+ * torch.optim.Adam's arithmetic (amsgrad off, no weight decay).  Replaces the
+ * per-group optimizer.step() of the reference training loop
+ * (src/trainers/binary_tree.py:204-206) over the optimizers built by
+ * GaussianModel.build_optimizers (src/models/gaussian_model.py:514-530). */
+R2S_API int r2s_adam_step_f32(const r2s_adam_group* groups, int n_groups, double beta1,
+                              double beta2, double eps, r2s_stream_t stream);
+
+/* Densification statistics of one training step: for every (view, Gaussian)
+ * with radius > 0, grad2d[g] += |(gx * scale_x, gy * scale_y)|, count[g] += 1,
+ * and, when max_radii is not NULL, max_radii[g] = max(max_radii[g],
+ * radius / extent).  grads2d [C,N,2] float32 (means2d.absgrad or .grad),
+ * radii [C,N] int32 (the per-axis maximum).  Replaces
+ * BinaryTreeStrategy._update_state (src/strategies/binary_tree.py:305-347,
+ * non-packed path; scale_x = W/2 * C, scale_y = H/2 * C, extent = max(W, H)). */
+R2S_API int r2s_densify_stats_f32(const float* grads2d, const int32_t* radii, int64_t C,
+                                  int64_t N, double scale_x, double scale_y, double extent,
+                                  float* grad2d, float* count, float* max_radii,
+                                  r2s_stream_t stream);
+
 R2S_API const char* r2s_version(void);
 /* Copies the last error message of this thread into buf (NUL-terminated,
  * truncated to len-1 bytes); returns the full message length. */

@@ -133,3 +133,15 @@ def test_wrapper_without_cuda_raises_runtime_error():
     assert W.is_cuda_extension_available() is False
     with pytest.raises(RuntimeError):
         W.conics_mu_fwd(torch.zeros(1, 1, 6), 0.0)
+
+
+def test_adam_step_rejects_unsupported_options():
+    from r2splat.ops.training import adam_step
+
+    p = torch.nn.Parameter(torch.zeros(3))
+    p.grad = torch.zeros(3)
+    for kwargs in ({"amsgrad": True}, {"weight_decay": 0.1}, {"maximize": True}):
+        with pytest.raises(ValueError, match="unsupported"):
+            adam_step(torch.optim.Adam([p], lr=0.1, **kwargs))
+    with pytest.raises(TypeError):
+        adam_step([torch.optim.SGD([p], lr=0.1)])
