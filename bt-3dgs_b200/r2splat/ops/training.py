@@ -13,6 +13,9 @@ interchangeable.
 * ``update_densify_state(state, info, ...)`` -- the strategy's per-step
   statistics (``BinaryTreeStrategy._update_state``,
   src/strategies/binary_tree.py:305-347, non-packed path) in one launch.
+* ``FusedBinaryTreeLossComputer`` -- the trainer's loss
+  (``BinaryTreeLossComputer``, src/utils/loss.py:125-172): L1, SSIM and
+  edge terms of the projections in one kernel each way, volume TV in one.
 """
 from __future__ import annotations
 
@@ -24,7 +27,8 @@ import torch
 from ..cuda import _wrapper as W
 from ..cuda._backend import AdamGroup
 
-__all__ = ["adam_step", "update_densify_state"]
+__all__ = ["FusedBinaryTreeLossComputer", "adam_step", "projection_losses", "tv_loss",
+           "update_densify_state"]
 
 _MAX_GROUPS = 8
 
@@ -129,3 +133,162 @@ def update_densify_state(state: dict, info: dict, *, absgrad: bool = True,
             width / 2.0 * n_cam, height / 2.0 * n_cam, max(width, height),
             W._ptr(state["grad2d"]), W._ptr(state["count"]),
             W._ptr(state["radii"]) if track_radii else None, W._stream(dev))
+
+
+# ---------------------------------------------------------------------------
+# losses (BinaryTreeLossComputer, src/utils/loss.py:125-172)
+# ---------------------------------------------------------------------------
+def _image_stack(t: torch.Tensor, name: str) -> torch.Tensor:
+    """[C, A, B] or single-channel [C, A, B, 1] -> contiguous float32 [C, A, B]."""
+    if t.dim() == 4:
+        if t.size(-1) != 1:
+            raise RuntimeError(f"{name}: fused losses take single-channel images")
+        t = t[..., 0]
+    if t.dim() != 3:
+        raise RuntimeError(f"{name}: expected [C, H, W] or [C, H, W, 1], got {tuple(t.shape)}")
+    if t.dtype != torch.float32:
+        raise RuntimeError(f"{name}: expected float32")
+    t = t.contiguous()
+    W._check_cuda(name, t)
+    return t
+
+
+_WINDOW_1D = {}
+
+
+def _window_1d(window_size: int = 11):
+    """The 1-D float32 SSIM weights exactly as the reference builds them
+    (src/utils/metric.py:14-18: a float32 tensor of exp(-(x - ws//2)^2 /
+    (2 sigma^2)), sigma 1.5, divided by its float32 sum)."""
+    import math
+
+    w = _WINDOW_1D.get(window_size)
+    if w is None:
+        g = torch.tensor([math.exp(-((x - window_size // 2) ** 2) / float(2 * 1.5 ** 2))
+                          for x in range(window_size)])
+        g = g / g.sum()
+        w = (ctypes.c_float * window_size)(*[float(v) for v in g.tolist()])
+        _WINDOW_1D[window_size] = w
+    return w
+
+
+class _ProjectionLoss(torch.autograd.Function):
+    """(l1, ssim, edge) means of one batch of projections; gradient w.r.t. the
+    renders only (the targets are data)."""
+
+    @staticmethod
+    def forward(ctx, renders, targets, edge_targets, edge_mask):
+        C, H, Wd = renders.shape
+        sums = torch.zeros(3, dtype=torch.float64, device=renders.device)
+        W._call("r2s_projection_loss_f32", W._ptr(renders), W._ptr(targets),
+                W._ptr(edge_targets), W._ptr(edge_mask), C, H, Wd, 11, _window_1d(), None, None,
+                W._ptr(sums), W._stream(renders.device))
+        ctx.save_for_backward(renders, targets, edge_targets, edge_mask)
+        means = (sums / max(1, renders.numel())).float()
+        return means[0], means[1], means[2]
+
+    @staticmethod
+    def backward(ctx, g_l1, g_ssim, g_edge):
+        renders, targets, edge_targets, edge_mask = ctx.saved_tensors
+        if not ctx.needs_input_grad[0]:
+            return None, None, None, None
+        dev = renders.device
+        weights = torch.stack([g if g is not None else torch.zeros((), device=dev)
+                               for g in (g_l1, g_ssim, g_edge)]).float().contiguous()
+        grad = torch.empty_like(renders)
+        sums = torch.zeros(3, dtype=torch.float64, device=dev)
+        C, H, Wd = renders.shape
+        W._call("r2s_projection_loss_f32", W._ptr(renders), W._ptr(targets),
+                W._ptr(edge_targets), W._ptr(edge_mask), C, H, Wd, 11, _window_1d(),
+                W._ptr(weights), W._ptr(grad), W._ptr(sums), W._stream(dev))
+        return grad, None, None, None
+
+
+class _TVLoss(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, vol):
+        D0, D1, D2 = vol.shape
+        s = torch.zeros(1, dtype=torch.float64, device=vol.device)
+        W._call("r2s_tv_loss_f32", W._ptr(vol), D0, D1, D2, None, None, W._ptr(s),
+                W._stream(vol.device))
+        denom = (D0 - 1) * D1 * D2 + D0 * (D1 - 1) * D2 + D0 * D1 * (D2 - 1)
+        ctx.save_for_backward(vol)
+        return (s[0] / max(1, denom)).float()
+
+    @staticmethod
+    def backward(ctx, g):
+        (vol,) = ctx.saved_tensors
+        D0, D1, D2 = vol.shape
+        grad = torch.empty_like(vol)
+        s = torch.zeros(1, dtype=torch.float64, device=vol.device)
+        weight = g.reshape(1).float().contiguous()
+        W._call("r2s_tv_loss_f32", W._ptr(vol), D0, D1, D2, W._ptr(weight), W._ptr(grad),
+                W._ptr(s), W._stream(vol.device))
+        return grad
+
+
+def projection_losses(renders, targets, edge_mask=None, edge_targets=None):
+    """(l1, ssim, edge) means as differentiable device scalars (11x11 SSIM
+    window); renders/targets [C, H, W] or [C, H, W, 1] float32 CUDA."""
+    r = _image_stack(renders, "renders")  # indexing and contiguous() keep the autograd edge
+    t = _image_stack(targets.detach(), "targets")
+    et = em = None
+    if edge_mask is not None:
+        et = t if edge_targets is None else _image_stack(edge_targets.detach(), "edge_targets")
+        em = _image_stack(edge_mask.detach().to(torch.float32), "edge_mask")
+    if r.shape != t.shape:
+        raise RuntimeError("renders and targets must have the same shape")
+    return _ProjectionLoss.apply(r, t, et, em)
+
+
+def tv_loss(volume):
+    """compute_tv_loss(volume, reduction="mean") (src/utils/loss.py:10-21)."""
+    vol = volume
+    if vol.dim() == 4 and vol.size(0) == 1:
+        vol = vol[0]
+    if vol.dim() != 3:
+        raise AssertionError("tv_3d_loss expects 3D volume")
+    if vol.dtype != torch.float32:
+        raise RuntimeError("tv_loss: expected float32")
+    vol = vol.contiguous()
+    W._check_cuda("volume", vol)
+    return _TVLoss.apply(vol)
+
+
+class FusedBinaryTreeLossComputer:
+    """Drop-in for the reference's BinaryTreeLossComputer: same constructor,
+    same call signature, same output keys; the projection terms and the
+    volume TV come from the fused kernels (one pass each way)."""
+
+    def __init__(self, w_l1: float, w_ssim: float, w_tv: float, w_edge: float,
+                 w_hierarchy: float = 0.0, ssim_window: int = 11):
+        if ssim_window != 11:
+            raise ValueError("the fused losses are built for the 11-pixel SSIM window")
+        self.w_l1, self.w_ssim, self.w_tv = w_l1, w_ssim, w_tv
+        self.w_edge, self.w_hierarchy, self.ssim_window = w_edge, w_hierarchy, ssim_window
+
+    def __call__(self, renders, targets, edge_mask=None, volume_pred=None, hierarchy_loss=None,
+                 edge_targets=None, edge_weight_override=None):
+        out = {}
+        l1, ssim_val, edge_loss = projection_losses(renders, targets, edge_mask, edge_targets)
+        if edge_mask is None:
+            edge_loss = torch.zeros((), device=renders.device)
+        out["proj_l1"] = l1
+        out["proj_ssim"] = 1.0 - ssim_val
+        if self.w_tv > 0 and volume_pred is not None:
+            try:
+                tv = tv_loss(volume_pred.squeeze())
+            except Exception:
+                tv = torch.zeros((), device=renders.device)
+        else:
+            tv = torch.zeros((), device=renders.device)
+        out["vol_tv"] = tv
+        out["edge"] = edge_loss
+        if hierarchy_loss is None:
+            hierarchy_loss = torch.zeros((), device=renders.device)
+        out["hierarchy"] = hierarchy_loss
+        edge_weight = self.w_edge if edge_weight_override is None else float(edge_weight_override)
+        out["edge_weight"] = torch.tensor(edge_weight, device=renders.device)
+        out["total"] = (self.w_l1 * l1 + self.w_ssim * out["proj_ssim"] + self.w_tv * tv
+                        + edge_weight * edge_loss + self.w_hierarchy * hierarchy_loss)
+        return out

@@ -88,6 +88,32 @@ R2S_API int r2s_densify_stats_f32(const float* grads2d, const int32_t* radii, in
                                   float* grad2d, float* count, float* max_radii,
                                   r2s_stream_t stream);
 
+/* Projection losses of the reference's BinaryTreeLossComputer
+ * (src/utils/loss.py:125-172) on C single-channel H x W images:
+ * sums[0] += sum |x - t|, sums[1] += sum of the SSIM map (11x11 Gaussian window,
+ * sigma 1.5, zero padding; src/utils/metric.py:36-56), sums[2] += sum
+ * mask |x - te| (edge terms only when edge_mask is not NULL); divide by C*H*W
+ * for the means.  When grad is not NULL it receives
+ * g_l1 d(mean l1)/dx + g_ssim d(mean ssim)/dx + g_edge d(mean edge)/dx with
+ * (g_l1, g_ssim, g_edge) read from the device array weights[3] (so an
+ * autograd backward needs no host sync).  window_size must be 11; window_1d
+ * is NULL or a host array of the 11 float32 1-D window weights as the caller's
+ * SSIM builds them (the 2-D window is their outer product).  sums is a device
+ * array of 3 doubles the caller zeroes. */
+R2S_API int r2s_projection_loss_f32(const float* renders, const float* targets,
+                                    const float* edge_targets, const float* edge_mask,
+                                    int64_t C, int64_t H, int64_t W, int window_size,
+                                    const float* window_1d, const float* weights, float* grad,
+                                    double* sums, r2s_stream_t stream);
+
+/* Volume total variation of compute_tv_loss (src/utils/loss.py:10-21) on a
+ * D0 x D1 x D2 float32 volume: *sum += sum of the absolute forward differences
+ * along the three axes (divide by their count for the "mean" reduction); when
+ * grad is not NULL it receives g_tv d(mean tv)/dv, g_tv read from the device
+ * scalar *weight. */
+R2S_API int r2s_tv_loss_f32(const float* volume, int64_t D0, int64_t D1, int64_t D2,
+                            const float* weight, float* grad, double* sum, r2s_stream_t stream);
+
 R2S_API const char* r2s_version(void);
 /* Copies the last error message of this thread into buf (NUL-terminated,
  * truncated to len-1 bytes); returns the full message length. */

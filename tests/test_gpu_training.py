@@ -99,3 +99,72 @@ def test_densify_radius_statistic():
     update_densify_state(st, info, track_radii=True)
     want = (info["radii"].float() / 512.0).amax(0)
     assert torch.equal(st["radii"], want)
+
+
+def _images(C, H, Wd, seed, smooth):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    if smooth:  # projection-like: smooth, positive, with structure
+        yy = torch.linspace(-1, 1, H, device="cuda")[:, None]
+        xx = torch.linspace(-1, 1, Wd, device="cuda")[None, :]
+        base = torch.stack([torch.exp(-((xx - 0.2 * c) ** 2 + yy ** 2) * (2 + c)) for c in range(C)])
+        r = base + 0.05 * torch.rand(C, H, Wd, generator=g, device="cuda")
+        t = base * 0.9 + 0.05 * torch.rand(C, H, Wd, generator=g, device="cuda")
+    else:
+        r = torch.rand(C, H, Wd, generator=g, device="cuda")
+        t = torch.rand(C, H, Wd, generator=g, device="cuda")
+    m = (torch.rand(C, H, Wd, generator=g, device="cuda") < 0.3).float()
+    return r[..., None], t[..., None], m[..., None]
+
+
+@pytest.mark.parametrize("smooth", [False, True])
+def test_fused_losses_match_reference_loss_computer(smooth):
+    from _helpers import rel_l2
+    from oracle import r2s_oracle as O
+    from r2splat.ops.training import FusedBinaryTreeLossComputer
+
+    C, H, Wd = 3, 70, 45  # tiles with ragged edges
+    r, t, m = _images(C, H, Wd, 8, smooth)
+    te = t * 1.1
+    g = torch.Generator(device="cuda").manual_seed(9)
+    vol = torch.rand(1, 12, 10, 9, generator=g, device="cuda")
+    w = dict(w_l1=0.8, w_ssim=0.2, w_tv=0.05, w_edge=0.3)
+    r_mine = r.clone().requires_grad_(True)
+    v_mine = vol.clone().requires_grad_(True)
+    mine = FusedBinaryTreeLossComputer(**w)(r_mine, t, m, v_mine, edge_targets=te)
+    mine["total"].backward()
+    r_ref = r.clone().requires_grad_(True)
+    v_ref = vol.clone().requires_grad_(True)
+    # the reference formulas in float32 without TF32 convolutions (cuDNN's
+    # default TF32 path alone moves the SSIM gradient by ~1e-4)
+    tf32 = torch.backends.cudnn.allow_tf32
+    torch.backends.cudnn.allow_tf32 = False
+    try:
+        ref = O.binary_tree_losses(r_ref, t, m, v_ref, edge_targets=te, **w)
+        ref["total"].backward()
+    finally:
+        torch.backends.cudnn.allow_tf32 = tf32
+    for k in ("proj_l1", "proj_ssim", "vol_tv", "edge", "total"):
+        assert abs(float(mine[k]) - float(ref[k])) <= 1e-5 * max(1e-3, abs(float(ref[k]))), k
+    assert rel_l2(r_mine.grad, r_ref.grad) < 1e-5, rel_l2(r_mine.grad, r_ref.grad)
+    assert rel_l2(v_mine.grad, v_ref.grad) < 1e-6
+
+
+def test_projection_losses_at_config_scale_against_float64():
+    """Full-size detector batch: values and gradient against the reference
+    formulas evaluated in float64."""
+    from _helpers import rel_l2
+    from oracle import r2s_oracle as O
+    from r2splat.ops.training import projection_losses
+
+    r, t, m = _images(4, 512, 512, 10, True)
+    x = r.clone().requires_grad_(True)
+    l1, ssim, edge = projection_losses(x, t, m)
+    (0.8 * l1 + 0.2 * (1 - ssim) + 0.3 * edge).backward()
+    x64 = r.double().clone().requires_grad_(True)
+    t64, m64 = t.double(), m.double()
+    ref = (0.8 * torch.abs(x64 - t64).mean()
+           + 0.2 * (1 - O.ssim2d(x64.permute(0, 3, 1, 2), t64.permute(0, 3, 1, 2)))
+           + 0.3 * (m64 * torch.abs(x64 - t64)).mean())
+    ref.backward()
+    assert abs(float(0.8 * l1 + 0.2 * (1 - ssim) + 0.3 * edge) - float(ref)) < 1e-5 * float(ref)
+    assert rel_l2(x.grad, x64.grad) < 1e-5
