@@ -438,12 +438,20 @@ def _training_inputs(cfg, dev):
 
 
 def training_rows(cfg, dev, reference: bool, reps: int = 10):
-    """Device time of one Adam step over all parameter groups and of one
-    step's densification statistics (config-sized), ours or the reference's
-    PyTorch code (torch.optim.Adam; the strategy's _update_state)."""
+    """Device time of one Adam step over all parameter groups, one step's
+    densification statistics and one loss forward+backward (config-sized),
+    ours or the reference's PyTorch code (torch.optim.Adam; the strategy's
+    _update_state; BinaryTreeLossComputer with torch's default conv settings)."""
     opts, grads2d, radii = _training_inputs(cfg, dev)
     C, N = radii.shape
     state = {"grad2d": None, "count": None, "radii": None}
+    g = torch.Generator(device=dev).manual_seed(301)
+    det, grid = cfg.detector, 64  # the 64^3 TV sub-volume of the reference trainer
+    renders = torch.rand((C, det, det, 1), generator=g, device=dev).requires_grad_(True)
+    targets = torch.rand((C, det, det, 1), generator=g, device=dev)
+    edge_mask = (torch.rand((C, det, det, 1), generator=g, device=dev) < 0.2).float()
+    vol = torch.rand((grid, grid, grid), generator=g, device=dev).requires_grad_(True)
+    weights = dict(w_l1=0.8, w_ssim=0.2, w_tv=0.05, w_edge=0.1)
     if reference:
         from oracle import r2s_oracle as O
 
@@ -454,6 +462,10 @@ def training_rows(cfg, dev, reference: bool, reps: int = 10):
         def densify():
             O.densify_state_update(state, grads2d, radii, cfg.detector, cfg.detector, C,
                                    track_radii=True)
+
+        def loss():
+            renders.grad = vol.grad = None
+            O.binary_tree_losses(renders, targets, edge_mask, vol, **weights)["total"].backward()
     else:
         from r2splat.ops import training as T
 
@@ -466,11 +478,18 @@ def training_rows(cfg, dev, reference: bool, reps: int = 10):
 
         def densify():
             T.update_densify_state(state, info, track_radii=True)
+
+        computer = T.FusedBinaryTreeLossComputer(**weights)
+
+        def loss():
+            renders.grad = vol.grad = None
+            computer(renders, targets, edge_mask, vol)["total"].backward()
     out = {}
-    for name, fn in (("adam", adam), ("densify", densify)):
+    for name, fn in (("adam", adam), ("densify", densify), ("loss_fwd_bwd", loss)):
         fn()
         out[name + "_ms"] = round(kernel_time(fn, reps), 4)
-    out["groups"] = "means [N,3], quats [N,4], scales [N,3], opacities [N]; densify [C,N] pairs"
+    out["groups"] = ("adam: means [N,3], quats [N,4], scales [N,3], opacities [N]; densify: [C,N] "
+                     "pairs; loss: L1+SSIM+edge on [C,H,W] projections + TV on a 64^3 volume")
     return out
 
 

@@ -215,6 +215,23 @@ proj_loss_kernel(const float* __restrict__ x, const float* __restrict__ t,
     block_add3(l1_sum, s_sum, edge_sum, sums);
 }
 
+// grad = g_ssim dssim + g_l1 d(mean l1)/dx + g_edge d(mean edge)/dx from a
+// stored d(mean ssim)/dx map (the same float operations as the fused kernel).
+__global__ void loss_combine_kernel(const float* __restrict__ x, const float* __restrict__ t,
+                                    const float* __restrict__ te, const float* __restrict__ mask,
+                                    const float* __restrict__ dssim,
+                                    const float* __restrict__ weights, float inv_m, int64_t n,
+                                    float* __restrict__ grad) {
+    const float g_l1 = weights[0], g_ssim = weights[1], g_edge = weights[2];
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const float xv = x[i];
+        float gv = g_ssim * dssim[i] + g_l1 * inv_m * sgnf(xv - t[i]);
+        if (mask != nullptr) gv += g_edge * inv_m * mask[i] * sgnf(xv - te[i]);
+        grad[i] = gv;
+    }
+}
+
 __global__ void tv_kernel(const float* __restrict__ v, int64_t D0, int64_t D1, int64_t D2,
                           float inv_denom, const float* __restrict__ weight,
                           float* __restrict__ grad, double* __restrict__ sum) {
@@ -311,4 +328,21 @@ extern "C" int r2s_tv_loss_f32(const float* volume, int64_t D0, int64_t D1, int6
     tv_kernel<<<(unsigned)blocks, kThreads, 0, stream>>>(volume, D0, D1, D2, (float)inv, weight,
                                                          grad, sum);
     return check_launch("tv_loss");
+}
+
+extern "C" int r2s_projection_loss_combine_f32(const float* renders, const float* targets,
+                                               const float* edge_targets, const float* edge_mask,
+                                               const float* dssim, int64_t n, const float* weights,
+                                               float* grad, r2s_stream_t stream) {
+    R2S_REQUIRE(n >= 0, "projection_loss_combine: negative size");
+    if (n == 0) return R2S_OK;
+    R2S_REQUIRE(renders && targets && dssim && weights && grad,
+                "projection_loss_combine: null pointer");
+    R2S_REQUIRE(edge_mask == nullptr || edge_targets != nullptr,
+                "projection_loss_combine: edge mask without edge targets");
+    const int64_t blocks = std::min<int64_t>((n + kThreads - 1) / kThreads, 148 * 32);
+    loss_combine_kernel<<<(unsigned)blocks, kThreads, 0, stream>>>(
+        renders, targets, edge_targets, edge_mask, dssim, weights, (float)(1.0 / double(n)), n,
+        grad);
+    return check_launch("projection_loss_combine");
 }

@@ -174,33 +174,38 @@ def _window_1d(window_size: int = 11):
 
 class _ProjectionLoss(torch.autograd.Function):
     """(l1, ssim, edge) means of one batch of projections; gradient w.r.t. the
-    renders only (the targets are data)."""
+    renders only (the targets are data).  The forward pass also stores the
+    SSIM gradient map, so the backward is one elementwise launch."""
 
     @staticmethod
     def forward(ctx, renders, targets, edge_targets, edge_mask):
         C, H, Wd = renders.shape
-        sums = torch.zeros(3, dtype=torch.float64, device=renders.device)
+        dev = renders.device
+        sums = torch.zeros(3, dtype=torch.float64, device=dev)
+        dssim = None
+        if ctx.needs_input_grad[0]:
+            dssim = torch.empty_like(renders)
+            unit = torch.tensor([0.0, 1.0, 0.0], dtype=torch.float32, device=dev)
         W._call("r2s_projection_loss_f32", W._ptr(renders), W._ptr(targets),
-                W._ptr(edge_targets), W._ptr(edge_mask), C, H, Wd, 11, _window_1d(), None, None,
-                W._ptr(sums), W._stream(renders.device))
-        ctx.save_for_backward(renders, targets, edge_targets, edge_mask)
+                W._ptr(edge_targets), W._ptr(edge_mask), C, H, Wd, 11, _window_1d(),
+                W._ptr(unit) if dssim is not None else None, W._ptr(dssim), W._ptr(sums),
+                W._stream(dev))
+        ctx.save_for_backward(renders, targets, edge_targets, edge_mask, dssim)
         means = (sums / max(1, renders.numel())).float()
         return means[0], means[1], means[2]
 
     @staticmethod
     def backward(ctx, g_l1, g_ssim, g_edge):
-        renders, targets, edge_targets, edge_mask = ctx.saved_tensors
+        renders, targets, edge_targets, edge_mask, dssim = ctx.saved_tensors
         if not ctx.needs_input_grad[0]:
             return None, None, None, None
         dev = renders.device
         weights = torch.stack([g if g is not None else torch.zeros((), device=dev)
                                for g in (g_l1, g_ssim, g_edge)]).float().contiguous()
         grad = torch.empty_like(renders)
-        sums = torch.zeros(3, dtype=torch.float64, device=dev)
-        C, H, Wd = renders.shape
-        W._call("r2s_projection_loss_f32", W._ptr(renders), W._ptr(targets),
-                W._ptr(edge_targets), W._ptr(edge_mask), C, H, Wd, 11, _window_1d(),
-                W._ptr(weights), W._ptr(grad), W._ptr(sums), W._stream(dev))
+        W._call("r2s_projection_loss_combine_f32", W._ptr(renders), W._ptr(targets),
+                W._ptr(edge_targets), W._ptr(edge_mask), W._ptr(dssim), renders.numel(),
+                W._ptr(weights), W._ptr(grad), W._stream(dev))
         return grad, None, None, None
 
 

@@ -106,6 +106,15 @@ R2S_API int r2s_projection_loss_f32(const float* renders, const float* targets,
                                     const float* window_1d, const float* weights, float* grad,
                                     double* sums, r2s_stream_t stream);
 
+/* grad = g_l1 d(mean l1)/dx + g_ssim dssim + g_edge d(mean edge)/dx over n
+ * pixels, where dssim is the map r2s_projection_loss_f32 wrote with weights
+ * (0, 1, 0) and (g_l1, g_ssim, g_edge) is the device array weights[3]: the
+ * backward of a loss whose SSIM gradient was computed in the forward pass. */
+R2S_API int r2s_projection_loss_combine_f32(const float* renders, const float* targets,
+                                            const float* edge_targets, const float* edge_mask,
+                                            const float* dssim, int64_t n, const float* weights,
+                                            float* grad, r2s_stream_t stream);
+
 /* Volume total variation of compute_tv_loss (src/utils/loss.py:10-21) on a
  * D0 x D1 x D2 float32 volume: *sum += sum of the absolute forward differences
  * along the three axes (divide by their count for the "mean" reduction); when

@@ -144,7 +144,8 @@ def test_fused_losses_match_reference_loss_computer(smooth):
     finally:
         torch.backends.cudnn.allow_tf32 = tf32
     for k in ("proj_l1", "proj_ssim", "vol_tv", "edge", "total"):
-        assert abs(float(mine[k]) - float(ref[k])) <= 1e-5 * max(1e-3, abs(float(ref[k]))), k
+        a, b = float(mine[k].detach()), float(ref[k].detach())
+        assert abs(a - b) <= 1e-5 * max(1e-3, abs(b)), k
     assert rel_l2(r_mine.grad, r_ref.grad) < 1e-5, rel_l2(r_mine.grad, r_ref.grad)
     assert rel_l2(v_mine.grad, v_ref.grad) < 1e-6
 
