@@ -13,9 +13,10 @@ interchangeable.
 * ``update_densify_state(state, info, ...)`` -- the strategy's per-step
   statistics (``BinaryTreeStrategy._update_state``,
   src/strategies/binary_tree.py:305-347, non-packed path) in one launch.
-* ``FusedBinaryTreeLossComputer`` -- the trainer's loss
-  (``BinaryTreeLossComputer``, src/utils/loss.py:125-172): L1, SSIM and
-  edge terms of the projections in one kernel each way, volume TV in one.
+* ``FusedBinaryTreeLossComputer`` / ``FusedLossComputer`` -- the trainers'
+  losses (``BinaryTreeLossComputer``, src/utils/loss.py:125-172;
+  ``LossComputer``, loss.py:72-109): L1, SSIM and edge terms of the
+  projections in one kernel each way, volume TV in one.
 """
 from __future__ import annotations
 
@@ -27,8 +28,8 @@ import torch
 from ..cuda import _wrapper as W
 from ..cuda._backend import AdamGroup
 
-__all__ = ["FusedBinaryTreeLossComputer", "adam_step", "projection_losses", "tv_loss",
-           "update_densify_state"]
+__all__ = ["FusedBinaryTreeLossComputer", "FusedLossComputer", "adam_step", "projection_losses",
+           "tv_loss", "update_densify_state"]
 
 _MAX_GROUPS = 8
 
@@ -296,4 +297,30 @@ class FusedBinaryTreeLossComputer:
         out["edge_weight"] = torch.tensor(edge_weight, device=renders.device)
         out["total"] = (self.w_l1 * l1 + self.w_ssim * out["proj_ssim"] + self.w_tv * tv
                         + edge_weight * edge_loss + self.w_hierarchy * hierarchy_loss)
+        return out
+
+
+class FusedLossComputer:
+    """Drop-in for the reference's LossComputer (src/utils/loss.py:72-109):
+    weighted projection L1 + SSIM and volume TV, from the fused kernels."""
+
+    def __init__(self, w_l1: float, w_ssim: float, w_tv: float, ssim_window: int = 11):
+        if ssim_window != 11:
+            raise ValueError("the fused losses are built for the 11-pixel SSIM window")
+        self.w_l1, self.w_ssim, self.w_tv, self.ssim_window = w_l1, w_ssim, w_tv, ssim_window
+
+    def __call__(self, renders, targets, volume_pred=None):
+        out = {}
+        l1, ssim_val, _ = projection_losses(renders, targets)
+        out["proj_l1"] = l1
+        out["proj_ssim"] = 1.0 - ssim_val
+        if self.w_tv > 0 and volume_pred is not None:
+            try:
+                tv = tv_loss(volume_pred.squeeze())
+            except Exception:
+                tv = torch.zeros((), device=renders.device)
+        else:
+            tv = torch.zeros((), device=renders.device)
+        out["vol_tv"] = tv
+        out["total"] = self.w_l1 * l1 + self.w_ssim * out["proj_ssim"] + self.w_tv * tv
         return out

@@ -169,3 +169,23 @@ def test_projection_losses_at_config_scale_against_float64():
     ref.backward()
     assert abs(float(0.8 * l1 + 0.2 * (1 - ssim) + 0.3 * edge) - float(ref)) < 1e-5 * float(ref)
     assert rel_l2(x.grad, x64.grad) < 1e-5
+
+
+def test_fused_plain_loss_computer_matches_reference():
+    from _helpers import rel_l2
+    from oracle import r2s_oracle as O
+    from r2splat.ops.training import FusedLossComputer
+
+    r, t, _ = _images(2, 40, 52, 12, True)
+    vol = torch.rand(10, 11, 12, device="cuda")
+    w = dict(w_l1=0.7, w_ssim=0.3, w_tv=0.1)
+    x1, v1 = r.clone().requires_grad_(True), vol.clone().requires_grad_(True)
+    FusedLossComputer(**w)(x1, t, v1)["total"].backward()
+    x2, v2 = r.clone().requires_grad_(True), vol.clone().requires_grad_(True)
+    tf32 = torch.backends.cudnn.allow_tf32
+    torch.backends.cudnn.allow_tf32 = False
+    try:
+        O.plain_losses(x2, t, v2, **w)["total"].backward()
+    finally:
+        torch.backends.cudnn.allow_tf32 = tf32
+    assert rel_l2(x1.grad, x2.grad) < 1e-5 and rel_l2(v1.grad, v2.grad) < 1e-6
