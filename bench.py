@@ -299,6 +299,215 @@ class RefVoxel:
 
 
 # ---------------------------------------------------------------------------
+# config 4: the training step (projection + TV sub-volume + losses + Adam)
+# ---------------------------------------------------------------------------
+TRAIN_VIEWS_PER_STEP = 8
+TRAIN_POOL = 32          # orbit views with seeded synthetic targets
+TRAIN_TV = 64            # edge of the random TV sub-volume (voxels)
+TRAIN_GRID = 256         # full-grid resolution that fixes the sub-volume's voxel size
+TRAIN_WEIGHTS = dict(w_l1=0.8, w_ssim=0.2, w_tv=0.05, w_edge=0.1)
+TRAIN_LRS = {"means": 1.6e-4, "quats": 1e-3, "scales": 5e-3, "opacities": 5e-2}
+
+
+class TrainData:
+    """Seeded synthetic data of the training step: a pool of orbit views with
+    target projections of a teacher Gaussian set and edge masks, the per-step
+    view choice and the per-step TV sub-box (default.py:444-470 restated:
+    a box of TRAIN_TV voxels of a TRAIN_GRID^3 grid over the unit cube, centre
+    uniform in the valid range)."""
+
+    def __init__(self, cfg, dev, render_targets):
+        self.det = cfg.detector
+        vm, K = wl.make_cameras(TRAIN_POOL, cfg.detector)
+        self.vm, self.K = vm.to(dev), K.to(dev)
+        self.targets = render_targets(self.vm, self.K)  # [P, H, W]
+        g = torch.Generator(device=dev).manual_seed(401)
+        self.edge = (torch.rand(self.targets.shape, generator=g, device=dev) < 0.2).float()
+        self.box = TRAIN_TV / TRAIN_GRID
+
+    def step_views(self, step, rank, world):
+        g = torch.Generator().manual_seed(1000 + step)
+        views = torch.randperm(TRAIN_POOL, generator=g)[:TRAIN_VIEWS_PER_STEP]
+        per = (TRAIN_VIEWS_PER_STEP + world - 1) // world
+        return views[rank * per:(rank + 1) * per]
+
+    def step_box(self, step, dev):
+        g = torch.Generator().manual_seed(2000 + step)
+        half = self.box / 2
+        center = (-0.5 + half) + (1.0 - 2 * half) * torch.rand(3, generator=g, dtype=torch.float64)
+        return (torch.full((3,), self.box, dtype=torch.float32, device=dev),
+                center.float().to(dev))
+
+
+def _teacher(cfg):
+    import dataclasses
+
+    return wl.make_gaussians(dataclasses.replace(cfg, seed=cfg.seed + 40), n=200_000)
+
+
+class OursTrain:
+    def __init__(self, cfg, world, rank, dev):
+        from r2splat.ops import explicit as E
+        from r2splat.ops import training as T
+
+        self.E, self.T = E, T
+        self.cfg, self.world, self.rank, self.dev = cfg, world, rank, dev
+        tm, tq, ts, to = (t.to(dev) for t in _teacher(cfg))
+
+        def render(vm, K):
+            with torch.no_grad():
+                st = E.prepare_explicit_gaussians(tq, ts, to, scale_min=wl.SCALE_MIN,
+                                                  scale_max=wl.SCALE_MAX)
+                return E.explicit_rasterize(st, tm, vm, K, img_w=cfg.detector,
+                                            img_h=cfg.detector, tile_size=wl.IMG_TILE,
+                                            eps2d=wl.EPS2D, radius_clip=wl.RADIUS_CLIP,
+                                            absgrad=False).image.detach().clone()
+
+        self.data = TrainData(cfg, dev, render)
+        m, q, s, o = wl.make_gaussians(cfg)
+        self.params = {k: torch.nn.Parameter(t.to(dev)) for k, t in
+                       zip(("means", "quats", "scales", "opacities"), (m, q, s, o))}
+        self.opts = {k: torch.optim.Adam([{"params": p, "name": k}], lr=TRAIN_LRS[k], eps=1e-15)
+                     for k, p in self.params.items()}
+        self.loss = T.FusedBinaryTreeLossComputer(**TRAIN_WEIGHTS)
+        self.densify = {"grad2d": None, "count": None}
+        self.allreduce = shard.GradientAllReduce()
+        self.step_no = 0
+
+    def step(self):
+        E, T, d, P = self.E, self.T, self.data, self.params
+        views = d.step_views(self.step_no, self.rank, self.world).to(self.dev)
+        rng, ctr = d.step_box(self.step_no, self.dev)
+        self.step_no += 1
+        st = E.prepare_explicit_gaussians(P["quats"], P["scales"], P["opacities"],
+                                          scale_min=wl.SCALE_MIN, scale_max=wl.SCALE_MAX)
+        res = E.explicit_rasterize(st, P["means"], d.vm[views], d.K[views], img_w=d.det,
+                                   img_h=d.det, tile_size=wl.IMG_TILE, eps2d=wl.EPS2D,
+                                   radius_clip=wl.RADIUS_CLIP, absgrad=True)
+        vox = E.explicit_voxelize(st, P["means"], rng, ctr, dim2=TRAIN_TV, dim1=TRAIN_TV,
+                                  dim0=TRAIN_TV, tile_size=wl.VOL_TILE, eps3d=wl.EPS3D,
+                                  radius_clip=wl.RADIUS_CLIP)
+        out = self.loss(res.image[..., None], d.targets[views][..., None],
+                        d.edge[views][..., None], vox.volume)
+        out["total"].backward()
+        E.explicit_backward(st, P["means"], P["quats"], P["scales"], P["opacities"])
+        if self.world > 1:
+            self.allreduce([p.grad for p in P.values()])
+        info = {"means2d": res.means2d, "radii": res.radii.amax(dim=-1), "width": d.det,
+                "height": d.det, "n_cameras": len(views)}
+        T.update_densify_state(self.densify, info, absgrad=True)
+        T.adam_step(self.opts)
+        for o in self.opts.values():
+            o.zero_grad(set_to_none=True)
+        return out["total"]
+
+
+class RefTrain:
+    """The same step through the reference's kernels (oracle/_ref in its op
+    layer's order) and its PyTorch code: BinaryTreeLossComputer with autograd,
+    the strategy's _update_state, torch.optim.Adam."""
+
+    def __init__(self, cfg, dev):
+        from oracle import r2s_oracle as O
+        from oracle.ref_harness import ReferencePipeline
+
+        self.O, self.ref, self.cfg, self.dev = O, ReferencePipeline(), cfg, dev
+        tm, tq, ts, to = (t.to(dev) for t in _teacher(cfg))
+
+        def render(vm, K):
+            cov, ms, op = self.ref.prepare(tq, ts, to, wl.SCALE_MIN, wl.SCALE_MAX)
+            return self.ref.rasterize_forward(tm, cov, op, vm, K, cfg.detector, cfg.detector,
+                                              wl.IMG_TILE, wl.EPS2D, wl.RADIUS_CLIP)["output"]
+
+        self.data = TrainData(cfg, dev, render)
+        m, q, s, o = wl.make_gaussians(cfg)
+        self.params = {k: torch.nn.Parameter(t.to(dev)) for k, t in
+                       zip(("means", "quats", "scales", "opacities"), (m, q, s, o))}
+        self.opts = {k: torch.optim.Adam([{"params": p, "name": k}], lr=TRAIN_LRS[k], eps=1e-15)
+                     for k, p in self.params.items()}
+        self.densify = {"grad2d": None, "count": None}
+        self.step_no = 0
+
+    def step(self):
+        d, P, R, O = self.data, self.params, self.ref, self.O
+        views = d.step_views(self.step_no, 0, 1).to(self.dev)
+        rng, ctr = d.step_box(self.step_no, self.dev)
+        self.step_no += 1
+        m, q, s, o = (P[k].detach() for k in ("means", "quats", "scales", "opacities"))
+        cov, ms, op = R.prepare(q, s, o, wl.SCALE_MIN, wl.SCALE_MAX)
+        p = R.rasterize_forward(m, cov, op, d.vm[views], d.K[views], d.det, d.det, wl.IMG_TILE,
+                                wl.EPS2D, wl.RADIUS_CLIP)
+        v = R.voxelize_forward(m, cov, ms, op, rng, ctr, TRAIN_TV, TRAIN_TV, TRAIN_TV,
+                               wl.VOL_TILE, wl.EPS3D, wl.RADIUS_CLIP)
+        image = p["output"].detach().requires_grad_(True)
+        volume = v["output"].detach().requires_grad_(True)
+        out = O.binary_tree_losses(image[..., None], d.targets[views][..., None],
+                                   d.edge[views][..., None], volume, **TRAIN_WEIGHTS)
+        out["total"].backward()
+        g = R.explicit_backward(p, image.grad, v, volume.grad, m, q, s, o, cov, op,
+                                wl.SCALE_MIN, wl.SCALE_MAX, absgrad=True)
+        for k, gk in (("means", "means"), ("quats", "quats"), ("scales", "scales"),
+                      ("opacities", "opacities")):
+            P[k].grad = g[gk]
+        O.densify_state_update(self.densify, g["means2d_abs"], p["radii"].amax(dim=-1), d.det,
+                               d.det, len(views))
+        for opt in self.opts.values():
+            opt.step()
+            opt.zero_grad(set_to_none=True)
+        return out["total"]
+
+
+def run_train_bench(args, cfg, dev, world, rank, local, flush):
+    """Config 4: whole-job Gaussian*views/s of the training step (8 views per
+    step in total, split over the GPUs: strong scaling)."""
+    ref = args.impl == "reference"
+    if ref:
+        try:
+            from oracle.ref_harness import reference_available
+
+            if not reference_available():
+                print(json.dumps({"impl": "reference", "unavailable":
+                                  "reference sm_100a build oracle/_ref missing"}))
+                return
+            trainer = RefTrain(cfg, dev)
+        except Exception as exc:
+            print(json.dumps({"impl": "reference", "unavailable": f"{type(exc).__name__}: {exc}"}))
+            return
+    else:
+        trainer = OursTrain(cfg, world, rank, dev)
+    with ClockSampler(local) as clk:
+        ms = time_steps(trainer.step, args.steps, args.warmup, 1 if ref else world, flush)
+    if rank != 0:
+        return
+    value = cfg.n_gaussians * TRAIN_VIEWS_PER_STEP / (ms * 1e-3)
+    line = {
+        "metric": "Gaussian*views/s training step (config 4)",
+        "value": round(value, 1), "unit": "Gaussian*views/s", "n_gpus": 1 if ref else world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded teacher projections, random edge masks, r2s_workloads)",
+        "config": {"workload": cfg.name, "n_gaussians": cfg.n_gaussians,
+                   "views_per_step": TRAIN_VIEWS_PER_STEP, "detector": cfg.detector,
+                   "tv_subvolume": TRAIN_TV, "loss": TRAIN_WEIGHTS,
+                   "step": "prepare + rasterize + 64^3 voxelize + L1/SSIM/edge/TV losses + "
+                           "backward + grad all-reduce + densify stats + Adam",
+                   "split": "binary split every 100 steps lies outside the timed window",
+                   "l2": "256MiB flush between steps"},
+        "clocks": clk.summary(),
+    }
+    if ref:
+        line["impl"] = "reference"
+        line["e2e"] = {"value": round(value, 1), "unit": "Gaussian*views/s",
+                       "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+        line["cpu_baseline"] = {"value": round(value, 1), "unit": "Gaussian*views/s", "cores": 0,
+                                "kind": "reference",
+                                "sample": "the reference's CUDA build and PyTorch code on GPU 0"}
+    else:
+        line["gpu_launches"] = args.steps * 22
+    print(json.dumps(line))
+
+
+# ---------------------------------------------------------------------------
 # timing helpers
 # ---------------------------------------------------------------------------
 def time_steps(fn, steps, warmup, world, flush):
@@ -546,6 +755,9 @@ def main():
                                   name=f"{cfg.name}-views{args.views}")
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     hbm_peak, peak_kind = _peaks()
+    if args.config == 4:
+        run_train_bench(args, cfg, dev, world, rank, local, flush)
+        return
 
     if args.impl == "reference":
         try:

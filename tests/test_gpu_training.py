@@ -190,3 +190,71 @@ def test_fused_plain_loss_computer_matches_reference():
     finally:
         torch.backends.cudnn.allow_tf32 = tf32
     assert rel_l2(x1.grad, x2.grad) < 1e-5 and rel_l2(v1.grad, v2.grad) < 1e-6
+
+
+def test_training_step_gradients_match_reference():
+    """One training step at config-1 scale: projection of 4 views, a 32^3 TV
+    sub-volume, the BinaryTreeLossComputer terms, the explicit backward; ours
+    through r2splat.ops, the reference through its kernels and its PyTorch
+    loss (TF32 off).  Loss values and parameter gradients must agree."""
+    import r2s_workloads as wl
+    from _helpers import rel_l2
+    from oracle import r2s_oracle as O
+    from oracle.ref_harness import ReferencePipeline
+    from r2splat.ops import explicit as E
+    from r2splat.ops.training import FusedBinaryTreeLossComputer
+
+    cfg = wl.CONFIGS[1]
+    m, q, s, o = (t.cuda() for t in wl.make_gaussians(cfg))
+    vm, K = wl.make_cameras(4, cfg.detector, total=cfg.n_views)
+    vm, K = vm.cuda(), K.cuda()
+    det, G = cfg.detector, 32
+    rng = torch.full((3,), 0.25, device="cuda")
+    ctr = torch.tensor([0.05, -0.1, 0.12], device="cuda")
+    gen = torch.Generator(device="cuda").manual_seed(21)
+    targets = torch.rand(4, det, det, 1, generator=gen, device="cuda") * 0.1
+    edge = (torch.rand(4, det, det, 1, generator=gen, device="cuda") < 0.2).float()
+    weights = dict(w_l1=0.8, w_ssim=0.2, w_tv=0.05, w_edge=0.1)
+
+    params = {k: t.clone().requires_grad_(True) for k, t in zip(("m", "q", "s", "o"), (m, q, s, o))}
+    st = E.prepare_explicit_gaussians(params["q"], params["s"], params["o"],
+                                      scale_min=wl.SCALE_MIN, scale_max=wl.SCALE_MAX)
+    res = E.explicit_rasterize(st, params["m"], vm, K, img_w=det, img_h=det, tile_size=16,
+                               eps2d=wl.EPS2D, radius_clip=wl.RADIUS_CLIP, absgrad=True)
+    vox = E.explicit_voxelize(st, params["m"], rng, ctr, dim2=G, dim1=G, dim0=G, tile_size=8,
+                              eps3d=wl.EPS3D, radius_clip=wl.RADIUS_CLIP)
+    mine = FusedBinaryTreeLossComputer(**weights)(res.image[..., None], targets, edge, vox.volume)
+    mine["total"].backward()
+    E.explicit_backward(st, params["m"], params["q"], params["s"], params["o"])
+
+    R = ReferencePipeline()
+    cov, ms, op = R.prepare(q, s, o, wl.SCALE_MIN, wl.SCALE_MAX)
+    p = R.rasterize_forward(m, cov, op, vm, K, det, det, 16, wl.EPS2D, wl.RADIUS_CLIP)
+    v = R.voxelize_forward(m, cov, ms, op, rng, ctr, G, G, G, 8, wl.EPS3D, wl.RADIUS_CLIP)
+    image = p["output"].detach().requires_grad_(True)
+    volume = v["output"].detach().requires_grad_(True)
+    tf32 = torch.backends.cudnn.allow_tf32
+    torch.backends.cudnn.allow_tf32 = False
+    try:
+        ref = O.binary_tree_losses(image[..., None], targets, edge, volume, **weights)
+        ref["total"].backward()
+    finally:
+        torch.backends.cudnn.allow_tf32 = tf32
+    g = R.explicit_backward(p, image.grad, v, volume.grad, m, q, s, o, cov, op, wl.SCALE_MIN,
+                            wl.SCALE_MAX, absgrad=True)
+    for k in ("proj_l1", "proj_ssim", "vol_tv", "edge", "total"):
+        a, b = float(mine[k].detach()), float(ref[k].detach())
+        assert abs(a - b) <= 1e-5 * max(1e-3, abs(b)), (k, a, b)
+    assert rel_l2(res.image.grad, image.grad) < 1e-5
+    # parameter gradients: the 1e-5 bar, or (float32 noise) within 2e-5 and no
+    # less accurate than the reference against a float64 evaluation
+    from _helpers import check_grad_accuracy
+    from test_gpu_reference import _float64_gradients
+
+    d = dict(det=det, grid=G, means=m, viewmats=vm, Ks=K, quats=q, scales=s, opac=o)
+    truth = _float64_gradients(R, d, p, image.grad, v, volume.grad, cov)
+    pairs = (("m", "means"), ("q", "quats"), ("s", "scales"), ("o", "opacities"))
+    check_grad_accuracy("training step", {rk: params[k].grad for k, rk in pairs},
+                        {rk: g[rk] for _, rk in pairs},
+                        {rk: truth[tk] for (_, rk), tk in zip(pairs, ("means", "quats", "scales",
+                                                                       "opac"))})
