@@ -646,9 +646,10 @@ def fused_project(means, covars, opacities, viewmats, Ks, W, H, tile, ntx, nty, 
     return means2d, radii, splats, rects, counts
 
 
-def fused_bin(rects, S, N, T, tiles_x, layered, want_keys=False, segment_base=0):
+def fused_bin(rects, S, N, T, tiles_x, layered, want_keys=False, segment_base=0, limit=None):
     """Binning from precomputed rectangles -> (tile_offsets [S*T], flatten_ids,
-    isect_ids or None)."""
+    isect_ids or None).  With ``limit``, returns None instead when the record
+    count exceeds it (the caller then bins in smaller batches)."""
     dev = rects.device
     st = _stream(dev)
     ws = _bin_workspace(dev, S, N, T, layered)
@@ -657,6 +658,8 @@ def fused_bin(rects, S, N, T, tiles_x, layered, want_keys=False, segment_base=0)
     _call("r2s_bin_prepare", _ptr(rects), S, N, T, tiles_x, layered, segment_base, _ptr(ws),
           ws.numel(), _ptr(offsets), _ptr(n_dev), st)
     n = _read_count(n_dev)
+    if limit is not None and n > limit:
+        return None
     flatten_ids = torch.empty((n,), dtype=torch.int32, device=dev)
     isect_ids = torch.empty((n,), dtype=torch.int64, device=dev) if want_keys else None
     if n:
@@ -665,21 +668,48 @@ def fused_bin(rects, S, N, T, tiles_x, layered, want_keys=False, segment_base=0)
     return offsets[: S * T], flatten_ids, isect_ids
 
 
-def fused_raster_fwd(splats, offsets, flatten_ids, C, N, W, H, tile, ntx, nty):
+def fused_raster_fwd(splats, offsets, flatten_ids, C, N, W, H, tile, ntx, nty, out=None):
     dev = splats.device
-    out = torch.empty((C, H, W), dtype=torch.float32, device=dev)
+    if out is None:
+        out = torch.empty((C, H, W), dtype=torch.float32, device=dev)
     _call("r2s_raster_splats_fwd_f32", _ptr(splats), _ptr(offsets), _ptr(flatten_ids), C, N,
           flatten_ids.numel(), W, H, tile, ntx, nty, _ptr(out), _stream(dev))
     return out
 
 
-def fused_raster_bwd(splats, offsets, flatten_ids, v_image, C, N, W, H, tile, ntx, nty, with_abs):
+def fused_raster_bwd(splats, offsets, flatten_ids, v_image, C, N, W, H, tile, ntx, nty, with_abs,
+                     out=None):
     dev = splats.device
-    stats = torch.empty((C * N, 8), dtype=torch.float32, device=dev)
+    stats = torch.empty((C * N, 8), dtype=torch.float32, device=dev) if out is None else out
     _call("r2s_raster_splats_bwd_f32", _ptr(splats), _ptr(offsets), _ptr(flatten_ids),
           _ptr(v_image), C, N, flatten_ids.numel(), W, H, tile, ntx, nty, 1 if with_abs else 0,
           _ptr(stats), _stream(dev))
     return stats
+
+
+# Largest number of intersection records one binning holds: tile offsets and
+# flatten ids are int32, as in the reference (IsectTiles.cpp:95-107).
+MAX_RECORDS_PER_BATCH = 2 ** 31 - 1
+
+
+def plan_view_batches(rects, C, N, max_records=None):
+    """Contiguous view ranges [(c0, c1)] whose records each fit one binning
+    (views of more records than the limit get a batch of their own, which the
+    binning then rejects).  rects: the [C*N] packed tile rectangles."""
+    limit = MAX_RECORDS_PER_BATCH if max_records is None else int(max_records)
+    r = rects.view(torch.int32).view(C, N, 2).to(torch.int64) & 0xFFFFFFFF
+    w = ((r[..., 0] >> 16) - (r[..., 0] & 0xFFFF)).clamp_min(0)
+    h = ((r[..., 1] >> 16) - (r[..., 1] & 0xFFFF)).clamp_min(0)
+    per_view = (w * h).sum(dim=1).tolist()
+    batches, c0, acc = [], 0, 0
+    for c, n in enumerate(per_view):
+        if c > c0 and acc + n > limit:
+            batches.append((c0, c))
+            c0, acc = c, 0
+        acc += n
+    if C > c0:
+        batches.append((c0, C))
+    return batches
 
 
 def fused_map(means, covars, opacities, ranges, centers, dim2, dim1, dim0, tile, nt2, nt1, nt0,

@@ -65,6 +65,10 @@ class ProjectionForwardBuffers:
     tile_size: int
     eps2d: float
     splats: Optional[torch.Tensor] = None
+    # float32 with more intersection records than one int32 binning holds:
+    # [(c0, c1, flatten_ids)] per contiguous view batch; the batch's rows of
+    # tile_offsets index its own flatten_ids (flatten_ids above is then empty)
+    view_batches: Optional[list] = None
     cov2d: Optional[torch.Tensor] = None
     conics: Optional[torch.Tensor] = None
     mus: Optional[torch.Tensor] = None
@@ -185,14 +189,42 @@ def _rasterize_forward(
             means2d, radii, splats, rects, _ = W.fused_project(
                 means_c, covars_c, opac, viewmats_c, Ks_c, img_w, img_h, tile_size, ntx, nty,
                 eps2d, radius_clip)
-            offsets, flatten_ids, _ = W.fused_bin(rects, n_cameras, N, ntx * nty, ntx, 0)
-            tile_offsets = offsets.view(n_cameras, nty, ntx)
-            output = W.fused_raster_fwd(splats, tile_offsets, flatten_ids, n_cameras, N, img_w,
-                                        img_h, tile_size, ntx, nty)
+            T = ntx * nty
+            limit = W.MAX_RECORDS_PER_BATCH if n_cameras > 1 else None
+            binned = W.fused_bin(rects, n_cameras, N, T, ntx, 0, limit=limit)
+            if binned is not None:
+                offsets, flatten_ids, _ = binned
+                tile_offsets = offsets.view(n_cameras, nty, ntx)
+                output = W.fused_raster_fwd(splats, tile_offsets, flatten_ids, n_cameras, N,
+                                            img_w, img_h, tile_size, ntx, nty)
+                view_batches = None
+            else:
+                # more records than one int32 binning holds: bin and rasterize
+                # in contiguous view batches
+                batches = W.plan_view_batches(rects, n_cameras, N, W.MAX_RECORDS_PER_BATCH)
+                tile_offsets = torch.empty((n_cameras, nty, ntx), dtype=torch.int32,
+                                           device=means_c.device)
+                output = torch.empty((n_cameras, img_h, img_w), dtype=torch.float32,
+                                     device=means_c.device)
+                view_batches = []
+                for c0, c1 in batches:
+                    rb = rects[c0 * N * 8:c1 * N * 8]
+                    binned = W.fused_bin(rb, c1 - c0, N, T, ntx, 0,
+                                         limit=W.MAX_RECORDS_PER_BATCH)
+                    if binned is None:
+                        raise RuntimeError(
+                            f"view {c0} alone holds more than {W.MAX_RECORDS_PER_BATCH} "
+                            "intersection records (int32 tile offsets)")
+                    offs_b, ids_b, _ = binned
+                    tile_offsets[c0:c1] = offs_b.view(c1 - c0, nty, ntx)
+                    W.fused_raster_fwd(splats[c0:c1], tile_offsets[c0:c1], ids_b, c1 - c0, N,
+                                       img_w, img_h, tile_size, ntx, nty, out=output[c0:c1])
+                    view_batches.append((c0, c1, ids_b))
+                flatten_ids = torch.empty((0,), dtype=torch.int32, device=means_c.device)
         return ProjectionForwardBuffers(
             output=output, means2d=means2d, radii=radii, tile_offsets=tile_offsets,
             flatten_ids=flatten_ids, viewmats=viewmats_c, Ks=Ks_c, img_w=img_w, img_h=img_h,
-            tile_size=tile_size, eps2d=float(eps2d), splats=splats)
+            tile_size=tile_size, eps2d=float(eps2d), splats=splats, view_batches=view_batches)
 
     # reference operator chain (r2splat/ops/direct.py:166-201)
     means2d, cov2d, radii = W.world_to_image_projection_fwd(

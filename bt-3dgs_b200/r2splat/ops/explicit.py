@@ -191,9 +191,18 @@ def _explicit_backward_fused(state, means, quats, raw_scales, raw_opacities) -> 
         v_image = proj.output.grad
         raster_stats = None
         if v_image is not None:
-            raster_stats = W.fused_raster_bwd(
-                pb.splats, pb.tile_offsets, pb.flatten_ids, v_image.contiguous(), C, N, pb.img_w,
-                pb.img_h, pb.tile_size, ntx, nty, proj.absgrad)
+            v_image = v_image.contiguous()
+            if pb.view_batches is None:
+                raster_stats = W.fused_raster_bwd(
+                    pb.splats, pb.tile_offsets, pb.flatten_ids, v_image, C, N, pb.img_w,
+                    pb.img_h, pb.tile_size, ntx, nty, proj.absgrad)
+            else:
+                raster_stats = torch.empty((C * N, 8), dtype=torch.float32, device=dev)
+                for c0, c1, ids_b in pb.view_batches:
+                    W.fused_raster_bwd(pb.splats[c0:c1], pb.tile_offsets[c0:c1], ids_b,
+                                       v_image[c0:c1], c1 - c0, N, pb.img_w, pb.img_h,
+                                       pb.tile_size, ntx, nty, proj.absgrad,
+                                       out=raster_stats[c0 * N:c1 * N])
             v_means2d = torch.empty((C, N, 2), dtype=torch.float32, device=dev)
             v_means2d_abs = (torch.empty((C, N, 2), dtype=torch.float32, device=dev)
                              if proj.absgrad else None)

@@ -125,3 +125,41 @@ def test_large_footprints(ref):
     s = wl.inverse_scale(wide).float().cuda()
     out = _run_both(ref, m, q, s, o, vm, K, 128, 128, 24)
     _check(*out)
+
+
+def test_view_batches_beyond_the_record_limit(monkeypatch):
+    """When the intersection records of all views pass the int32 limit of one
+    binning, the float32 path bins and rasterizes in view batches; forced here
+    with a small limit, the image and gradients equal the single-batch run."""
+    import r2s_workloads as wl
+    from r2splat.cuda import _wrapper as W
+    from r2splat.ops import explicit as E
+
+    cfg = wl.CONFIGS[1]
+    m, q, s, o = (t.cuda() for t in wl.make_gaussians(cfg, n=20000))
+    vm, K = wl.make_cameras(6, 128, total=6)
+    vm, K = vm.cuda(), K.cuda()
+    g = torch.Generator(device="cuda").manual_seed(4)
+    v_img = torch.randn((6, 128, 128), generator=g, device="cuda")
+
+    def run():
+        params = [t.clone().requires_grad_(True) for t in (m, q, s, o)]
+        st = E.prepare_explicit_gaussians(params[1], params[2], params[3],
+                                          scale_min=wl.SCALE_MIN, scale_max=wl.SCALE_MAX)
+        res = E.explicit_rasterize(st, params[0], vm, K, img_w=128, img_h=128, tile_size=16,
+                                   eps2d=wl.EPS2D, radius_clip=wl.RADIUS_CLIP, absgrad=True)
+        (res.image * v_img).sum().backward()
+        E.explicit_backward(st, *params)
+        return st, res, params
+
+    st1, res1, p1 = run()
+    n = st1.projection.buffers.flatten_ids.numel()
+    monkeypatch.setattr(W, "MAX_RECORDS_PER_BATCH", n // 4)
+    st2, res2, p2 = run()
+    batches = st2.projection.buffers.view_batches
+    assert batches is not None and len(batches) >= 4
+    assert sum(ids.numel() for _, _, ids in batches) == n
+    assert torch.equal(res2.image, res1.image)
+    for a, b in zip(p2, p1):
+        assert rel_l2(a.grad, b.grad) < 1e-6
+    assert rel_l2(res2.means2d.absgrad, res1.means2d.absgrad) < 1e-6
