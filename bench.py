@@ -217,10 +217,19 @@ class OursVoxel:
         self.world = world
         self.G = cfg.grid
         self.nt = (self.G + wl.VOL_TILE - 1) // wl.VOL_TILE
-        self.l0, self.l1 = shard.layer_range(self.nt, rank, world)
         self.params = params
         rng, ctr = wl.unit_cube_box()
         self.rng, self.ctr = rng.to(dev), ctr.to(dev)
+        # z-slabs balanced by records per brick layer (every rank computes the
+        # same ranges from the same mapping)
+        with torch.no_grad():
+            m, q, s, o = params
+            cov, _, op = W.fused_prepare(q, s, o, wl.SCALE_MIN, wl.SCALE_MAX)
+            rects = W.fused_map(m, cov, op, self.rng, self.ctr, self.G, self.G, self.G,
+                                wl.VOL_TILE, self.nt, self.nt, self.nt, wl.EPS3D,
+                                wl.RADIUS_CLIP)[4]
+        self.l0, self.l1 = shard.balanced_layer_ranges(shard.layer_weights(rects, self.nt),
+                                                       world)[rank]
         z0, z1 = shard.slab_rows(self.l0, self.l1, wl.VOL_TILE, self.G)
         g = torch.Generator(device=dev).manual_seed(200 + rank)
         self.v_vol = torch.randn((z1 - z0, self.G, self.G), generator=g, device=dev)

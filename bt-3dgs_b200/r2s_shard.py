@@ -32,6 +32,58 @@ def layer_range(n_layers: int, rank: int, world: int) -> Tuple[int, int]:
     return l0, min(n_layers, l0 + per)
 
 
+def balanced_layer_ranges(weights: Sequence[float], world: int) -> List[Tuple[int, int]]:
+    """Contiguous brick-layer ranges, one per rank, minimizing the largest
+    total weight (records per layer) of any rank: binary search on that
+    maximum with greedy packing as the feasibility test.  Deterministic: every
+    rank computes the same ranges from the same weights."""
+    n = len(weights)
+    if world < 1:
+        raise ValueError("world must be positive")
+    w = [max(0.0, float(x)) for x in weights]
+    total = sum(w)
+    if total <= 0.0:
+        return [layer_range(n, r, world) for r in range(world)]
+
+    def pack(cap):
+        ranges, start, acc = [], 0, 0.0
+        for i, x in enumerate(w):
+            if acc + x > cap and i > start:
+                ranges.append((start, i))
+                start, acc = i, 0.0
+            acc += x
+        ranges.append((start, n))
+        return ranges
+
+    lo, hi = max(w), total
+    for _ in range(60):
+        mid = 0.5 * (lo + hi)
+        if len(pack(mid)) <= world:
+            hi = mid
+        else:
+            lo = mid
+    ranges = pack(hi)
+    ranges += [(n, n)] * (world - len(ranges))
+    return ranges
+
+
+def layer_weights(rects3: torch.Tensor, n_layers: int) -> List[float]:
+    """Records per brick layer from the packed 3D brick rectangles
+    ([N] x 16 bytes: x0|x1<<16, y0|y1<<16, z0|z1<<16, pad, as the volume
+    mapping writes them): each Gaussian adds its x-y brick area to every layer
+    of its z range."""
+    r = rects3.view(torch.int32).view(-1, 4)[:, :3].to(torch.int64) & 0xFFFFFFFF
+    lo, hi = r & 0xFFFF, r >> 16
+    area = ((hi[:, 0] - lo[:, 0]).clamp_min(0) * (hi[:, 1] - lo[:, 1]).clamp_min(0)).double()
+    z0 = lo[:, 2].clamp(0, n_layers)
+    z1 = hi[:, 2].clamp(0, n_layers)
+    ok = z1 > z0
+    diff = torch.zeros(n_layers + 1, dtype=torch.float64, device=rects3.device)
+    diff.scatter_add_(0, z0[ok], area[ok])
+    diff.scatter_add_(0, z1[ok], -area[ok])
+    return torch.cumsum(diff, 0)[:n_layers].tolist()
+
+
 def slab_rows(l0: int, l1: int, tile: int, dim0: int) -> Tuple[int, int]:
     """Voxel rows [z0, z1) of brick layers [l0, l1) in a grid of depth dim0."""
     z0 = l0 * tile

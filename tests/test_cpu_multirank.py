@@ -173,3 +173,39 @@ def test_voxel_slabs_equal_the_full_volume_and_gradient(sharded):
     ref = torch.autograd.grad((full * v_full).sum(), params)
     for a, b in zip(sharded["vgrads"], ref):
         torch.testing.assert_close(a, b, rtol=1e-10, atol=1e-12)
+
+
+def test_balanced_layer_ranges():
+    _setup_paths()
+    import r2s_shard as shard
+
+    # clustered load like the config-2 voxel grid: a bump in the middle layers
+    w = [0.06, 0.09, 0.14, 0.2, 0.29, 0.38, 0.49, 0.6, 0.71, 0.8, 0.87, 0.91, 0.94, 0.95, 0.94,
+         0.94, 0.95, 0.97, 1.01, 1.04, 1.06, 1.05, 1.0, 0.9, 0.78, 0.63, 0.49, 0.36, 0.25, 0.16,
+         0.1, 0.06]
+    for world in (1, 2, 3, 8, 40):
+        ranges = shard.balanced_layer_ranges(w, world)
+        assert len(ranges) == world
+        assert ranges[0][0] == 0 and ranges[-1][1] == len(w)
+        assert all(a[1] == b[0] for a, b in zip(ranges, ranges[1:]))
+        loads = [sum(w[l0:l1]) for l0, l1 in ranges]
+        if world <= len(w):
+            assert max(loads) <= sum(w) / world + max(w) + 1e-9
+    even = [sum(w[l0:l1]) for l0, l1 in (shard.layer_range(len(w), r, 8) for r in range(8))]
+    balanced = [sum(w[l0:l1]) for l0, l1 in shard.balanced_layer_ranges(w, 8)]
+    assert max(balanced) < 0.75 * max(even)
+    assert shard.balanced_layer_ranges([0.0] * 4, 2) == [(0, 2), (2, 4)]
+
+
+def test_layer_weights_from_packed_rects():
+    _setup_paths()
+    import r2s_shard as shard
+
+    def pack(lo, hi):
+        return lo | (hi << 16)
+
+    rows = [(pack(0, 2), pack(1, 4), pack(0, 3), 0),   # area 2*3, layers 0..2
+            (pack(1, 2), pack(0, 1), pack(2, 4), 0),   # area 1, layers 2..3
+            (pack(3, 3), pack(0, 1), pack(0, 4), 0)]   # empty in x
+    rects = torch.tensor(rows, dtype=torch.int64).to(torch.int32).contiguous().view(torch.uint8)
+    assert shard.layer_weights(rects, 4) == [6.0, 6.0, 7.0, 1.0]
