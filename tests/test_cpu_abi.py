@@ -101,3 +101,28 @@ def test_workspace_sizes_are_bounded(lib):
     b3 = lib.r2s_bin_workspace_bytes(32, 500_000, 1024, 1)
     assert 0 < b3 <= (256 << 20) + (1 << 20)
     assert lib.r2s_bin_workspace_bytes(-1, 1, 1, 0) == -1
+
+
+def test_training_entry_points_validate_arguments(lib):
+    from r2splat.cuda._backend import AdamGroup
+
+    buf = ctypes.create_string_buffer(256)
+    groups = (AdamGroup * 9)()
+    assert lib.r2s_adam_step_f32(groups, 9, 0.9, 0.999, 1e-15, None) == 1
+    lib.r2s_last_error(buf, 256)
+    assert b"groups" in buf.value
+    one = (AdamGroup * 1)(AdamGroup(None, None, None, None, 4, 1e-3, 0))
+    assert lib.r2s_adam_step_f32(one, 1, 0.9, 0.999, 1e-15, None) == 1  # step 0
+    assert lib.r2s_adam_step_f32(one, 1, 1.5, 0.999, 1e-15, None) == 1  # beta out of range
+    assert lib.r2s_densify_stats_f32(None, None, -1, 4, 1.0, 1.0, 1.0, None, None, None,
+                                     None) == 1
+    assert lib.r2s_densify_stats_f32(None, None, 1, 4, 1.0, 1.0, 0.0, None, None, None,
+                                     None) == 1
+    # the SSIM window of the reference configs is the only one built
+    assert lib.r2s_projection_loss_f32(None, None, None, None, 1, 8, 8, 7, None, None, None,
+                                       None, None) == 1
+    lib.r2s_last_error(buf, 256)
+    assert b"window" in buf.value
+    assert lib.r2s_tv_loss_f32(None, 4, 4, 4, None, None, None, None) == 1
+    assert lib.r2s_projection_loss_combine_f32(None, None, None, None, None, -1, None, None,
+                                               None) == 1
