@@ -491,11 +491,11 @@ int bin_prepare_impl(const void* rects, int64_t S, int64_t N, int64_t T, uint32_
         const dim3 grid((unsigned)p.n_chunks, (unsigned)S);
         const size_t smem = (size_t)T * 4;
         if (layered) {
-            cudaFuncSetAttribute(bin_count_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (int rc = set_dynamic_smem(bin_count_kernel<true>, smem, "binning")) return rc;
             bin_count_kernel<true><<<grid, 256, smem, stream>>>(rects, N, (int)T, tiles_x, seg_base,
                                                                 p.chunk, p.n_chunks, w.hist);
         } else {
-            cudaFuncSetAttribute(bin_count_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (int rc = set_dynamic_smem(bin_count_kernel<false>, smem, "binning")) return rc;
             bin_count_kernel<false><<<grid, 256, smem, stream>>>(rects, N, (int)T, tiles_x, seg_base,
                                                                  p.chunk, p.n_chunks, w.hist);
         }
@@ -532,14 +532,14 @@ int bin_place_impl(const void* rects, int64_t S, int64_t N, int64_t T, uint32_t 
         const size_t smem = (size_t)(fixed + cap * 2);
         const unsigned blocks = (unsigned)(S * p.n_chunks);
         if (layered) {
-            cudaFuncSetAttribute(bin_place_staged_kernel<true>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (int rc = set_dynamic_smem(bin_place_staged_kernel<true>, smem, "bin_place"))
+                return rc;
             bin_place_staged_kernel<true><<<blocks, kStagedWarps * 32, smem, stream>>>(
                 rects, N, (int)T, tiles_x, seg_base, p.chunk, p.n_chunks, w.hist, offsets,
                 flatten_ids, (int)cap);
         } else {
-            cudaFuncSetAttribute(bin_place_staged_kernel<false>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (int rc = set_dynamic_smem(bin_place_staged_kernel<false>, smem, "bin_place"))
+                return rc;
             bin_place_staged_kernel<false><<<blocks, kStagedWarps * 32, smem, stream>>>(
                 rects, N, (int)T, tiles_x, seg_base, p.chunk, p.n_chunks, w.hist, offsets,
                 flatten_ids, (int)cap);
@@ -558,12 +558,12 @@ int bin_place_impl(const void* rects, int64_t S, int64_t N, int64_t T, uint32_t 
     const unsigned blocks = (unsigned)((n_warps + warps - 1) / warps);
     const size_t smem = (size_t)warps * per_warp;
     if (layered) {
-        cudaFuncSetAttribute(bin_place_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (int rc = set_dynamic_smem(bin_place_kernel<true>, smem, "bin_place")) return rc;
         bin_place_kernel<true><<<blocks, warps * 32, smem, stream>>>(
             rects, S, N, (int)T, tiles_x, seg_base, p.chunk, p.n_chunks, w.hist, offsets,
             flatten_ids);
     } else {
-        cudaFuncSetAttribute(bin_place_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (int rc = set_dynamic_smem(bin_place_kernel<false>, smem, "bin_place")) return rc;
         bin_place_kernel<false><<<blocks, warps * 32, smem, stream>>>(
             rects, S, N, (int)T, tiles_x, seg_base, p.chunk, p.n_chunks, w.hist, offsets,
             flatten_ids);

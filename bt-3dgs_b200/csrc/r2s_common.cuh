@@ -23,6 +23,19 @@ constexpr int kThreads = 256;
 int fail(int code, const char* fmt, ...);
 int check_launch(const char* what);
 
+// Opt a kernel in to `bytes` of dynamic shared memory; R2S_ERR_CUDA on failure.
+template <typename Kernel>
+inline int set_dynamic_smem(Kernel kernel, size_t bytes, const char* what) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (e != cudaSuccess) {
+        (void)cudaGetLastError();
+        return fail(R2S_ERR_CUDA, "%s: cannot reserve %zu bytes of shared memory: %s", what, bytes,
+                    cudaGetErrorString(e));
+    }
+    return R2S_OK;
+}
+
 #define R2S_REQUIRE(cond, ...)                                                 \
     do {                                                                       \
         if (!(cond)) return ::r2s::fail(R2S_ERR_ARG, __VA_ARGS__);             \

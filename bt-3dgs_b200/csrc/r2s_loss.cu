@@ -304,8 +304,7 @@ extern "C" int r2s_projection_loss_f32(const float* renders, const float* target
         }
         for (int k = 0; k < 2 * kR + 1; ++k) w.g[k] = (double)(float)(e[k] / tot);
     }
-    cudaFuncSetAttribute(proj_loss_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)kLossSmem);
+    if (int rc = set_dynamic_smem(proj_loss_kernel, kLossSmem, "projection_loss")) return rc;
     const dim3 grid((unsigned)((W + kTO - 1) / kTO), (unsigned)((H + kTO - 1) / kTO), (unsigned)C);
     proj_loss_kernel<<<grid, kLossThreads, kLossSmem, stream>>>(
         renders, targets, edge_targets, edge_mask, (int)H, (int)W, w, 0.01 * 0.01, 0.03 * 0.03,

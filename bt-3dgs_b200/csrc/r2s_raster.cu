@@ -805,7 +805,7 @@ int launch_raster_fwd(const RasterSrc<S>& src, const int32_t* offsets, const int
     const size_t smem = 6 * al16((size_t)geo.nthr * sizeof(S)) + al16((size_t)geo.nthr * 4) +
                         (size_t)n_warps * 16;
     auto kern = raster_fwd_kernel<S, SPLATS>;
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (int rc = set_dynamic_smem(kern, smem, "rasterize")) return rc;
     const dim3 grid(ntx, nty, (unsigned)C);
     kern<<<grid, geo.nthr, smem, stream>>>(src, offsets, flatten_ids, C * (int64_t)ntx * nty,
                                            n_isects, W, H, geo, ntx, nty, image);
@@ -825,7 +825,7 @@ int launch_raster_bwd(const RasterSrc<S>& src, const int32_t* offsets, const int
     nthr = (nthr + 31) / 32 * 32;
     const size_t smem = (size_t)T * (T + 1) * sizeof(S) + (size_t)nthr * (6 * sizeof(S) + 8);
     auto kern = raster_bwd_kernel<S, SPLATS, EXPMODE>;
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (int rc = set_dynamic_smem(kern, smem, "rasterize")) return rc;
     const dim3 grid(ntx, nty, (unsigned)C);
     kern<<<grid, nthr, smem, stream>>>(src, offsets, flatten_ids, C * (int64_t)ntx * nty, n_isects,
                                        v_image, W, H, (int)T, ntx, nty, with_abs, stats);

@@ -732,7 +732,7 @@ int launch_voxel_fwd(const VoxSrc<S>& src, const int32_t* offsets, const int32_t
     const size_t smem = 10 * al16v((size_t)geo.nthr * sizeof(S)) +
                         al16v((size_t)std::max(geo.nthr, n_warps * 6) * 4) + n_warps * 8;
     auto kern = voxel_fwd_kernel<S, SPLATS>;
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (int rc = set_dynamic_smem(kern, smem, "voxelize")) return rc;
     const uint32_t layers = layer_end - layer_begin;
     const dim3 grid(nt2, nt1, layers);
     kern<<<grid, geo.nthr, smem, stream>>>(src, offsets, flatten_ids,
@@ -752,7 +752,7 @@ int launch_voxel_bwd(const VoxSrc<S>& src, const int32_t* offsets, const int32_t
     const size_t smem = al16v((size_t)T * T * T * sizeof(S)) + 10 * al16v((size_t)nthr * sizeof(S)) +
                         al16v((size_t)nthr * 4) + (size_t)nthr * 8;
     auto kern = voxel_bwd_kernel<S, SPLATS, EXPMODE>;
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (int rc = set_dynamic_smem(kern, smem, "voxelize")) return rc;
     const uint32_t layers = layer_end - layer_begin;
     const dim3 grid(nt2, nt1, layers);
     kern<<<grid, nthr, smem, stream>>>(src, offsets, flatten_ids, (int64_t)layers * nt1 * nt2,
