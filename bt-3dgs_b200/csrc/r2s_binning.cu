@@ -272,16 +272,21 @@ __device__ __forceinline__ void walk_items(const void* __restrict__ rects, int64
     }
 }
 
-// Per-tile record counts of items [w0, w1), one item per lane (order-free).
+// Per-tile record counts of items [w0, w1), one item per lane (order-free),
+// into 16-bit counters packed two per 32-bit word (tile t: half t & 1 of word
+// t >> 1, added with one 32-bit atomic; counts stay below 2^16).
 template <bool LAYERED>
 __device__ __forceinline__ void count_items(const void* __restrict__ rects, int64_t s, int64_t N,
                                             int64_t layer, int64_t w0, int64_t w1,
-                                            uint32_t tiles_x, int32_t* counts) {
+                                            uint32_t tiles_x, uint32_t* words) {
     for (int64_t i = w0 + (threadIdx.x & 31); i < w1; i += 32) {
         const ItemRect r = load_rect<LAYERED>(rects, s, i, N, layer);
         if (r.n == 0) continue;
         for (uint32_t y = r.y0; y < r.y1; ++y)
-            for (uint32_t x = r.x0; x < r.x1; ++x) atomicAdd(&counts[y * tiles_x + x], 1);
+            for (uint32_t x = r.x0; x < r.x1; ++x) {
+                const uint32_t t = y * tiles_x + x;
+                atomicAdd(&words[t >> 1], (t & 1u) ? 0x10000u : 1u);
+            }
     }
 }
 
@@ -316,10 +321,11 @@ __device__ __forceinline__ int block_exclusive_scan(const int32_t* v, int32_t* o
     return total;
 }
 
-constexpr int kStagedWarps = 8;
+constexpr int kStagedWarps = 16;
 
-// Phase 3, staged: one CTA per (segment, chunk).  Warps take consecutive
-// sub-chunks; shared-memory atomics give per-(warp, tile) counts, whose prefix over
+// Phase 3, staged: one CTA per (segment, chunk).  16 warps take consecutive
+// sub-chunks; shared-memory atomics give per-(warp, tile) 16-bit counts (a chunk
+// holds at most 2^16 items), whose prefix over
 // warps and tiles places every record of the chunk in a tile-major staging
 // buffer in shared memory (16-bit item offsets), in item order per tile.  The
 // buffer is then written out one tile run at a time, so each tile's records
@@ -334,8 +340,10 @@ bin_place_staged_kernel(const void* __restrict__ rects, int64_t N, int T, uint32
     extern __shared__ __align__(16) int32_t smem[];
     __shared__ int32_t s_scan[33];
     const int tid = threadIdx.x, nthr = blockDim.x, warp = tid >> 5, lane = tid & 31;
-    int32_t* wc = smem;                  // [warps][T]: counts, then running positions
-    int32_t* gpos = wc + kStagedWarps * T;  // [T] first global position of the chunk's run
+    const int TW = (T + 1) >> 1;  // 32-bit words per warp row of 16-bit counters
+    uint32_t* wcw = reinterpret_cast<uint32_t*>(smem);  // [warps][TW]
+    uint16_t* wc = reinterpret_cast<uint16_t*>(smem);   // [warps][2 TW]: counts, then positions
+    int32_t* gpos = smem + kStagedWarps * TW;  // [T] first global position of the chunk's run
     int32_t* tot = gpos + T;             // [T] records of the chunk per tile
     int32_t* lofs = tot + T;             // [T] first staging slot per tile
     uint16_t* stage = reinterpret_cast<uint16_t*>(lofs + T);
@@ -350,19 +358,19 @@ bin_place_staged_kernel(const void* __restrict__ rects, int64_t N, int T, uint32
     const int64_t w0 = min(i1, i0 + warp * per), w1 = min(i1, w0 + per);
     const int32_t* hrow = hist + (s * n_chunks + k) * (int64_t)T;
     const int32_t* orow = offsets + s * (int64_t)T;
-    for (int t = tid; t < kStagedWarps * T; t += nthr) wc[t] = 0;
+    for (int t = tid; t < kStagedWarps * TW; t += nthr) wcw[t] = 0u;
     for (int t = tid; t < T; t += nthr) gpos[t] = orow[t] + hrow[t];
     __syncthreads();
 
-    int32_t* mine = wc + warp * T;
-    count_items<LAYERED>(rects, s, N, layer, w0, w1, tiles_x, mine);
+    count_items<LAYERED>(rects, s, N, layer, w0, w1, tiles_x, wcw + warp * TW);
+    uint16_t* mine = wc + warp * 2 * TW;
     __syncthreads();
     for (int t = tid; t < T; t += nthr) {
         int run = 0;
 #pragma unroll
         for (int w = 0; w < kStagedWarps; ++w) {
-            const int c = wc[w * T + t];
-            wc[w * T + t] = run;
+            const int c = wc[w * 2 * TW + t];
+            wc[w * 2 * TW + t] = (uint16_t)run;
             run += c;
         }
         tot[t] = run;
@@ -372,7 +380,7 @@ bin_place_staged_kernel(const void* __restrict__ rects, int64_t N, int T, uint32
     if (total <= cap) {
         walk_items<LAYERED>(rects, s, N, layer, w0, w1, i0, tiles_x, [&](int tile, int local) {
             const int p = mine[tile];
-            mine[tile] = p + 1;
+            mine[tile] = (uint16_t)(p + 1);
             stage[lofs[tile] + p] = (uint16_t)local;
         });
         __syncthreads();
@@ -385,7 +393,7 @@ bin_place_staged_kernel(const void* __restrict__ rects, int64_t N, int T, uint32
     } else {
         walk_items<LAYERED>(rects, s, N, layer, w0, w1, i0, tiles_x, [&](int tile, int local) {
             const int p = mine[tile];
-            mine[tile] = p + 1;
+            mine[tile] = (uint16_t)(p + 1);
             flatten_ids[gpos[tile] + p] = (int32_t)(id0 + local);
         });
     }
@@ -524,9 +532,9 @@ int bin_place_impl(const void* rects, int64_t S, int64_t N, int64_t T, uint32_t 
     R2S_REQUIRE(ws_bytes >= p.bytes, "binning: workspace too small");
     const WsView w = carve(const_cast<void*>(ws), p);
     // staged placement when the per-(warp, tile) counters leave room for a
-    // staging buffer of at least 4096 records in ~104 KB (two CTAs per SM)
+    // staging buffer of at least 4096 records in ~104 KB (two 16-warp CTAs per SM)
     constexpr int kStagedSmem = 104 * 1024;
-    const int64_t fixed = (int64_t)(kStagedWarps + 3) * T * 4;
+    const int64_t fixed = (int64_t)kStagedWarps * ((T + 1) / 2) * 4 + (int64_t)3 * T * 4;
     const int64_t cap = ((kStagedSmem - fixed) / 2) & ~int64_t(7);
     if (cap >= 4096 && p.chunk <= 65536) {
         const size_t smem = (size_t)(fixed + cap * 2);
