@@ -124,7 +124,19 @@ __global__ void bin_colscan_kernel(int32_t* __restrict__ hist, int64_t S, int64_
     const int64_t s = idx / T, t = idx - s * T;
     int32_t* col = hist + s * n_chunks * T + t;
     int32_t run = 0;
-    for (int64_t k = 0; k < n_chunks; ++k) {
+    // eight loads in flight per thread: the column walk is latency-bound
+    int64_t k = 0;
+    for (; k + 8 <= n_chunks; k += 8) {
+        int32_t v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[u] = col[(k + u) * T];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            col[(k + u) * T] = run;
+            run += v[u];
+        }
+    }
+    for (; k < n_chunks; ++k) {
         const int32_t v = col[k * T];
         col[k * T] = run;
         run += v;
