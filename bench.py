@@ -627,10 +627,12 @@ def dominant_kernel_roofline(proj: OursProjection, hbm_peak, peak_kind, clock_mh
     intersection record), every (view, Gaussian) splat record once (32 B) and
     its statistics once (32 B), the upstream image (4 B per pixel) and the
     tile offsets (4 B per tile).  The kernel is bound by the SM pipes, not by
-    HBM: every pixel of every record's tile needs one exponential (the
-    reference evaluates all tile_size^2 pixels per record), so `sfu` reports
-    pairs/s against 16 ex2 per clock per SM at the sampled SM clock, and
-    `fp32` the same pairs at 30 FP32 flops each against the FP32 peak."""
+    HBM.  `sfu` and `fp32` count the algorithmic pairs P2 = n_isects x
+    tile_size^2 (the reference evaluates every pixel of a record's tile, one
+    exponential and 30 FP32 flops each) against 16 ex2 per clock per SM at
+    the sampled SM clock and against the nominal FP32 peak.  The kernel
+    itself evaluates fewer pairs (only the rows or columns a record's
+    ellipse reaches inside the tile), so these fractions can exceed 1."""
     from r2splat.cuda import _wrapper as W
 
     E = proj.E
@@ -680,7 +682,8 @@ def dominant_kernel_roofline(proj: OursProjection, hbm_peak, peak_kind, clock_mh
         "n_isects": n_isects,
         "sfu": {"achieved_ex2_per_s": round(pairs / (ms * 1e-3), -6),
                 "peak_ex2_per_s": round(sfu_peak, -6), "frac": round(pairs / (ms * 1e-3) / sfu_peak, 4),
-                "pairs": pairs, "clock_mhz": mhz},
+                "pairs": pairs, "pairs_basis": "algorithmic n_isects x 256; the kernel culls",
+                "clock_mhz": mhz},
         "fp32": {"achieved_tflops": round(tflops, 2), "peak_tflops_nominal": round(fp32_peak, 1),
                  "frac": round(tflops / fp32_peak, 4), "flops_per_pair": 30},
     }

@@ -9,8 +9,10 @@
 //     reach the |alpha| >= 1e-5 cut-off; a warp only evaluates the Gaussians
 //     of its mask bits (ballot + find-first-set);
 //   * float32 16x16 kernel: every warp covers the whole tile for a quarter of
-//     the list and evaluates only the 4-row groups a Gaussian's culling box
-//     reaches; partial sums of the four warps are added at the end;
+//     the list and evaluates only the 4-row groups that the Gaussian's
+//     ellipse reaches inside the tile (r2s_cull.cuh narrows the culling box
+//     to the rows where the ellipse crosses the tile's columns); partial
+//     sums of the four warps are added at the end;
 //   * float32 evaluates sigma*log2(e) with a pre-scaled conic and one ex2.
 //
 // Backward (reference: csrc/RasterizeToPixelsBwd.cu:76-265 "pixel" and
@@ -18,7 +20,8 @@
 // gradient in shared memory.  The generic kernel gives each warp whole
 // Gaussians and walks only the pixel rectangle that can contribute; the
 // float32 16x16 kernel gives each thread one Gaussian record and walks the
-// rows of its culling box.  Per (Gaussian, tile) both reduce
+// rows, or the columns when they are fewer, of its culling box narrowed to
+// the ellipse inside the tile.  Per (Gaussian, tile) both reduce
 // six moments of the contributing pixels,
 //   S0 = sum v e,  Sx = sum v e dx,  Sy = sum v e dy,
 //   Sxx = sum v e dx^2,  Sxy = sum v e dx dy,  Syy = sum v e dy^2
@@ -32,6 +35,7 @@
 #include <math_constants.h>
 
 #include "r2s_common.cuh"
+#include "r2s_cull.cuh"
 
 namespace r2s {
 
@@ -502,6 +506,9 @@ raster_fwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict
             int c_lo, c_hi, r_lo, r_hi;
             cull_range(p.x, q.z, (float)X0, cmax, c_lo, c_hi);
             cull_range(p.y, q.w, (float)Y0, rmax, r_lo, r_hi);
+            const float s_thr = s_threshold(q.y);
+            tile_cull(p.x, p.y, p.z, p.w, q.x, s_thr, (float)X0, (float)Y0, c_lo, c_hi, r_lo,
+                      r_hi);
             uint32_t m = 0;
             if (c_lo <= c_hi) {
 #pragma unroll
@@ -513,7 +520,7 @@ raster_fwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict
             // signed integers against INT_MIN + bits(s_thr)
             s_p[tid] = make_float4(p.x, p.y, -0.5f * kLog2e * p.z, -kLog2e * p.w);
             s_q[tid] = make_float4(-0.5f * kLog2e * q.x, q.y,
-                                   __uint_as_float(__float_as_uint(s_threshold(q.y)) ^ 0x80000000u),
+                                   __uint_as_float(__float_as_uint(s_thr) ^ 0x80000000u),
                                    __uint_as_float(m));
         }
         __syncthreads();
@@ -558,11 +565,15 @@ constexpr int kBwd16Batch = 1024;   // records staged and sorted per batch (32 g
 
 // Backward statistics of 16x16 tiles, one Gaussian record per thread.
 //
-// The tile's upstream gradient sits in shared memory.  The CTA stages the
-// tile's list in batches of 1024 records and orders each batch with a
-// counting sort on the record's row range (first row, last row of the
-// culling box), so that each group of 32 lanes walks similar rows: a warp
-// executes the union of its lanes' rows.  Warp w takes the sorted groups
+// The tile's upstream gradient sits in shared memory, row-major and
+// column-major.  Staging narrows each record's culling box to the ellipse
+// inside the tile (tile_cull) and picks the shorter axis to walk: a record
+// with fewer columns than rows is stored transposed (x <-> y, a <-> c, its
+// index flagged in the sign bit) and walks the columns of the column-major
+// copy; its moments are swapped back at the end.  The CTA stages the tile's
+// list in batches of 1024 records and orders each batch with a counting sort
+// on the walked range (first, last index), so that each group of 32 lanes
+// walks similar ranges: a warp executes the union of its lanes' ranges.  Warp w takes the sorted groups
 // w, w+8, w+16, w+24, which spreads short and long row ranges evenly over the
 // warps.  Per pixel: sigma from the column offset dx (exact per column) and
 // the row terms B dy, C dy^2, one ex2, and packed updates of the per-column
@@ -578,7 +589,11 @@ raster_bwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict
                     const int32_t* __restrict__ flatten_ids, int64_t n_keys, int64_t n_isects,
                     const float* __restrict__ v_image, uint32_t W, uint32_t H, uint32_t ntx,
                     uint32_t nty, float* __restrict__ stats) {
-    __shared__ __align__(16) float s_v[256];
+    // upstream gradient of the tile, row-major and (16 floats further, so
+    // that the two copies sit in different banks) column-major
+    __shared__ __align__(16) float s_vv[2 * 256 + 16];
+    float* const s_v = s_vv;
+    float* const s_vT = s_vv + 256 + 16;
     __shared__ float4 s_p[kBwd16Batch];
     __shared__ float4 s_q[kBwd16Batch];
     __shared__ int32_t s_g[kBwd16Batch];
@@ -598,7 +613,9 @@ raster_bwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict
     {
         const float* vc = v_image + cam * (int64_t)H * W;
         const int r = tid >> 4, c = tid & 15;
-        s_v[tid] = (c <= cmax && r <= rmax) ? vc[(int64_t)(Y0 + r) * W + X0 + c] : 0.f;
+        const float v = (c <= cmax && r <= rmax) ? vc[(int64_t)(Y0 + r) * W + X0 + c] : 0.f;
+        s_v[tid] = v;
+        s_vT[c * 16 + r] = v;
     }
     const float X0f = (float)X0, Y0f = (float)Y0;
 
@@ -624,7 +641,20 @@ raster_bwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict
                 int c_lo, c_hi, r_lo, r_hi;
                 cull_range(p.x, q.z, X0f, cmax, c_lo, c_hi);
                 cull_range(p.y, q.w, Y0f, rmax, r_lo, r_hi);
+                tile_cull(p.x, p.y, p.z, p.w, q.x, s_threshold(q.y), X0f, Y0f, c_lo, c_hi, r_lo,
+                          r_hi);
                 if (c_lo <= c_hi && r_lo <= r_hi) {
+                    if (c_hi - c_lo < r_hi - r_lo) {
+                        // fewer columns than rows: walk the columns, with the
+                        // record transposed (x <-> y, a <-> c) and flagged in
+                        // the sign bit of its index
+                        const float a = p.z;
+                        p = make_float4(p.y, p.x, q.x, p.w);
+                        q = make_float4(a, q.y, q.w, q.z);
+                        r_lo = c_lo;
+                        r_hi = c_hi;
+                        g = (int32_t)((uint32_t)g | 0x80000000u);
+                    }
                     bucket[k] = r_lo * 16 + r_hi;
                     rows = r_lo | (r_hi << 4);
                 }
@@ -662,7 +692,11 @@ raster_bwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict
             const int row0 = __reduce_min_sync(0xffffffffu, r_lo);
             const int row1 = __reduce_max_sync(0xffffffffu, r_hi);
             if (row0 > row1) continue;  // warp-uniform
-            const int64_t g = s_g[idx];
+            const int32_t gi = s_g[idx];
+            const bool tr = gi < 0;  // transposed record: walks columns
+            const int64_t g = gi & 0x7fffffff;
+            const float Uo = tr ? Y0f : X0f, Vo = tr ? X0f : Y0f;
+            const float* const vb = tr ? s_vT : s_v;
             const float4 p = s_p[idx], q = s_q[idx];
 
             // negated coefficients: the packed chain yields -s exactly (see the
@@ -674,18 +708,18 @@ raster_bwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict
             float2 dx[8], col[8];
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-                dx[j] = make_float2((X0f + (2 * j + 0.5f)) - p.x, (X0f + (2 * j + 1.5f)) - p.x);
+                dx[j] = make_float2((Uo + (2 * j + 0.5f)) - p.x, (Uo + (2 * j + 1.5f)) - p.x);
                 col[j] = make_float2(0.f, 0.f);
             }
             float Sy = 0.f, Syy = 0.f, Sxy = 0.f, Ax = 0.f, Ay = 0.f;
             for (int r = row0; r <= row1; ++r) {
                 const bool rin = r >= r_lo && r <= r_hi;
-                const float dy = (Y0f + ((float)r + 0.5f)) - p.y;
+                const float dy = (Vo + ((float)r + 0.5f)) - p.y;
                 const float by = B * dy, cyy = Cc * dy * dy;
                 const float2 by2 = make_float2(by, by), cyy2 = make_float2(cyy, cyy);
                 const float bdy = p.w * dy, cdy = q.x * dy;
                 const float2 bdy2 = make_float2(bdy, bdy), cdy2 = make_float2(cdy, cdy);
-                const float4* vr = reinterpret_cast<const float4*>(s_v + r * 16);
+                const float4* vr = reinterpret_cast<const float4*>(vb + r * 16);
                 float2 r0 = make_float2(0.f, 0.f), r1 = r0;
 #pragma unroll
                 for (int j4 = 0; j4 < 4; ++j4) {
@@ -727,6 +761,14 @@ raster_bwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict
                 Sx += cx.x + cx.y;
                 Sxx = fmaf(cx.x, dx[j].x, Sxx);
                 Sxx = fmaf(cx.y, dx[j].y, Sxx);
+            }
+            if (tr) {  // back to image axes
+                float t = Sx;
+                Sx = Sy, Sy = t;
+                t = Sxx;
+                Sxx = Syy, Syy = t;
+                t = Ax;
+                Ax = Ay, Ay = t;
             }
             float* st = stats + g * 8;
             red_add_v4(st, S0, Sx, Sy, Sxx);
