@@ -909,6 +909,19 @@ __global__ void map_vsplats_kernel(const float* __restrict__ means,
 // ===========================================================================
 // Fused explicit backward (float32), one thread per Gaussian
 // ===========================================================================
+
+// Densification statistics of BinaryTreeStrategy._update_state
+// (src/strategies/binary_tree.py:305-347, unpacked renders) taken from the
+// per-view screen-space gradients as the explicit backward produces them.
+struct DensifyArgs {
+    const int2* radii;  // [C,N,2]; a view counts when max(rx, ry) > 0
+    float scale_x, scale_y, extent;
+    int absgrad;       // 1: v_means2d_abs, 0: v_means2d
+    float* grad2d;     // [N] += |(g_x scale_x, g_y scale_y)| per counted view; NULL: off
+    float* count;      // [N] += counted views
+    float* max_radii;  // [N] max(.., max radius / extent) when non-NULL
+};
+
 __global__ void explicit_bwd_kernel(
     const float* __restrict__ means, const float* __restrict__ quats,
     const float* __restrict__ raw_scales, const float* __restrict__ raw_opac, float smin,
@@ -919,7 +932,7 @@ __global__ void explicit_bwd_kernel(
     const float* __restrict__ centers, uint32_t dim2, uint32_t dim1, uint32_t dim0, float eps3d,
     const float4* __restrict__ vstats, int accumulate, float* __restrict__ out_means,
     float* __restrict__ out_quats, float* __restrict__ out_scales,
-    float* __restrict__ out_opac) {
+    float* __restrict__ out_opac, DensifyArgs dens) {
     const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (g >= N) return;
     RotScale<float> rs;
@@ -931,11 +944,14 @@ __global__ void explicit_bwd_kernel(
 
     float acc_p[3] = {0.f, 0.f, 0.f}, acc_s[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     float acc_w = 0.f;
-    if (rstats != nullptr) {
+    // densification sums, in the operation order of densify_stats_kernel
+    float d_acc = 0.f, d_cnt = 0.f, d_rmax = 0.f;
+    if (rstats != nullptr || dens.grad2d != nullptr) {
         for (int64_t c = 0; c < C; ++c) {
             const int64_t idx = c * N + g;
-            const float4 s0 = rstats[idx * 2];
-            const float4 s1 = rstats[idx * 2 + 1];
+            const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+            const float4 s0 = rstats != nullptr ? rstats[idx * 2] : zero;
+            const float4 s1 = rstats != nullptr ? rstats[idx * 2 + 1] : zero;
             const View<float> v = load_view(viewmats, Ks, c);
             ProjState<float> p;
             float vmx = 0.f, vmy = 0.f, amx = 0.f, amy = 0.f;
@@ -969,7 +985,24 @@ __global__ void explicit_bwd_kernel(
             }
             if (v_means2d) v_means2d[idx] = make_float2(vmx, vmy);
             if (v_means2d_abs) v_means2d_abs[idx] = make_float2(amx, amy);
+            if (dens.grad2d != nullptr) {
+                const int2 r2 = dens.radii[idx];
+                const int32_t r = max(r2.x, r2.y);
+                if (r > 0) {
+                    const float x = __fmul_rn(dens.absgrad ? amx : vmx, dens.scale_x);
+                    const float y = __fmul_rn(dens.absgrad ? amy : vmy, dens.scale_y);
+                    d_acc = __fadd_rn(d_acc, __fsqrt_rn(__fadd_rn(__fmul_rn(x, x), __fmul_rn(y, y))));
+                    d_cnt = __fadd_rn(d_cnt, 1.f);
+                    d_rmax = fmaxf(d_rmax, __fdiv_rn((float)r, dens.extent));
+                }
+            }
         }
+    }
+    if (dens.grad2d != nullptr) {
+        dens.grad2d[g] = __fadd_rn(dens.grad2d[g], d_acc);
+        dens.count[g] = __fadd_rn(dens.count[g], d_cnt);
+        if (dens.max_radii != nullptr && d_cnt > 0.f)
+            dens.max_radii[g] = fmaxf(dens.max_radii[g], d_rmax);
     }
     if (vstats != nullptr) {
         const float4 t0 = vstats[g * 3], t1 = vstats[g * 3 + 1], t2 = vstats[g * 3 + 2];
@@ -1200,6 +1233,44 @@ extern "C" int r2s_map_vsplats_f32(const float* means, const float* covars, cons
     return check_launch("map_vsplats");
 }
 
+namespace {
+int explicit_backward_launch(
+    const float* means, const float* quats, const float* raw_scales, const float* raw_opacities,
+    double smin, double smax, const float* viewmats, const float* Ks, int64_t C, int64_t N,
+    uint32_t width, uint32_t height, double eps2d, const float* raster_stats, float* v_means2d,
+    float* v_means2d_abs, const float* ranges, const float* centers, uint32_t dim2,
+    uint32_t dim1, uint32_t dim0, double eps3d, const float* vox_stats, int accumulate,
+    float* v_means, float* v_quats, float* v_raw_scales, float* v_raw_opacities,
+    const r2s_densify_args* densify, r2s_stream_t stream) {
+    R2S_REQUIRE(C >= 0 && N >= 0, "explicit_backward: negative size");
+    R2S_REQUIRE(vox_stats == nullptr || (ranges && centers),
+                "explicit_backward: voxel statistics need ranges and centers");
+    DensifyArgs dens{};
+    if (densify != nullptr) {
+        R2S_REQUIRE(densify->grad2d && densify->count && (C == 0 || densify->radii),
+                    "explicit_backward: densify statistics need radii, grad2d and count");
+        R2S_REQUIRE(densify->extent > 0.0, "explicit_backward: densify extent must be positive");
+        R2S_REQUIRE(C == 0 || viewmats, "explicit_backward: densify statistics need the views");
+        dens.radii = reinterpret_cast<const int2*>(densify->radii);
+        dens.scale_x = (float)densify->scale_x;
+        dens.scale_y = (float)densify->scale_y;
+        dens.extent = (float)densify->extent;
+        dens.absgrad = densify->absgrad ? 1 : 0;
+        dens.grad2d = densify->grad2d;
+        dens.count = densify->count;
+        dens.max_radii = densify->max_radii;
+    }
+    if (N == 0) return R2S_OK;
+    explicit_bwd_kernel<<<grid_for(N, 128), 128, 0, stream>>>(
+        means, quats, raw_scales, raw_opacities, (float)smin, (float)smax, viewmats, Ks, C, N,
+        width, height, (float)eps2d, (const float4*)raster_stats, (float2*)v_means2d,
+        (float2*)v_means2d_abs, ranges, centers, dim2, dim1, dim0, (float)eps3d,
+        (const float4*)vox_stats, accumulate, v_means, v_quats, v_raw_scales, v_raw_opacities,
+        dens);
+    return check_launch("explicit_backward");
+}
+}  // namespace
+
 extern "C" int r2s_explicit_backward_f32(
     const float* means, const float* quats, const float* raw_scales, const float* raw_opacities,
     double smin, double smax, const float* viewmats, const float* Ks, int64_t C, int64_t N,
@@ -1208,14 +1279,25 @@ extern "C" int r2s_explicit_backward_f32(
     uint32_t dim1, uint32_t dim0, double eps3d, const float* vox_stats, int accumulate,
     float* v_means, float* v_quats, float* v_raw_scales, float* v_raw_opacities,
     r2s_stream_t stream) {
-    R2S_REQUIRE(C >= 0 && N >= 0, "explicit_backward: negative size");
-    R2S_REQUIRE(vox_stats == nullptr || (ranges && centers),
-                "explicit_backward: voxel statistics need ranges and centers");
-    if (N == 0) return R2S_OK;
-    explicit_bwd_kernel<<<grid_for(N, 128), 128, 0, stream>>>(
-        means, quats, raw_scales, raw_opacities, (float)smin, (float)smax, viewmats, Ks, C, N,
-        width, height, (float)eps2d, (const float4*)raster_stats, (float2*)v_means2d,
-        (float2*)v_means2d_abs, ranges, centers, dim2, dim1, dim0, (float)eps3d,
-        (const float4*)vox_stats, accumulate, v_means, v_quats, v_raw_scales, v_raw_opacities);
-    return check_launch("explicit_backward");
+    return explicit_backward_launch(means, quats, raw_scales, raw_opacities, smin, smax, viewmats,
+                                    Ks, C, N, width, height, eps2d, raster_stats, v_means2d,
+                                    v_means2d_abs, ranges, centers, dim2, dim1, dim0, eps3d,
+                                    vox_stats, accumulate, v_means, v_quats, v_raw_scales,
+                                    v_raw_opacities, nullptr, stream);
+}
+
+extern "C" int r2s_explicit_backward_densify_f32(
+    const float* means, const float* quats, const float* raw_scales, const float* raw_opacities,
+    double smin, double smax, const float* viewmats, const float* Ks, int64_t C, int64_t N,
+    uint32_t width, uint32_t height, double eps2d, const float* raster_stats, float* v_means2d,
+    float* v_means2d_abs, const float* ranges, const float* centers, uint32_t dim2,
+    uint32_t dim1, uint32_t dim0, double eps3d, const float* vox_stats, int accumulate,
+    float* v_means, float* v_quats, float* v_raw_scales, float* v_raw_opacities,
+    const r2s_densify_args* densify, r2s_stream_t stream) {
+    R2S_REQUIRE(densify != nullptr, "explicit_backward_densify: null densify arguments");
+    return explicit_backward_launch(means, quats, raw_scales, raw_opacities, smin, smax, viewmats,
+                                    Ks, C, N, width, height, eps2d, raster_stats, v_means2d,
+                                    v_means2d_abs, ranges, centers, dim2, dim1, dim0, eps3d,
+                                    vox_stats, accumulate, v_means, v_quats, v_raw_scales,
+                                    v_raw_opacities, densify, stream);
 }

@@ -36,6 +36,15 @@ class AdamGroup(ctypes.Structure):
                 ("numel", ctypes.c_int64), ("lr", ctypes.c_double), ("step", ctypes.c_int64)]
 
 
+class DensifyArgs(ctypes.Structure):
+    """r2s_densify_args of include/r2s.h."""
+
+    _fields_ = [("radii", ctypes.c_void_p), ("scale_x", ctypes.c_double),
+                ("scale_y", ctypes.c_double), ("extent", ctypes.c_double),
+                ("absgrad", ctypes.c_int32), ("grad2d", ctypes.c_void_p),
+                ("count", ctypes.c_void_p), ("max_radii", ctypes.c_void_p)]
+
+
 # argument type lists of every exported function (include/r2s.h)
 _SIGNATURES = {
     "r2s_version": ([], ctypes.c_char_p),
@@ -102,6 +111,10 @@ _SIGNATURES = {
     "r2s_explicit_backward_f32": (
         [_p, _p, _p, _p, _f64, _f64, _p, _p, _i64, _i64, _u32, _u32, _f64, _p, _p, _p, _p, _p,
          _u32, _u32, _u32, _f64, _p, _i32, _p, _p, _p, _p, _p], _i32),
+    "r2s_explicit_backward_densify_f32": (
+        [_p, _p, _p, _p, _f64, _f64, _p, _p, _i64, _i64, _u32, _u32, _f64, _p, _p, _p, _p, _p,
+         _u32, _u32, _u32, _f64, _p, _i32, _p, _p, _p, _p, ctypes.POINTER(DensifyArgs), _p],
+        _i32),
 }
 
 UNAVAILABLE_MESSAGE = (

@@ -759,17 +759,28 @@ def fused_voxel_bwd(vsplats, offsets, flatten_ids, v_volume, N, dim2, dim1, dim0
 
 def fused_explicit_backward(means, quats, raw_scales, raw_opacities, scale_min, scale_max,
                             viewmats, Ks, W, H, eps2d, raster_stats, v_means2d, v_means2d_abs,
-                            ranges, centers, dim2, dim1, dim0, eps3d, vox_stats, accumulate, outs):
+                            ranges, centers, dim2, dim1, dim0, eps3d, vox_stats, accumulate, outs,
+                            densify=None):
+    """``densify``: None, or (radii [C,N,2] int32, scale_x, scale_y, extent,
+    absgrad, grad2d [N], count [N], max_radii [N] or None) for the fused
+    densification statistics."""
     dev = means.device
     C = 0 if viewmats is None else viewmats.size(0)
     N = means.size(0)
     v_means, v_quats, v_scales, v_opac = outs
-    _call("r2s_explicit_backward_f32", _ptr(means), _ptr(quats), _ptr(raw_scales),
-          _ptr(raw_opacities), float(scale_min), float(scale_max), _ptr(viewmats), _ptr(Ks), C, N,
-          W, H, float(eps2d), _ptr(raster_stats), _ptr(v_means2d), _ptr(v_means2d_abs),
-          _ptr(ranges), _ptr(centers), dim2, dim1, dim0, float(eps3d), _ptr(vox_stats),
-          1 if accumulate else 0, _ptr(v_means), _ptr(v_quats), _ptr(v_scales), _ptr(v_opac),
-          _stream(dev))
+    args = (_ptr(means), _ptr(quats), _ptr(raw_scales), _ptr(raw_opacities), float(scale_min),
+            float(scale_max), _ptr(viewmats), _ptr(Ks), C, N, W, H, float(eps2d),
+            _ptr(raster_stats), _ptr(v_means2d), _ptr(v_means2d_abs), _ptr(ranges),
+            _ptr(centers), dim2, dim1, dim0, float(eps3d), _ptr(vox_stats),
+            1 if accumulate else 0, _ptr(v_means), _ptr(v_quats), _ptr(v_scales), _ptr(v_opac))
+    if densify is None:
+        _call("r2s_explicit_backward_f32", *args, _stream(dev))
+        return
+    radii, sx, sy, extent, absgrad, grad2d, count, max_radii = densify
+    from ._backend import DensifyArgs
+    d = DensifyArgs(_ptr(radii), float(sx), float(sy), float(extent), 1 if absgrad else 0,
+                    _ptr(grad2d), _ptr(count), _ptr(max_radii))
+    _call("r2s_explicit_backward_densify_f32", *args, ctypes.byref(d), _stream(dev))
 
 
 def is_cuda_extension_available() -> bool:

@@ -164,8 +164,15 @@ def explicit_backward(
     quats: torch.Tensor,
     raw_scales: torch.Tensor,
     raw_opacities: torch.Tensor,
+    *,
+    densify=None,
 ) -> None:
-    """Apply the saved first-order CUDA VJP and accumulate raw parameter grads."""
+    """Apply the saved first-order CUDA VJP and accumulate raw parameter grads.
+
+    ``densify`` (an ``r2splat.ops.training.DensifyAccumulator``, float32
+    renders only) additionally accumulates the densification statistics of
+    the render in the same kernel; without it the behaviour is the
+    reference's (r2splat/ops/explicit.py:233-385)."""
     if state.backward_called:
         raise RuntimeError("Explicit first-order backward can only run once per state.")
     if state.projection is None:
@@ -173,13 +180,17 @@ def explicit_backward(
     proj = state.projection
     pb = proj.buffers
     if pb.splats is not None:
-        _explicit_backward_fused(state, means, quats, raw_scales, raw_opacities)
+        _explicit_backward_fused(state, means, quats, raw_scales, raw_opacities, densify)
     else:
+        if densify is not None:
+            raise RuntimeError("explicit_backward: fused densification statistics need a "
+                               "float32 render")
         _explicit_backward_chain(state, means, quats, raw_scales, raw_opacities)
     state.backward_called = True
 
 
-def _explicit_backward_fused(state, means, quats, raw_scales, raw_opacities) -> None:
+def _explicit_backward_fused(state, means, quats, raw_scales, raw_opacities,
+                             densify=None) -> None:
     from ..cuda import _wrapper as W
 
     proj = state.projection
@@ -209,6 +220,14 @@ def _explicit_backward_fused(state, means, quats, raw_scales, raw_opacities) -> 
         else:
             v_means2d = torch.zeros_like(proj.means2d)
             v_means2d_abs = torch.zeros_like(proj.means2d) if proj.absgrad else None
+        store = densify is None or densify.store_screen_grads
+        if densify is not None and densify.absgrad and not proj.absgrad:
+            raise RuntimeError("explicit_backward: densify with absgrad needs a render with "
+                               "absgrad=True")
+        if not store:
+            v_means2d = v_means2d_abs = None
+        dens_args = (None if densify is None
+                     else densify.launch_args(pb.radii.contiguous(), pb.img_w, pb.img_h))
 
         vox = state.voxel
         vox_stats = None
@@ -234,10 +253,11 @@ def _explicit_backward_fused(state, means, quats, raw_scales, raw_opacities) -> 
             vb.ranges if vb is not None else None, vb.centers if vb is not None else None,
             vb.dim2 if vb is not None else 0, vb.dim1 if vb is not None else 0,
             vb.dim0 if vb is not None else 0, vb.eps3d if vb is not None else 0.0, vox_stats,
-            accumulate, outs)
-    proj.means2d.grad = v_means2d.detach()
-    if proj.absgrad:
-        proj.means2d.absgrad = v_means2d_abs.detach()
+            accumulate, outs, densify=dens_args)
+    if store:
+        proj.means2d.grad = v_means2d.detach()
+        if proj.absgrad:
+            proj.means2d.absgrad = v_means2d_abs.detach()
     if not accumulate:
         for p, g in zip((means, quats, raw_scales, raw_opacities), outs):
             _accumulate_grad(p, g)

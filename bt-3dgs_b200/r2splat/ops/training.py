@@ -12,7 +12,9 @@ interchangeable.
   opt.step()`` (src/trainers/binary_tree.py:204-205).
 * ``update_densify_state(state, info, ...)`` -- the strategy's per-step
   statistics (``BinaryTreeStrategy._update_state``,
-  src/strategies/binary_tree.py:305-347, non-packed path) in one launch.
+  src/strategies/binary_tree.py:305-347, non-packed path) in one launch;
+  ``DensifyAccumulator(state)`` passed to ``explicit_backward(...,
+  densify=...)`` computes the same statistics inside the backward kernel.
 * ``FusedBinaryTreeLossComputer`` / ``FusedLossComputer`` -- the trainers'
   losses (``BinaryTreeLossComputer``, src/utils/loss.py:125-172;
   ``LossComputer``, loss.py:72-109): L1, SSIM and edge terms of the
@@ -21,15 +23,16 @@ interchangeable.
 from __future__ import annotations
 
 import ctypes
-from typing import Dict, Iterable, List, Union
+from dataclasses import dataclass
+from typing import Dict, Iterable, List, Optional, Union
 
 import torch
 
 from ..cuda import _wrapper as W
 from ..cuda._backend import AdamGroup
 
-__all__ = ["FusedBinaryTreeLossComputer", "FusedLossComputer", "adam_step", "projection_losses",
-           "tv_loss", "update_densify_state"]
+__all__ = ["DensifyAccumulator", "FusedBinaryTreeLossComputer", "FusedLossComputer", "adam_step",
+           "projection_losses", "tv_loss", "update_densify_state"]
 
 _MAX_GROUPS = 8
 
@@ -134,6 +137,56 @@ def update_densify_state(state: dict, info: dict, *, absgrad: bool = True,
             width / 2.0 * n_cam, height / 2.0 * n_cam, max(width, height),
             W._ptr(state["grad2d"]), W._ptr(state["count"]),
             W._ptr(state["radii"]) if track_radii else None, W._stream(dev))
+
+
+@dataclass
+class DensifyAccumulator:
+    """``BinaryTreeStrategy._update_state`` fused into the explicit backward.
+
+    Pass as ``explicit_backward(..., densify=DensifyAccumulator(state))``:
+    the backward kernel that turns the raster statistics into the per-view
+    screen-space gradients also adds, for every view where the Gaussian's
+    radius is positive, the norm of its (scaled) absgrad -- or grad with
+    ``absgrad=False`` -- to ``state["grad2d"]``, one to ``state["count"]`` and,
+    with ``track_radii``, the radius over max(width, height) to
+    ``state["radii"]`` (src/strategies/binary_tree.py:305-347).  The result is
+    bit-identical to :func:`update_densify_state` on the same render, without
+    the second pass over the [C, N, 2] gradients.  ``n_cameras`` defaults to
+    the render's views (the adapter's ``info["n_cameras"]``).  With
+    ``store_screen_grads=False`` the backward also skips writing
+    ``means2d.grad`` / ``.absgrad`` (left None), whose only consumer in the
+    reference's training step is this statistic."""
+
+    state: dict
+    absgrad: bool = True
+    track_radii: bool = False
+    n_cameras: Optional[int] = None
+    store_screen_grads: bool = True
+
+    def launch_args(self, radii: torch.Tensor, width: int, height: int):
+        """The (radii, scale_x, scale_y, extent, absgrad, grad2d, count,
+        max_radii) tuple of the fused entry point; creates the state tensors
+        on first use as the strategy does."""
+        C, N = radii.shape[:2]
+        dev = radii.device
+        if radii.dtype != torch.int32 or radii.shape != (C, N, 2) or not radii.is_contiguous():
+            raise RuntimeError("densify: radii must be contiguous int32 [C, N, 2]")
+        st = self.state
+        if st.get("grad2d") is None:
+            st["grad2d"] = torch.zeros(N, device=dev)
+        if st.get("count") is None:
+            st["count"] = torch.zeros(N, device=dev)
+        if self.track_radii and st.get("radii") is None:
+            st["radii"] = torch.zeros(N, device=dev)
+        for key in ("grad2d", "count") + (("radii",) if self.track_radii else ()):
+            t = st[key]
+            W._check_cuda(f"state[{key!r}]", t)
+            if t.dtype != torch.float32 or t.numel() != N or not t.is_contiguous():
+                raise RuntimeError(f"densify: state[{key!r}] must be contiguous float32 [{N}]")
+        n_cam = float(C if self.n_cameras is None else self.n_cameras)
+        return (radii, float(width) / 2.0 * n_cam, float(height) / 2.0 * n_cam,
+                float(max(width, height)), self.absgrad, st["grad2d"], st["count"],
+                st["radii"] if self.track_radii else None)
 
 
 # ---------------------------------------------------------------------------

@@ -427,6 +427,39 @@ R2S_API int r2s_explicit_backward_f32(
     const float* vox_stats, int accumulate, float* v_means, float* v_quats,
     float* v_raw_scales, float* v_raw_opacities, r2s_stream_t stream);
 
+/* Densification statistics of BinaryTreeStrategy._update_state
+ * (src/strategies/binary_tree.py:305-347, unpacked renders) fused into the
+ * explicit backward: for every view c where max(radii[c,n,0], radii[c,n,1])
+ * > 0, with g = the view's v_means2d_abs (absgrad != 0) or v_means2d row,
+ *   grad2d[n] += sqrt((g_x scale_x)^2 + (g_y scale_y)^2),  count[n] += 1,
+ *   max_radii[n] = max(max_radii[n], max radius / extent)   (max_radii non-NULL)
+ * in the same float32 operations as r2s_densify_stats_f32, whose [C,N] radii
+ * input is the amax of these [C,N,2] radii.  scale_x = width/2 * n_cameras,
+ * scale_y = height/2 * n_cameras, extent = max(width, height). */
+typedef struct r2s_densify_args {
+    const int32_t* radii; /* [C,N,2] */
+    double scale_x, scale_y, extent;
+    int absgrad;
+    float* grad2d;    /* [N] */
+    float* count;     /* [N] */
+    float* max_radii; /* [N] or NULL */
+} r2s_densify_args;
+
+/* r2s_explicit_backward_f32 plus the densification statistics of the same
+ * views in the same kernel (replaces the strategy's pass over
+ * means2d.absgrad after BinaryTreeTrainer's backward_explicit,
+ * src/trainers/binary_tree.py:159-194).  v_means2d / v_means2d_abs may be NULL:
+ * the statistics do not need them stored. */
+R2S_API int r2s_explicit_backward_densify_f32(
+    const float* means, const float* quats, const float* raw_scales,
+    const float* raw_opacities, double scale_min, double scale_max, const float* viewmats,
+    const float* Ks, int64_t C, int64_t N, uint32_t width, uint32_t height, double eps2d,
+    const float* raster_stats, float* v_means2d, float* v_means2d_abs, const float* ranges,
+    const float* centers, uint32_t dim2, uint32_t dim1, uint32_t dim0, double eps3d,
+    const float* vox_stats, int accumulate, float* v_means, float* v_quats,
+    float* v_raw_scales, float* v_raw_opacities, const r2s_densify_args* densify,
+    r2s_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -258,3 +258,135 @@ def test_training_step_gradients_match_reference():
                         {rk: g[rk] for _, rk in pairs},
                         {rk: truth[tk] for (_, rk), tk in zip(pairs, ("means", "quats", "scales",
                                                                        "opac"))})
+
+
+def _render_step(seed, densify=None, with_image_grad=True):
+    """One explicit render of a small scene (3 views, 128^2, + a 32^3 volume)
+    and its explicit backward; returns the raw parameters and the render."""
+    import r2s_workloads as wl
+    from r2splat.ops import explicit as E
+
+    cfg = wl.CONFIGS[0]
+    m, q, s, o = (t.cuda() for t in wl.make_gaussians(cfg, n=3000, seed=seed))
+    vm, K = (t.cuda() for t in wl.make_cameras(3, 128))
+    params = [t.clone().requires_grad_(True) for t in (m, q, s, o)]
+    st = E.prepare_explicit_gaussians(params[1], params[2], params[3], scale_min=wl.SCALE_MIN,
+                                      scale_max=wl.SCALE_MAX)
+    res = E.explicit_rasterize(st, params[0], vm, K, img_w=128, img_h=128, tile_size=16,
+                               eps2d=wl.EPS2D, radius_clip=wl.RADIUS_CLIP, absgrad=True)
+    vox = E.explicit_voxelize(st, params[0], torch.ones(3, device="cuda"),
+                              torch.zeros(3, device="cuda"), dim2=32, dim1=32, dim0=32,
+                              tile_size=8, eps3d=wl.EPS3D, radius_clip=wl.RADIUS_CLIP)
+    g = torch.Generator(device="cuda").manual_seed(seed + 100)
+    if with_image_grad:
+        (res.image * torch.randn(res.image.shape, generator=g, device="cuda")).sum().backward()
+    (vox.volume * torch.randn(vox.volume.shape, generator=g, device="cuda")).sum().backward()
+    E.explicit_backward(st, *params, densify=densify)
+    return params, res
+
+
+def _explicit_outputs(st, params, raster_stats, densify_args):
+    """One fused explicit backward from fixed raster statistics."""
+    from r2splat.cuda import _wrapper as W
+
+    pb = st.projection.buffers
+    C, N = pb.means2d.shape[:2]
+    v2 = torch.empty((C, N, 2), device="cuda")
+    va = torch.empty((C, N, 2), device="cuda")
+    outs = [torch.empty(p.shape, device="cuda") for p in params]
+    W.fused_explicit_backward(*(p.detach() for p in params), st.scale_min, st.scale_max,
+                              pb.viewmats, pb.Ks, pb.img_w, pb.img_h, pb.eps2d, raster_stats,
+                              v2 if raster_stats is not None else None,
+                              va if raster_stats is not None else None, None, None, 0, 0, 0,
+                              0.0, None, False, outs, densify=densify_args)
+    return outs, v2, va
+
+
+@pytest.mark.parametrize("absgrad", [True, False])
+@pytest.mark.parametrize("with_image_grad", [True, False])
+def test_fused_densify_equals_separate_pass(absgrad, with_image_grad):
+    """From the same raster statistics, the fused entry point gives
+    bit-identical parameter gradients and densification statistics to the
+    plain explicit backward followed by update_densify_state (the raster
+    backward itself sums with float atomics, so two renders differ in the
+    last bits and the comparison starts after it)."""
+    import r2s_workloads as wl
+    from r2splat.cuda import _wrapper as W
+    from r2splat.ops import explicit as E
+    from r2splat.ops.training import DensifyAccumulator, update_densify_state
+
+    cfg = wl.CONFIGS[0]
+    m, q, s_, o = (t.cuda() for t in wl.make_gaussians(cfg, n=3000, seed=21))
+    vm, K = (t.cuda() for t in wl.make_cameras(3, 128))
+    params = [t.clone().requires_grad_(True) for t in (m, q, s_, o)]
+    st = E.prepare_explicit_gaussians(params[1], params[2], params[3], scale_min=wl.SCALE_MIN,
+                                      scale_max=wl.SCALE_MAX)
+    res = E.explicit_rasterize(st, params[0], vm, K, img_w=128, img_h=128, tile_size=16,
+                               eps2d=wl.EPS2D, radius_clip=wl.RADIUS_CLIP, absgrad=True)
+    pb = st.projection.buffers
+    C, N = pb.means2d.shape[:2]
+    stats = None
+    if with_image_grad:
+        g = torch.Generator(device="cuda").manual_seed(5)
+        v_img = torch.randn(res.image.shape, generator=g, device="cuda")
+        stats = W.fused_raster_bwd(pb.splats, pb.tile_offsets, pb.flatten_ids, v_img, C, N,
+                                   128, 128, 16, pb.tile_offsets.size(2), pb.tile_offsets.size(1),
+                                   True)
+    sep, fused = {"grad2d": None, "count": None}, {"grad2d": None, "count": None}
+    for _ in range(2):  # two steps: accumulation
+        outs_a, v2, va = _explicit_outputs(st, params, stats, None)
+        means2d = torch.zeros(C, N, 2, device="cuda")
+        means2d.grad = v2 if stats is not None else torch.zeros_like(v2)
+        means2d.absgrad = va if stats is not None else torch.zeros_like(va)
+        info = {"means2d": means2d, "radii": res.radii.amax(-1), "width": 128, "height": 128,
+                "n_cameras": C}
+        update_densify_state(sep, info, absgrad=absgrad, track_radii=True)
+        acc = DensifyAccumulator(fused, absgrad=absgrad, track_radii=True)
+        outs_b, _, _ = _explicit_outputs(st, params, stats,
+                                         acc.launch_args(res.radii.contiguous(), 128, 128))
+        for a, b in zip(outs_a, outs_b):
+            assert torch.equal(a, b)
+    for key in ("grad2d", "count", "radii"):
+        assert torch.equal(sep[key], fused[key]), key
+    assert fused["count"].max() > 0
+    if with_image_grad:
+        assert fused["grad2d"].max() > 0
+    else:
+        assert fused["grad2d"].max() == 0
+
+
+def test_explicit_backward_densify_keyword():
+    """explicit_backward(densify=...) on two renders of the same scene: the
+    statistics agree with the separate pass to float rounding, the counts
+    exactly."""
+    from r2splat.ops.training import DensifyAccumulator, update_densify_state
+
+    sep, fused = {"grad2d": None, "count": None}, {"grad2d": None, "count": None}
+    p_sep, r_sep = _render_step(21)
+    update_densify_state(sep, {"means2d": r_sep.means2d, "radii": r_sep.radii.amax(-1),
+                               "width": 128, "height": 128, "n_cameras": 3}, absgrad=True)
+    p_fus, r_fus = _render_step(21, DensifyAccumulator(fused, absgrad=True))
+    for a, b in zip(p_sep, p_fus):
+        torch.testing.assert_close(a.grad, b.grad, rtol=1e-4, atol=1e-5)
+    assert torch.equal(sep["count"], fused["count"])
+    torch.testing.assert_close(sep["grad2d"], fused["grad2d"], rtol=1e-4, atol=1e-6)
+
+
+def test_fused_densify_without_screen_gradients():
+    from r2splat.ops.training import DensifyAccumulator
+
+    a, b = {"grad2d": None, "count": None}, {"grad2d": None, "count": None}
+    _, ra = _render_step(23, DensifyAccumulator(a))
+    _, rb = _render_step(23, DensifyAccumulator(b, store_screen_grads=False))
+    assert rb.means2d.grad is None and getattr(rb.means2d, "absgrad", None) is None
+    assert ra.means2d.absgrad is not None
+    assert torch.equal(a["count"], b["count"])
+    torch.testing.assert_close(a["grad2d"], b["grad2d"], rtol=1e-4, atol=1e-6)
+
+
+def test_fused_densify_argument_errors():
+    from r2splat.ops.training import DensifyAccumulator
+
+    with pytest.raises(RuntimeError, match="must be contiguous float32"):
+        _render_step(24, DensifyAccumulator({"grad2d": torch.zeros(5, device="cuda"),
+                                             "count": None}))
