@@ -19,11 +19,22 @@
 // times the conditioning a c / det for the rounding of the three-term sum,
 // absolute 2e-4 for the approximate log2 of the threshold); the interval
 // gets a further margin of 1e-2 px plus 1e-5 of the magnitudes that enter
-// the root for the rounding of the root itself.  Culling only drops pixels
-// the cut-off rejects, so the sums it feeds are unchanged.
+// the root (and of the offsets) for the rounding of the root itself.
+// Culling only drops pixels the cut-off rejects, so the sums it feeds are
+// unchanged.
+//
+// Voxels (brick_rows): the 3D splat passes where s(u, v, w) = d^T P d / 2
+// <= S with S = ln(|w| / 1e-6) (csrc/VoxelizeToVoxelsFwd.cu:182-214).  In the
+// slice w = dz the quadratic in (u, v) has the 2x2 block M = [[a, b], [b, d]]
+// of the conic P = [[a, b, c], [b, d, e], [c, e, f]], its centre shifted by
+// -M^-1 (c dz, e dz) and its minimum raised by dz^2 det(P) / (2 det(M)); each
+// slice keeps the rows of that ellipse's bounding box (and none when the box
+// misses the x range), with S first widened by the 3D conditioning
+// a d f / det(P) and the slice's level then by strip_range's 2D margins.
 #pragma once
 
 #include <math.h>
+#include <stdint.h>
 
 #ifdef __CUDACC__
 #define R2S_HD __host__ __device__ __forceinline__
@@ -82,9 +93,11 @@ R2S_HD void strip_range(float a, float b, float c, float S, float uL, float uR, 
         vlo = (-r - b * u0) / c;
         mlo = (fabsf(b * u0) + r) / c;
     }
-    // index i has offset v0 + i: keep i in [vlo - m - v0, vhi + m - v0]
-    const float flo = (vlo - (1e-2f + 1e-5f * mlo)) - v0;
-    const float fhi = (vhi + (1e-2f + 1e-5f * mhi)) - v0;
+    // index i has offset v0 + i: keep i in [vlo - m - v0, vhi + m - v0]; the
+    // margin also covers the rounding of offsets the caller shifted
+    const float mag = fabsf(v0) + fmaxf(fabsf(uL), fabsf(uR));
+    const float flo = (vlo - (1e-2f + 1e-5f * (mlo + mag))) - v0;
+    const float fhi = (vhi + (1e-2f + 1e-5f * (mhi + mag))) - v0;
     if (!(flo <= fhi)) return;  // rounding or NaN: keep the range
     const float flo_c = fminf(fmaxf(flo, (float)lo), (float)hi + 1.0f);
     const float fhi_c = fmaxf(fminf(fhi, (float)hi), (float)lo - 1.0f);
@@ -112,6 +125,72 @@ R2S_HD void tile_cull(float mx, float my, float a, float b, float c, float s_thr
     if (c_lo > c_hi) {
         r_lo = 1;
         r_hi = 0;
+    }
+}
+
+// Row ranges of a 3D splat in the eight z-slices of an 8x8x8 brick with
+// origin (X0, Y0, Z0), inside its culling box [xl, xh] x [yl, yh] x [zl, zh]:
+// byte k of (tab_lo, tab_hi) (slices 0-3, 4-7) = first row | last row << 4,
+// 0x0f for a slice with no row; [ezl, ezh] the slices with rows (ezl > ezh:
+// none).  q = (P00, P01, P02, P11, P12, P22) = (a, b, c, d, e, f); s_thr the
+// cut-off in log2 units (log2(|w| 1e6)).  Each slice is bounded by the
+// axis-aligned box of its ellipse: centre (du, dv) = dz (ku, kv) from the
+// mean, half-widths sqrt(2 S_z d / det M) and sqrt(2 S_z a / det M) at level
+// S_z = S' - ks dz^2; a slice whose box misses the culling box's x or y range
+// has no row.  Branch-free over the eight slices (one square root each); a
+// degenerate or ill-conditioned conic keeps the box's rows in every slice.
+R2S_HD void brick_rows(float mx, float my, float mz, const float q[6], float s_thr, float X0,
+                       float Y0, float Z0, int xl, int xh, int yl, int yh, int zl, int zh,
+                       uint32_t& tab_lo, uint32_t& tab_hi, int& ezl, int& ezh) {
+    tab_lo = tab_hi = 0x0f0f0f0fu;
+    ezl = 8;
+    ezh = -1;
+    if (xl > xh || yl > yh || zl > zh) return;
+    const float a = q[0], b = q[1], c = q[2], d = q[3], e = q[4], f = q[5];
+    const float S = s_thr * kCullLn2;
+    const float x0 = (X0 + 0.5f) - mx, y0 = (Y0 + 0.5f) - my;  // offsets of voxel 0
+    const float detM = a * d - b * b;
+    const float det3 = f * detM - a * e * e + 2.0f * b * c * e - d * c * c;
+    const float cond3 = (a * d * f) / det3, cond2 = (a * d) / detM;
+    const bool exact = a > 0.f && d > 0.f && f > 0.f && detM > 0.f && det3 > 0.f && S >= 0.f &&
+                       S < 1e30f && cond3 < 1e6f && cond2 < 1e6f && fabsf(x0) < 1e30f &&
+                       fabsf(y0) < 1e30f && fabsf(mz) < 1e30f;
+    // the 3D level with strip_range's margins on the 3D conditioning, then the
+    // 2D widening of each slice's level
+    const float Sm = S * (1.0f + 2e-4f + 1e-6f * cond3) + 2e-4f;
+    const float rel2 = 1.0f + 2e-4f + 1e-6f * cond2;
+    const float inv = 1.0f / detM;
+    const float ku = -(d * c - b * e) * inv, kv = -(a * e - b * c) * inv, ks = 0.5f * det3 * inv;
+    const float wu = sqrtf(2.0f * d * inv), wv = sqrtf(2.0f * a * inv);
+    for (int k = 0; k < 8; ++k) {
+        if (k < zl || k > zh) continue;
+        int lo = yl, hi = yh;
+        if (exact) {
+            const float dz = (Z0 + ((float)k + 0.5f)) - mz;
+            const float Sz = Sm - ks * dz * dz;
+            const float r = sqrtf(fmaxf(Sz * rel2 + 2e-4f, 0.0f));
+            const float cu = ku * dz, cv = kv * dz;
+            const float hu = r * wu, hv = r * wv;
+            // voxel i has offset x0 + i: keep i in [cu - hu - m - x0, cu + hu + m - x0]
+            const float mu_ = 1e-2f + 1e-5f * (fabsf(cu) + hu + fabsf(x0));
+            const float mv_ = 1e-2f + 1e-5f * (fabsf(cv) + hv + fabsf(y0));
+            const float fxl = (cu - hu - mu_) - x0, fxh = (cu + hu + mu_) - x0;
+            const float fyl = (cv - hv - mv_) - y0, fyh = (cv + hv + mv_) - y0;
+            const bool hit = Sz >= 0.f && fxl <= (float)xh && fxh >= (float)xl;
+            const int ylo = (int)ceilf(fminf(fmaxf(fyl, (float)yl), (float)yh + 1.0f));
+            const int yhi = (int)floorf(fmaxf(fminf(fyh, (float)yh), (float)yl - 1.0f));
+            lo = hit ? ylo : 1;
+            hi = hit ? yhi : 0;
+            if (!(fyl <= fyh)) lo = yl, hi = yh;  // NaN: keep the box
+        }
+        if (lo > hi) continue;
+        const uint32_t byte = (uint32_t)lo | ((uint32_t)hi << 4);
+        if (k < 4)
+            tab_lo = (tab_lo & ~(0xffu << (8 * k))) | (byte << (8 * k));
+        else
+            tab_hi = (tab_hi & ~(0xffu << (8 * (k - 4)))) | (byte << (8 * (k - 4)));
+        ezl = k < ezl ? k : ezl;
+        ezh = k;
     }
 }
 

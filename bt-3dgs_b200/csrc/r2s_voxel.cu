@@ -8,9 +8,11 @@
 // Gaussians whose cut-off box (alpha >= 1e-6) reaches its voxels.
 //
 // Backward (reference: csrc/VoxelizeToVoxelsBwd.cu:70-250 and 321-441): one
-// CTA per brick with the brick's upstream gradient in shared memory; warps
-// take whole Gaussians, walk the voxel box that can contribute and reduce ten
-// moments of the contributing voxels,
+// CTA per brick with the brick's upstream gradient in shared memory; the
+// float32 8^3 kernel gives each thread one record, narrows its culling box to
+// the rows of each z-slice that the ellipsoid's slice can reach (brick_rows in
+// r2s_cull.cuh), sorts the brick's records by their slice range, walks those
+// rows and reduces ten moments of the contributing voxels,
 //   S0 = sum v e, S_i = sum v e d_i, S_ij = sum v e d_i d_j (i <= j),
 // which map linearly to the reference gradients:
 //   v_means3d = w Q (Sx, Sy, Sz),   v_opacity = S0,
@@ -24,6 +26,7 @@
 #include <algorithm>
 
 #include "r2s_common.cuh"
+#include "r2s_cull.cuh"
 
 namespace r2s {
 
@@ -476,6 +479,18 @@ __device__ __forceinline__ VRecord load_vrecord(const float4* __restrict__ vspla
     return r;
 }
 
+// The natural conic (P00, P01, P02, P11, P12, P22) of a voxel splat record.
+__device__ __forceinline__ void raw_conic(const float4* __restrict__ vsplats, int64_t g,
+                                          float q[6]) {
+    const float4 a = vsplats[4 * g], b = vsplats[4 * g + 1], c = vsplats[4 * g + 2];
+    q[0] = a.w;
+    q[1] = b.x;
+    q[2] = b.y;
+    q[3] = b.z;
+    q[4] = b.w;
+    q[5] = c.x;
+}
+
 constexpr int kVFwd8Threads = 64;  // 2 warps; a warp owns four z-slices, a thread 4x2 voxels (x, z)
 constexpr int kVFwd8Batch = 128;
 
@@ -514,6 +529,8 @@ voxel_fwd8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict_
             cull_range_v(r.m[0], r.e[0], (float)X0, xmax, xl, xh);
             cull_range_v(r.m[1], r.e[1], (float)Y0, ymax, yl, yh);
             cull_range_v(r.m[2], r.e[2], (float)Z0, zmax, zl, zh);
+            // bit h: warp h's four slices meet the culling box (per-slice rows,
+            // brick_rows, cost more to stage here than the work they save)
             uint32_t msk = 0;
             if (xl <= xh && yl <= yh && zl <= zh) {
 #pragma unroll
@@ -572,20 +589,31 @@ voxel_fwd8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict_
 }
 
 constexpr int kVBwd8Threads = 256;  // one brick per CTA, one Gaussian record per thread
+constexpr int kVBwd8Batch = 1024;   // records staged and sorted per batch
 
-// Backward statistics of 8x8x8 bricks, one record per thread: the thread walks
-// the (y, z) rows of its culling box (a warp executes the union of its
-// lanes' rows) and the 8 voxels of each row in packed pairs.  Per-column sums
-// Col_x = sum v e over rows give S0, Sx, Sxx; per-row sums R0 = sum_x v e and
-// R1 = sum_x v e dx give the y/z moments, so every moment is a direct sum.
+// Backward statistics of 8x8x8 bricks, one record per thread.  Staging
+// narrows each record's culling box to the rows of every z-slice where its
+// ellipsoid reaches the brick (brick_rows: per-slice row ranges and the
+// slices that have rows) and counting-sorts each batch of 1024 records by
+// that slice range, so that a group of 32 lanes walks similar slices.  A
+// thread walks, per slice of its warp's union, the union of its lanes' rows
+// in that slice, and the 8 voxels of each row in packed pairs.  Per-column
+// sums Col_x = sum v e over rows give S0, Sx, Sxx; per-row sums R0 = sum_x v e
+// and R1 = sum_x v e dx give the y/z moments, so every moment is a direct sum.
 __global__ void __launch_bounds__(kVBwd8Threads)
 voxel_bwd8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict__ offsets,
                   const int32_t* __restrict__ flatten_ids, int64_t n_keys, int64_t n_isects,
                   const float* __restrict__ v_vol, uint32_t dim2, uint32_t dim1, uint32_t dim0,
                   uint32_t nt2, uint32_t nt1, uint32_t layer_begin, float* __restrict__ stats) {
     __shared__ __align__(16) float s_v[512];
+    __shared__ uint2 s_tab[kVBwd8Batch];     // per-slice rows (byte k: first | last << 4)
+    __shared__ int32_t s_g[kVBwd8Batch];
+    __shared__ uint8_t s_zr[kVBwd8Batch];    // first slice | last slice << 4; 0x0f: none
+    __shared__ uint16_t s_perm[kVBwd8Batch];
+    __shared__ int32_t s_cnt[65];            // bucket 64: records that reach no voxel
+    __shared__ int s_next;                   // next group to take
 
-    const int tid = threadIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint32_t bz = blockIdx.z + layer_begin;
     const int64_t key = ((int64_t)blockIdx.z * nt1 + blockIdx.y) * nt2 + blockIdx.x;
     const int X0 = blockIdx.x * 8, Y0 = blockIdx.y * 8, Z0 = bz * 8;
@@ -602,91 +630,153 @@ voxel_bwd8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict_
                      ? v_vol[((Z0 + z - zoff) * (int64_t)dim1 + (Y0 + y)) * dim2 + X0 + x]
                      : 0.f;
     }
-    __syncthreads();
     const float X0f = (float)X0, Y0f = (float)Y0, Z0f = (float)Z0;
 
-    // the trip count is the same for every thread: warp votes stay convergent
-    for (int base = start; base < end; base += kVBwd8Threads) {
-        const int i = base + tid;
-        int64_t g = 0;
-        VRecord r{};
-        int xl = 1, xh = 0, yl = 1, yh = 0, zl = 1, zh = 0;
-        if (i < end) {
-            g = flatten_ids[i];
-            r = load_vrecord(vsplats, g);
-            cull_range_v(r.m[0], r.e[0], X0f, xmax, xl, xh);
-            cull_range_v(r.m[1], r.e[1], Y0f, ymax, yl, yh);
-            cull_range_v(r.m[2], r.e[2], Z0f, zmax, zl, zh);
-        }
-        const bool live = xl <= xh && yl <= yh && zl <= zh;
-        if (!live) yl = zl = 8, yh = zh = -1;
-        const int z0 = __reduce_min_sync(0xffffffffu, zl);
-        const int z1 = __reduce_max_sync(0xffffffffu, zh);
-        const int y0 = __reduce_min_sync(0xffffffffu, yl);
-        const int y1 = __reduce_max_sync(0xffffffffu, yh);
-        if (z0 > z1) continue;
-
-        const int thr_n = thr_neg_v(s_threshold_v(r.w));
-        const float2 A2 = make_float2(r.A, r.A);
-        float2 dx[4], col[4];
+    for (int base = start; base < end; base += kVBwd8Batch) {
+        if (tid < 65) s_cnt[tid] = 0;
+        __syncthreads();
+        constexpr int kPer = kVBwd8Batch / kVBwd8Threads;
+        int bucket[kPer], rank[kPer];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            dx[j] = make_float2((X0f + (2 * j + 0.5f)) - r.m[0], (X0f + (2 * j + 1.5f)) - r.m[0]);
-            col[j] = make_float2(0.f, 0.f);
+        for (int k = 0; k < kPer; ++k) {
+            const int idx = k * kVBwd8Threads + tid;
+            const int i = base + idx;
+            int32_t g = 0;
+            uint32_t tlo = 0x0f0f0f0fu, thi = 0x0f0f0f0fu;
+            int ezl = 8, ezh = -1;
+            if (i < end) {
+                g = flatten_ids[i];
+                const VRecord r = load_vrecord(vsplats, g);
+                int xl, xh, yl, yh, zl, zh;
+                cull_range_v(r.m[0], r.e[0], X0f, xmax, xl, xh);
+                cull_range_v(r.m[1], r.e[1], Y0f, ymax, yl, yh);
+                cull_range_v(r.m[2], r.e[2], Z0f, zmax, zl, zh);
+                float q[6];
+                raw_conic(vsplats, g, q);
+                brick_rows(r.m[0], r.m[1], r.m[2], q, s_threshold_v(r.w), X0f, Y0f, Z0f, xl, xh,
+                           yl, yh, zl, zh, tlo, thi, ezl, ezh);
+            }
+            const bool live = ezl <= ezh;
+            bucket[k] = live ? ezl * 8 + ezh : 64;
+            s_g[idx] = g;
+            s_tab[idx] = make_uint2(tlo, thi);
+            s_zr[idx] = live ? (uint8_t)(ezl | (ezh << 4)) : (uint8_t)0x0f;
+            rank[k] = atomicAdd(&s_cnt[bucket[k]], 1);
         }
-        float Sy = 0.f, Sz = 0.f, Syy = 0.f, Syz = 0.f, Szz = 0.f, Sxy = 0.f, Sxz = 0.f;
-        for (int z = z0; z <= z1; ++z) {
-            const bool zin = z >= zl && z <= zh;
-            const float dz = (Z0f + ((float)z + 0.5f)) - r.m[2];
-            const float cdz = r.Cq * dz, edz = r.E * dz, fzz = r.F * dz * dz;
-            for (int y = y0; y <= y1; ++y) {
-                const bool rin = zin && y >= yl && y <= yh;
-                const float dy = (Y0f + ((float)y + 0.5f)) - r.m[1];
-                const float by = fmaf(r.B, dy, cdz);
-                const float rest = fmaf(dy, fmaf(r.D, dy, edz), fzz);
-                const float2 by2 = make_float2(by, by), rest2 = make_float2(rest, rest);
-                const float4* vr = reinterpret_cast<const float4*>(s_v + z * 64 + y * 8);
-                const float4 va = vr[0], vb = vr[1];
-                float2 r0 = make_float2(0.f, 0.f), r1 = r0;
+        __syncthreads();
+        if (warp == 0) {  // exclusive scan of the 65 bucket counts, 3 per lane
+            int c[3], sum = 0;
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const float2 v2 = j == 0   ? make_float2(va.x, va.y)
-                                      : j == 1 ? make_float2(va.z, va.w)
-                                      : j == 2 ? make_float2(vb.x, vb.y)
-                                               : make_float2(vb.z, vb.w);
-                    const float2 sn = ffma2(dx[j], ffma2(A2, dx[j], by2), rest2);  // -s
-                    float e0 = exp2f(sn.x), e1 = exp2f(sn.y);
-                    e0 = (rin && sn_valid_v(sn.x, thr_n)) ? e0 : 0.f;
-                    e1 = (rin && sn_valid_v(sn.y, thr_n)) ? e1 : 0.f;
-                    const float2 ve = fmul2(v2, make_float2(e0, e1));
-                    col[j] = fadd2(col[j], ve);
-                    r0 = fadd2(r0, ve);
-                    r1 = ffma2(ve, dx[j], r1);
-                }
-                const float R0 = r0.x + r0.y, R1 = r1.x + r1.y;
-                Sy = fmaf(dy, R0, Sy);
-                Sz = fmaf(dz, R0, Sz);
-                Syy = fmaf(dy * dy, R0, Syy);
-                Syz = fmaf(dy * dz, R0, Syz);
-                Szz = fmaf(dz * dz, R0, Szz);
-                Sxy = fmaf(dy, R1, Sxy);
-                Sxz = fmaf(dz, R1, Sxz);
+            for (int j = 0; j < 3; ++j) {
+                const int b = lane * 3 + j;
+                c[j] = b < 65 ? s_cnt[b] : 0;
+                sum += c[j];
+            }
+            const int excl = warp_inclusive_scan(sum) - sum;
+            int run = excl;
+#pragma unroll
+            for (int j = 0; j < 3; ++j) {
+                const int b = lane * 3 + j;
+                if (b < 65) s_cnt[b] = run;
+                run += c[j];
             }
         }
-        if (!live) continue;
-        float S0 = 0.f, Sx = 0.f, Sxx = 0.f;
+        __syncthreads();
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            S0 += col[j].x + col[j].y;
-            const float2 cx = fmul2(col[j], dx[j]);
-            Sx += cx.x + cx.y;
-            Sxx = fmaf(cx.x, dx[j].x, Sxx);
-            Sxx = fmaf(cx.y, dx[j].y, Sxx);
+        for (int k = 0; k < kPer; ++k)
+            s_perm[s_cnt[bucket[k]] + rank[k]] = (uint16_t)(k * kVBwd8Threads + tid);
+        if (tid == 0) s_next = kVBwd8Threads / 32;
+        __syncthreads();
+        const int n_groups = (min(kVBwd8Batch, end - base) + 31) >> 5;
+
+        // groups are taken from a shared counter: sorted groups differ in cost
+        auto process = [&](int grp) {
+            const int idx = s_perm[grp * 32 + lane];
+            const uint32_t zr = s_zr[idx];
+            const int zl = zr & 15, zh = zr >> 4;
+            const bool live = zl <= zh;
+            const int z0 = __reduce_min_sync(0xffffffffu, live ? zl : 15);
+            const int z1 = __reduce_max_sync(0xffffffffu, live ? zh : 0);
+            if (z0 > z1) return;  // warp-uniform
+            const int64_t g = s_g[idx];
+            const uint2 tab = s_tab[idx];
+            const VRecord r = load_vrecord(vsplats, g);
+
+            const int thr_n = thr_neg_v(s_threshold_v(r.w));
+            const float2 A2 = make_float2(r.A, r.A);
+            float2 dx[4], col[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                dx[j] = make_float2((X0f + (2 * j + 0.5f)) - r.m[0], (X0f + (2 * j + 1.5f)) - r.m[0]);
+                col[j] = make_float2(0.f, 0.f);
+            }
+            float Sy = 0.f, Sz = 0.f, Syy = 0.f, Syz = 0.f, Szz = 0.f, Sxy = 0.f, Sxz = 0.f;
+            for (int z = z0; z <= z1; ++z) {
+                const uint32_t byte = ((z < 4 ? tab.x : tab.y) >> (8 * (z & 3))) & 0xffu;
+                const int ylo = live ? (int)(byte & 15u) : 15, yhi = live ? (int)(byte >> 4) : 0;
+                const int y0 = __reduce_min_sync(0xffffffffu, ylo);
+                const int y1 = __reduce_max_sync(0xffffffffu, yhi);
+                if (y0 > y1) continue;  // warp-uniform: no row of this slice
+                const float dz = (Z0f + ((float)z + 0.5f)) - r.m[2];
+                const float cdz = r.Cq * dz, edz = r.E * dz, fzz = r.F * dz * dz;
+                for (int y = y0; y <= y1; ++y) {
+                    const bool rin = y >= ylo && y <= yhi;
+                    const float dy = (Y0f + ((float)y + 0.5f)) - r.m[1];
+                    const float by = fmaf(r.B, dy, cdz);
+                    const float rest = fmaf(dy, fmaf(r.D, dy, edz), fzz);
+                    const float2 by2 = make_float2(by, by), rest2 = make_float2(rest, rest);
+                    const float4* vr = reinterpret_cast<const float4*>(s_v + z * 64 + y * 8);
+                    const float4 va = vr[0], vb = vr[1];
+                    float2 r0 = make_float2(0.f, 0.f), r1 = r0;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const float2 v2 = j == 0   ? make_float2(va.x, va.y)
+                                          : j == 1 ? make_float2(va.z, va.w)
+                                          : j == 2 ? make_float2(vb.x, vb.y)
+                                                   : make_float2(vb.z, vb.w);
+                        const float2 sn = ffma2(dx[j], ffma2(A2, dx[j], by2), rest2);  // -s
+                        float e0 = exp2f(sn.x), e1 = exp2f(sn.y);
+                        e0 = (rin && sn_valid_v(sn.x, thr_n)) ? e0 : 0.f;
+                        e1 = (rin && sn_valid_v(sn.y, thr_n)) ? e1 : 0.f;
+                        const float2 ve = fmul2(v2, make_float2(e0, e1));
+                        col[j] = fadd2(col[j], ve);
+                        r0 = fadd2(r0, ve);
+                        r1 = ffma2(ve, dx[j], r1);
+                    }
+                    const float R0 = r0.x + r0.y, R1 = r1.x + r1.y;
+                    Sy = fmaf(dy, R0, Sy);
+                    Sz = fmaf(dz, R0, Sz);
+                    Syy = fmaf(dy * dy, R0, Syy);
+                    Syz = fmaf(dy * dz, R0, Syz);
+                    Szz = fmaf(dz * dz, R0, Szz);
+                    Sxy = fmaf(dy, R1, Sxy);
+                    Sxz = fmaf(dz, R1, Sxz);
+                }
+            }
+            if (!live) return;
+            float S0 = 0.f, Sx = 0.f, Sxx = 0.f;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                S0 += col[j].x + col[j].y;
+                const float2 cx = fmul2(col[j], dx[j]);
+                Sx += cx.x + cx.y;
+                Sxx = fmaf(cx.x, dx[j].x, Sxx);
+                Sxx = fmaf(cx.y, dx[j].y, Sxx);
+            }
+            float* st = stats + g * 12;
+            red_add_v4(st, S0, Sx, Sy, Sz);
+            red_add_v4(st + 4, Sxx, Sxy, Sxz, Syy);
+            red_add_v2(st + 8, Syz, Szz);
+                };
+        int grp = warp;
+        while (grp < n_groups) {
+            process(grp);
+            __syncwarp();
+            int nxt = 0;
+            if (lane == 0) nxt = atomicAdd(&s_next, 1);
+            grp = __shfl_sync(0xffffffffu, nxt, 0);
         }
-        float* st = stats + g * 12;
-        red_add_v4(st, S0, Sx, Sy, Sz);
-        red_add_v4(st + 4, Sxx, Sxy, Sxz, Syy);
-        red_add_v2(st + 8, Syz, Szz);
+        __syncthreads();
     }
 }
 

@@ -142,3 +142,79 @@ def test_tile_cull_keeps_degenerate_records(probe):
     for k in range(len(rows)):
         assert out[k, 4] == 0
         assert tuple(out[k, :4]) == (0, 15, 0, 15), (rows[k], out[k])
+
+
+def _rotations(rng, n):
+    q = rng.standard_normal((n, 4))
+    q /= np.linalg.norm(q, axis=1, keepdims=True)
+    w, x, y, z = q.T
+    return np.stack([
+        np.stack([1 - 2 * (y * y + z * z), 2 * (x * y - w * z), 2 * (x * z + w * y)], -1),
+        np.stack([2 * (x * y + w * z), 1 - 2 * (x * x + z * z), 2 * (y * z - w * x)], -1),
+        np.stack([2 * (x * z - w * y), 2 * (y * z + w * x), 1 - 2 * (x * x + y * y)], -1)], -2)
+
+
+def _cases3(rng, n, lo, hi, max_cond=None, snap=False):
+    s = np.exp(rng.uniform(np.log(lo), np.log(hi), (n, 3)))
+    if max_cond is not None:
+        s[:, 2] = s[:, 0] / np.sqrt(np.exp(rng.uniform(0, np.log(max_cond), n)))
+    R = _rotations(rng, n)
+    P = R @ (np.eye(3)[None] / (s * s)[:, None, :]) @ R.transpose(0, 2, 1)  # conic = R S^-2 R^T
+    q = np.stack([P[:, 0, 0], P[:, 0, 1], P[:, 0, 2], P[:, 1, 1], P[:, 1, 2], P[:, 2, 2]], -1)
+    w = np.exp(rng.uniform(np.log(1e-6), np.log(20.0), n)) * rng.choice([-1.0, 1.0], n)
+    org = 8.0 * rng.integers(0, 32, (n, 3))
+    reach = 4.0 + np.minimum(4.0 * s.max(1), 2000.0)
+    m = org + 4.0 + rng.uniform(-1, 1, (n, 3)) * reach[:, None]
+    if snap:
+        m = np.floor(m) + rng.choice([0.0, 0.5], (n, 3))
+    return np.concatenate([m, q, w[:, None], org], 1).astype(np.float32)
+
+
+@pytest.fixture(scope="module")
+def probe3(probe, tmp_path_factory):
+    import glob
+    lib = ctypes.CDLL(glob.glob(str(tmp_path_factory.getbasetemp() / "cull*" / "libcullprobe.so"))[0])
+    lib.cull_probe3.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p]
+
+    def run(cases, boxes):
+        cases = np.ascontiguousarray(cases, dtype=np.float32)
+        boxes = np.ascontiguousarray(boxes, dtype=np.int32)
+        out = np.zeros((len(cases), 4), dtype=np.int32)
+        lib.cull_probe3(cases.ctypes.data, boxes.ctypes.data, len(cases), out.ctypes.data)
+        return out
+
+    return run
+
+
+def _boxes3(rng, n, random_box):
+    if not random_box:
+        return np.tile(np.array([[0, 7, 0, 7, 0, 7]], np.int32), (n, 1))
+    lo = rng.integers(0, 8, (n, 3))
+    hi = np.minimum(lo + rng.integers(0, 8, (n, 3)), 7)
+    return np.stack([lo[:, 0], hi[:, 0], lo[:, 1], hi[:, 1], lo[:, 2], hi[:, 2]], -1).astype(np.int32)
+
+
+@pytest.mark.parametrize("kind", ["realistic", "tiny", "huge", "ill_conditioned", "snapped",
+                                  "random_boxes"])
+def test_brick_rows_never_drop_a_passing_voxel(probe3, kind):
+    rng = np.random.default_rng(["realistic", "tiny", "huge", "ill_conditioned", "snapped",
+                                 "random_boxes"].index(kind) + 31)
+    n = 20000
+    args = {"realistic": (0.3, 30.0), "tiny": (0.02, 0.5), "huge": (50.0, 2000.0),
+            "ill_conditioned": (0.5, 50.0), "snapped": (0.3, 20.0),
+            "random_boxes": (0.3, 30.0)}[kind]
+    cases = _cases3(rng, n, *args, max_cond=1e6 if kind == "ill_conditioned" else None,
+                    snap=kind == "snapped")
+    out = probe3(cases, _boxes3(rng, n, kind == "random_boxes"))
+    bad = np.nonzero(out[:, 0])[0]
+    assert len(bad) == 0, f"{len(bad)} cases drop passing voxels, first: {cases[bad[0]]} -> {out[bad[0]]}"
+
+
+def test_brick_rows_are_tight(probe3):
+    rng = np.random.default_rng(7)
+    n = 20000
+    out = probe3(_cases3(rng, n, 1.0, 10.0), _boxes3(rng, n, False))
+    live = out[:, 3] > 0
+    assert (out[live, 2] >= out[live, 1]).all()
+    # at most about one spare row per slice on average
+    assert out[live, 2].mean() <= out[live, 1].mean() * 1.15 + 1.0
