@@ -436,7 +436,13 @@ class OursTrain:
                                   radius_clip=wl.RADIUS_CLIP)
         out = self.loss(res.image[..., None], d.targets[views][..., None],
                         d.edge[views][..., None], vox.volume)
-        out["total"].backward()
+        if self.world > 1:  # gradients summed over ranks = the one-GPU step's gradients
+            objective = shard.data_parallel_objective(
+                out, self.loss.w_l1, self.loss.w_ssim, self.loss.w_tv, len(views),
+                TRAIN_VIEWS_PER_STEP, self.world)
+        else:
+            objective = out["total"]
+        objective.backward()
         # densification statistics in the backward kernel; every rank adds its
         # own views with the step's global camera count, so the sum of the
         # ranks' states (taken when the strategy reads them) is the one-GPU state

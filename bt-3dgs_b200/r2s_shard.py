@@ -115,3 +115,19 @@ class GradientAllReduce:
             g.copy_(self.flat[off:off + g.numel()].view_as(g))
             off += g.numel()
         return list(grads)
+
+
+def data_parallel_objective(out: dict, w_l1: float, w_ssim: float, w_tv: float,
+                            n_local_views: int, n_total_views: int, world: int) -> torch.Tensor:
+    """The scalar a rank backpropagates so that the sum of the ranks'
+    gradients equals the one-process gradient of the training loss
+    (BinaryTreeLossComputer, src/utils/loss.py:125-172) over all the step's
+    views.  ``out`` is the loss computer's dict for this rank's views.
+
+    L1, SSIM and the edge term are means over (view, pixel) with per-view
+    SSIM windows, so a rank's mean over its own views weighted by
+    n_local / n_total sums to the mean over all views.  Every rank evaluates
+    the same TV sub-volume, so TV is weighted 1 / world."""
+    frac = float(n_local_views) / float(n_total_views)
+    proj = w_l1 * out["proj_l1"] + w_ssim * out["proj_ssim"] + out["edge_weight"] * out["edge"]
+    return frac * proj + (w_tv / float(world)) * out["vol_tv"]

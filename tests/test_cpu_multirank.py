@@ -209,3 +209,40 @@ def test_layer_weights_from_packed_rects():
             (pack(3, 3), pack(0, 1), pack(0, 4), 0)]   # empty in x
     rects = torch.tensor(rows, dtype=torch.int64).to(torch.int32).contiguous().view(torch.uint8)
     assert shard.layer_weights(rects, 4) == [6.0, 6.0, 7.0, 1.0]
+
+
+@pytest.mark.parametrize("split", [(4, 4), (3, 5), (1, 2, 5)])
+def test_data_parallel_objective_sums_to_the_single_process_gradient(split):
+    """Ranks holding view blocks of one training step backpropagate
+    data_parallel_objective; the summed gradients equal the gradients of the
+    full loss (BinaryTreeLossComputer over all views, TV once)."""
+    import r2s_shard as shard
+    from oracle import r2s_oracle as O
+
+    w = dict(w_l1=0.8, w_ssim=0.2, w_tv=0.05, w_edge=0.1)
+    g = torch.Generator().manual_seed(4)
+    C, H = sum(split), 24
+    renders = torch.rand(C, H, H, 1, generator=g, dtype=torch.float64)
+    targets = torch.rand(C, H, H, 1, generator=g, dtype=torch.float64)
+    edge = (torch.rand(C, H, H, 1, generator=g) < 0.3).double()
+    vol = torch.rand(10, 10, 10, generator=g, dtype=torch.float64)
+
+    r_full = renders.clone().requires_grad_(True)
+    v_full = vol.clone().requires_grad_(True)
+    O.binary_tree_losses(r_full, targets, edge, v_full, **w)["total"].backward()
+
+    grad_r = torch.zeros_like(renders)
+    grad_v = torch.zeros_like(vol)
+    v0 = 0
+    for n in split:
+        r = renders[v0:v0 + n].clone().requires_grad_(True)
+        v = vol.clone().requires_grad_(True)
+        out = O.binary_tree_losses(r, targets[v0:v0 + n], edge[v0:v0 + n], v, **w)
+        out["edge_weight"] = torch.tensor(w["w_edge"], dtype=torch.float64)
+        shard.data_parallel_objective(out, w["w_l1"], w["w_ssim"], w["w_tv"], n, C,
+                                      len(split)).backward()
+        grad_r[v0:v0 + n] = r.grad
+        grad_v += v.grad
+        v0 += n
+    torch.testing.assert_close(grad_r, r_full.grad, rtol=1e-12, atol=1e-15)
+    torch.testing.assert_close(grad_v, v_full.grad, rtol=1e-12, atol=1e-15)
