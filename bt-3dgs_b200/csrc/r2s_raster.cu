@@ -464,14 +464,15 @@ __device__ __forceinline__ float s_threshold(float wmu) {
 }
 
 constexpr int kFwd16Threads = 128;  // 4 warps, each covering the whole tile for a quarter of the list
-constexpr int kFwd16Batch = 128;
+constexpr int kFwd16Batch = 256;
 
 // Forward of 16x16 tiles.  Every warp covers all 256 pixels of the tile (lane
 // L: column L & 15, rows (L >> 4) + 2k), so a warp evaluates one record at a
 // time with no per-warp work list.  A record reaches a contiguous range
 // [g0, g1] of the four 4-row groups (its culling box narrowed to the ellipse,
-// tile_cull); staging sorts each batch by that range, one of ten patterns,
-// with a deterministic counting sort (ballots, thread order), and the warps
+// tile_cull); staging (two records per thread, batches of 256) sorts each
+// batch by that range, one of ten patterns, with a deterministic counting
+// sort (ballots, slot order), and the warps
 // take every fourth record of each pattern's run through a loop compiled for
 // that pattern: no per-record group tests, straight-line group bodies.  Each
 // group is 2 pixels per lane in packed pairs.  The four warps' partial sums
@@ -484,9 +485,9 @@ raster_fwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict
     __shared__ float4 s_p[kFwd16Batch];  // mx, my, A = a/2 log2e, B = b log2e
     __shared__ float4 s_q[kFwd16Batch];  // C = c/2 log2e, w*mu, s_thr, 0
     __shared__ float s_acc[kFwd16Threads / 32][256];
-    __shared__ int s_wc[kFwd16Threads / 32][11];  // per-warp pattern counts, then slots
+    __shared__ int s_wc[2 * kFwd16Threads / 32][11];  // per-(half, warp) pattern counts, then slots
     __shared__ int s_off[12];                     // first slot of each pattern's run
-    __shared__ uint8_t s_perm[kFwd16Batch];       // staged records in pattern order
+    __shared__ uint16_t s_perm[kFwd16Batch];      // staged records in pattern order
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int64_t cam = blockIdx.z;
@@ -507,9 +508,11 @@ raster_fwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict
     for (int b0 = start; b0 < end; b0 += kFwd16Batch) {
         const int n = min(kFwd16Batch, end - b0);
         __syncthreads();
-        int pid = 10;  // row-group pattern of the record; 10: no pixel
-        if (tid < n) {
-            const int64_t g = flatten_ids[b0 + tid];
+        int pid[2] = {10, 10};  // row-group pattern of the records; 10: no pixel
+        for (int k = 0; k < 2; ++k) {
+            const int ti = k * kFwd16Threads + tid;
+            if (ti >= n) continue;
+            const int64_t g = flatten_ids[b0 + ti];
             const float4 p = splats[2 * g];
             const float4 q = splats[2 * g + 1];
             int c_lo, c_hi, r_lo, r_hi;
@@ -520,30 +523,32 @@ raster_fwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict
                       r_hi);
             if (c_lo <= c_hi && r_lo <= r_hi) {  // (g0, g1) -> 0..9, g0 <= g1
                 const int g0 = r_lo >> 2, g1 = r_hi >> 2;
-                pid = g0 * 4 + g1 - (g0 * (g0 + 1)) / 2;
+                pid[k] = g0 * 4 + g1 - (g0 * (g0 + 1)) / 2;
             }
             // negated coefficients: the packed chain yields -s exactly, so ex2
             // takes it as is; the cut-off test compares the bits of -s as
             // signed integers against INT_MIN + bits(s_thr)
-            s_p[tid] = make_float4(p.x, p.y, -0.5f * kLog2e * p.z, -kLog2e * p.w);
-            s_q[tid] = make_float4(-0.5f * kLog2e * q.x, q.y,
+            s_p[ti] = make_float4(p.x, p.y, -0.5f * kLog2e * p.z, -kLog2e * p.w);
+            s_q[ti] = make_float4(-0.5f * kLog2e * q.x, q.y,
                                    __uint_as_float(__float_as_uint(s_thr) ^ 0x80000000u), 0.f);
         }
-        {  // deterministic counting sort of the batch by pattern (ballots, tid order)
+        {  // deterministic counting sort of the batch by pattern (ballots, slot order)
             const unsigned below = (1u << lane) - 1u;
-            int rank = 0;
+            int rank[2] = {0, 0};
 #pragma unroll
-            for (int p = 0; p < 11; ++p) {
-                const unsigned bm = __ballot_sync(0xffffffffu, pid == p);
-                if (pid == p) rank = __popc(bm & below);
-                if (lane == 0) s_wc[warp][p] = __popc(bm);
-            }
+            for (int k = 0; k < 2; ++k)
+#pragma unroll
+                for (int p = 0; p < 11; ++p) {
+                    const unsigned bm = __ballot_sync(0xffffffffu, pid[k] == p);
+                    if (pid[k] == p) rank[k] = __popc(bm & below);
+                    if (lane == 0) s_wc[k * (kFwd16Threads / 32) + warp][p] = __popc(bm);
+                }
             __syncthreads();
             if (tid == 0) {
                 int run = 0;
                 for (int p = 0; p < 11; ++p) {
                     s_off[p] = run;
-                    for (int w = 0; w < kFwd16Threads / 32; ++w) {
+                    for (int w = 0; w < 2 * kFwd16Threads / 32; ++w) {
                         const int c = s_wc[w][p];
                         s_wc[w][p] = run;
                         run += c;
@@ -552,7 +557,11 @@ raster_fwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict
                 s_off[11] = run;
             }
             __syncthreads();
-            if (pid < 10) s_perm[s_wc[warp][pid] + rank] = (uint8_t)tid;
+#pragma unroll
+            for (int k = 0; k < 2; ++k)
+                if (pid[k] < 10)
+                    s_perm[s_wc[k * (kFwd16Threads / 32) + warp][pid[k]] + rank[k]] =
+                        (uint16_t)(k * kFwd16Threads + tid);
         }
         __syncthreads();
         auto run = [&](auto c0, auto c1, int b, int e) {
