@@ -277,10 +277,12 @@ class OursVoxel:
                                                    wl.RADIUS_CLIP)
             S = self.l1 - self.l0
             offs, fids, _ = W.fused_bin(rects, S, m.size(0), nt * nt, nt, 1, segment_base=self.l0)
+            rows = W.fused_voxel_rows(vs, offs, fids, m.size(0), G, G, G, wl.VOL_TILE, nt, nt, nt,
+                                      self.l0, self.l1)
             vol = W.fused_voxel_fwd(vs, offs, fids, m.size(0), G, G, G, wl.VOL_TILE, nt, nt, nt,
-                                    self.l0, self.l1)
+                                    self.l0, self.l1, rows=rows)
             stats = W.fused_voxel_bwd(vs, offs, fids, self.v_vol, m.size(0), G, G, G,
-                                      wl.VOL_TILE, nt, nt, nt, self.l0, self.l1)
+                                      wl.VOL_TILE, nt, nt, nt, self.l0, self.l1, rows=rows)
             outs = [torch.empty_like(t) for t in (m, q, s, o)]
             W.fused_explicit_backward(m, q, s, o, wl.SCALE_MIN, wl.SCALE_MAX, None, None, 0, 0,
                                       wl.EPS2D, None, None, None, self.rng, self.ctr, G, G, G,
@@ -890,10 +892,10 @@ def main():
     barrier(world)
     # our kernels per timed step: projection = prepare, project_splats, binning
     # (count, column scan, scan, place), raster forward, raster backward,
-    # explicit backward; voxel = prepare, map, binning (4), voxel forward,
-    # voxel backward, explicit backward
+    # explicit backward; voxel = prepare, map, binning (4), row table, voxel
+    # forward, voxel backward, explicit backward
     gpu_launches = args.steps * 9
-    vox_launches = args.steps * 9
+    vox_launches = args.steps * 10
     if rank != 0:
         return
     line = {

@@ -491,14 +491,64 @@ __device__ __forceinline__ void raw_conic(const float4* __restrict__ vsplats, in
     q[5] = c.x;
 }
 
+// First and last slice with rows of a brick_rows table (ezl > ezh: none).
+__device__ __forceinline__ void table_slices(uint32_t tlo, uint32_t thi, int& ezl, int& ezh) {
+    ezl = 8;
+    ezh = -1;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const uint32_t byte = ((k < 4 ? tlo : thi) >> (8 * (k & 3))) & 0xffu;
+        if ((byte & 15u) <= (byte >> 4)) {
+            ezl = min(ezl, k);
+            ezh = k;
+        }
+    }
+}
+
+// Row table of every (record, brick) pair of the brick lists: rows[i] =
+// brick_rows of record i against its brick (per-slice first | last row,
+// 0x0f for none).  One CTA per brick; computed once per binning and read by
+// the forward and the backward, so neither pays for it in its staging.
+constexpr int kVRowsThreads = 128;
+
+__global__ void __launch_bounds__(kVRowsThreads)
+voxel_rows8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict__ offsets,
+                   const int32_t* __restrict__ flatten_ids, int64_t n_keys, int64_t n_isects,
+                   uint32_t dim2, uint32_t dim1, uint32_t dim0, uint32_t nt2, uint32_t nt1,
+                   uint32_t layer_begin, uint2* __restrict__ rows) {
+    const uint32_t bz = blockIdx.z + layer_begin;
+    const int64_t key = ((int64_t)blockIdx.z * nt1 + blockIdx.y) * nt2 + blockIdx.x;
+    const int X0 = blockIdx.x * 8, Y0 = blockIdx.y * 8, Z0 = bz * 8;
+    const int xmax = min(7, (int)dim2 - 1 - X0);
+    const int ymax = min(7, (int)dim1 - 1 - Y0);
+    const int zmax = min(7, (int)dim0 - 1 - Z0);
+    const int start = offsets[key];
+    const int end = key + 1 < n_keys ? offsets[key + 1] : (int)n_isects;
+    for (int i = start + threadIdx.x; i < end; i += kVRowsThreads) {
+        const int64_t g = flatten_ids[i];
+        const VRecord r = load_vrecord(vsplats, g);
+        int xl, xh, yl, yh, zl, zh;
+        cull_range_v(r.m[0], r.e[0], (float)X0, xmax, xl, xh);
+        cull_range_v(r.m[1], r.e[1], (float)Y0, ymax, yl, yh);
+        cull_range_v(r.m[2], r.e[2], (float)Z0, zmax, zl, zh);
+        float q[6];
+        raw_conic(vsplats, g, q);
+        uint32_t tlo, thi;
+        int ezl, ezh;
+        brick_rows(r.m[0], r.m[1], r.m[2], q, s_threshold_v(r.w), (float)X0, (float)Y0,
+                   (float)Z0, xl, xh, yl, yh, zl, zh, tlo, thi, ezl, ezh);
+        rows[i] = make_uint2(tlo, thi);
+    }
+}
+
 constexpr int kVFwd8Threads = 64;  // 2 warps; a warp owns four z-slices, a thread 4x2 voxels (x, z)
 constexpr int kVFwd8Batch = 128;
 
 __global__ void __launch_bounds__(kVFwd8Threads)
 voxel_fwd8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict__ offsets,
-                  const int32_t* __restrict__ flatten_ids, int64_t n_keys, int64_t n_isects,
-                  uint32_t dim2, uint32_t dim1, uint32_t dim0, uint32_t nt2, uint32_t nt1,
-                  uint32_t layer_begin, float* __restrict__ vol) {
+                  const int32_t* __restrict__ flatten_ids, const uint2* __restrict__ rows,
+                  int64_t n_keys, int64_t n_isects, uint32_t dim2, uint32_t dim1, uint32_t dim0,
+                  uint32_t nt2, uint32_t nt1, uint32_t layer_begin, float* __restrict__ vol) {
     __shared__ float4 s_a[kVFwd8Batch];  // mx, my, mz, A
     __shared__ float4 s_b[kVFwd8Batch];  // B, Cq, D, E
     __shared__ float4 s_c[kVFwd8Batch];  // F, w, s threshold, warp mask (bits)
@@ -529,10 +579,17 @@ voxel_fwd8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict_
             cull_range_v(r.m[0], r.e[0], (float)X0, xmax, xl, xh);
             cull_range_v(r.m[1], r.e[1], (float)Y0, ymax, yl, yh);
             cull_range_v(r.m[2], r.e[2], (float)Z0, zmax, zl, zh);
-            // bit h: warp h's four slices meet the culling box (per-slice rows,
-            // brick_rows, cost more to stage here than the work they save)
+            // bit h: warp h's four slices can hold a passing voxel -- from the
+            // row table when there is one, else from the culling box
             uint32_t msk = 0;
-            if (xl <= xh && yl <= yh && zl <= zh) {
+            if (rows != nullptr) {
+                const uint2 tab = rows[b0 + j];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    const uint32_t byte = ((k < 4 ? tab.x : tab.y) >> (8 * (k & 3))) & 0xffu;
+                    if ((byte & 15u) <= (byte >> 4)) msk |= 1u << (k >> 2);
+                }
+            } else if (xl <= xh && yl <= yh && zl <= zh) {
 #pragma unroll
                 for (int k = 0; k < 2; ++k)
                     if (zl <= 4 * k + 3 && zh >= 4 * k) msk |= 1u << k;
@@ -602,9 +659,10 @@ constexpr int kVBwd8Batch = 1024;   // records staged and sorted per batch
 // and R1 = sum_x v e dx give the y/z moments, so every moment is a direct sum.
 __global__ void __launch_bounds__(kVBwd8Threads)
 voxel_bwd8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict__ offsets,
-                  const int32_t* __restrict__ flatten_ids, int64_t n_keys, int64_t n_isects,
-                  const float* __restrict__ v_vol, uint32_t dim2, uint32_t dim1, uint32_t dim0,
-                  uint32_t nt2, uint32_t nt1, uint32_t layer_begin, float* __restrict__ stats) {
+                  const int32_t* __restrict__ flatten_ids, const uint2* __restrict__ rows,
+                  int64_t n_keys, int64_t n_isects, const float* __restrict__ v_vol,
+                  uint32_t dim2, uint32_t dim1, uint32_t dim0, uint32_t nt2, uint32_t nt1,
+                  uint32_t layer_begin, float* __restrict__ stats) {
     __shared__ __align__(16) float s_v[512];
     __shared__ uint2 s_tab[kVBwd8Batch];     // per-slice rows (byte k: first | last << 4)
     __shared__ int32_t s_g[kVBwd8Batch];
@@ -646,15 +704,22 @@ voxel_bwd8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict_
             int ezl = 8, ezh = -1;
             if (i < end) {
                 g = flatten_ids[i];
-                const VRecord r = load_vrecord(vsplats, g);
-                int xl, xh, yl, yh, zl, zh;
-                cull_range_v(r.m[0], r.e[0], X0f, xmax, xl, xh);
-                cull_range_v(r.m[1], r.e[1], Y0f, ymax, yl, yh);
-                cull_range_v(r.m[2], r.e[2], Z0f, zmax, zl, zh);
-                float q[6];
-                raw_conic(vsplats, g, q);
-                brick_rows(r.m[0], r.m[1], r.m[2], q, s_threshold_v(r.w), X0f, Y0f, Z0f, xl, xh,
-                           yl, yh, zl, zh, tlo, thi, ezl, ezh);
+                if (rows != nullptr) {
+                    const uint2 tab = rows[i];
+                    tlo = tab.x;
+                    thi = tab.y;
+                    table_slices(tlo, thi, ezl, ezh);
+                } else {
+                    const VRecord r = load_vrecord(vsplats, g);
+                    int xl, xh, yl, yh, zl, zh;
+                    cull_range_v(r.m[0], r.e[0], X0f, xmax, xl, xh);
+                    cull_range_v(r.m[1], r.e[1], Y0f, ymax, yl, yh);
+                    cull_range_v(r.m[2], r.e[2], Z0f, zmax, zl, zh);
+                    float q[6];
+                    raw_conic(vsplats, g, q);
+                    brick_rows(r.m[0], r.m[1], r.m[2], q, s_threshold_v(r.w), X0f, Y0f, Z0f, xl,
+                               xh, yl, yh, zl, zh, tlo, thi, ezl, ezh);
+                }
             }
             const bool live = ezl <= ezh;
             bucket[k] = live ? ezl * 8 + ezh : 64;
@@ -919,8 +984,28 @@ extern "C" int r2s_voxelize_to_voxels_bwd(int dtype, int mode, const void* means
     });
 }
 
+extern "C" int r2s_voxel_rows_f32(const float* vsplats, const int32_t* offsets,
+                                  const int32_t* flatten_ids, int64_t N, int64_t n_isects,
+                                  uint32_t dim2, uint32_t dim1, uint32_t dim0, uint32_t T,
+                                  uint32_t nt2, uint32_t nt1, uint32_t nt0, uint32_t layer_begin,
+                                  uint32_t layer_end, uint32_t* rows, r2s_stream_t stream) {
+    R2S_REQUIRE(N >= 0 && n_isects >= 0, "voxel_rows: negative size");
+    R2S_REQUIRE(T == 8, "voxel_rows: the row table is built for 8-voxel bricks");
+    R2S_REQUIRE(layer_begin <= layer_end && layer_end <= nt0, "voxel_rows: bad layer range");
+    if (int rc = check_bricks(T, nt2, nt1, nt0)) return rc;
+    if (N == 0 || n_isects == 0 || layer_end == layer_begin) return R2S_OK;
+    R2S_REQUIRE(rows != nullptr, "voxel_rows: null output");
+    const dim3 grid(nt2, nt1, layer_end - layer_begin);
+    voxel_rows8_kernel<<<grid, kVRowsThreads, 0, stream>>>(
+        (const float4*)vsplats, offsets, flatten_ids,
+        (int64_t)(layer_end - layer_begin) * nt1 * nt2, n_isects, dim2, dim1, dim0, nt2, nt1,
+        layer_begin, reinterpret_cast<uint2*>(rows));
+    return check_launch("voxel_rows");
+}
+
 extern "C" int r2s_voxel_splats_fwd_f32(const float* vsplats, const int32_t* offsets,
-                                        const int32_t* flatten_ids, int64_t N, int64_t n_isects,
+                                        const int32_t* flatten_ids, const uint32_t* rows,
+                                        int64_t N, int64_t n_isects,
                                         uint32_t dim2, uint32_t dim1, uint32_t dim0, uint32_t T,
                                         uint32_t nt2, uint32_t nt1, uint32_t nt0,
                                         uint32_t layer_begin, uint32_t layer_end, float* volume,
@@ -938,7 +1023,7 @@ extern "C" int r2s_voxel_splats_fwd_f32(const float* vsplats, const int32_t* off
     if (T == 8) {
         const dim3 grid(nt2, nt1, layer_end - layer_begin);
         voxel_fwd8_kernel<<<grid, kVFwd8Threads, 0, stream>>>(
-            (const float4*)vsplats, offsets, flatten_ids,
+            (const float4*)vsplats, offsets, flatten_ids, reinterpret_cast<const uint2*>(rows),
             (int64_t)(layer_end - layer_begin) * nt1 * nt2, n_isects, dim2, dim1, dim0, nt2, nt1,
             layer_begin, volume);
         return check_launch("voxel_splats_fwd");
@@ -949,7 +1034,8 @@ extern "C" int r2s_voxel_splats_fwd_f32(const float* vsplats, const int32_t* off
 }
 
 extern "C" int r2s_voxel_splats_bwd_f32(const float* vsplats, const int32_t* offsets,
-                                        const int32_t* flatten_ids, const float* v_volume,
+                                        const int32_t* flatten_ids, const uint32_t* rows,
+                                        const float* v_volume,
                                         int64_t N, int64_t n_isects, uint32_t dim2, uint32_t dim1,
                                         uint32_t dim0, uint32_t T, uint32_t nt2, uint32_t nt1,
                                         uint32_t nt0, uint32_t layer_begin, uint32_t layer_end,
@@ -963,7 +1049,7 @@ extern "C" int r2s_voxel_splats_bwd_f32(const float* vsplats, const int32_t* off
         if (n_isects > 0 && layer_end > layer_begin) {
             const dim3 grid(nt2, nt1, layer_end - layer_begin);
             voxel_bwd8_kernel<<<grid, kVBwd8Threads, 0, stream>>>(
-                (const float4*)vsplats, offsets, flatten_ids,
+                (const float4*)vsplats, offsets, flatten_ids, reinterpret_cast<const uint2*>(rows),
                 (int64_t)(layer_end - layer_begin) * nt1 * nt2, n_isects, v_volume, dim2, dim1,
                 dim0, nt2, nt1, layer_begin, stats);
         }

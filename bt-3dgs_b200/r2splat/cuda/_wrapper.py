@@ -730,8 +730,24 @@ def fused_map(means, covars, opacities, ranges, centers, dim2, dim1, dim0, tile,
     return means3d, conics, radii, vsplats, rects, counts
 
 
+def fused_voxel_rows(vsplats, offsets, flatten_ids, N, dim2, dim1, dim0, tile, nt2, nt1, nt0,
+                     layer_begin=0, layer_end=None):
+    """Row table [n_isects, 2] (int32 bit patterns) of a 3D binning with
+    8-voxel bricks, or None for other brick sizes."""
+    if tile != 8:
+        return None
+    dev = vsplats.device
+    if layer_end is None:
+        layer_end = nt0
+    rows = torch.empty((flatten_ids.numel(), 2), dtype=torch.int32, device=dev)
+    _call("r2s_voxel_rows_f32", _ptr(vsplats), _ptr(offsets), _ptr(flatten_ids), N,
+          flatten_ids.numel(), dim2, dim1, dim0, tile, nt2, nt1, nt0, layer_begin, layer_end,
+          _ptr(rows), _stream(dev))
+    return rows
+
+
 def fused_voxel_fwd(vsplats, offsets, flatten_ids, N, dim2, dim1, dim0, tile, nt2, nt1, nt0,
-                    layer_begin=0, layer_end=None, out=None):
+                    layer_begin=0, layer_end=None, out=None, rows=None):
     dev = vsplats.device
     if layer_end is None:
         layer_end = nt0
@@ -739,19 +755,19 @@ def fused_voxel_fwd(vsplats, offsets, flatten_ids, N, dim2, dim1, dim0, tile, nt
     z1 = min(layer_end * tile, dim0)
     if out is None:
         out = torch.empty((max(z1 - z0, 0), dim1, dim2), dtype=torch.float32, device=dev)
-    _call("r2s_voxel_splats_fwd_f32", _ptr(vsplats), _ptr(offsets), _ptr(flatten_ids), N,
-          flatten_ids.numel(), dim2, dim1, dim0, tile, nt2, nt1, nt0, layer_begin, layer_end,
+    _call("r2s_voxel_splats_fwd_f32", _ptr(vsplats), _ptr(offsets), _ptr(flatten_ids), _ptr(rows),
+          N, flatten_ids.numel(), dim2, dim1, dim0, tile, nt2, nt1, nt0, layer_begin, layer_end,
           _ptr(out), _stream(dev))
     return out
 
 
 def fused_voxel_bwd(vsplats, offsets, flatten_ids, v_volume, N, dim2, dim1, dim0, tile, nt2, nt1,
-                    nt0, layer_begin=0, layer_end=None):
+                    nt0, layer_begin=0, layer_end=None, rows=None):
     dev = vsplats.device
     if layer_end is None:
         layer_end = nt0
     stats = torch.empty((N, 12), dtype=torch.float32, device=dev)
-    _call("r2s_voxel_splats_bwd_f32", _ptr(vsplats), _ptr(offsets), _ptr(flatten_ids),
+    _call("r2s_voxel_splats_bwd_f32", _ptr(vsplats), _ptr(offsets), _ptr(flatten_ids), _ptr(rows),
           _ptr(v_volume), N, flatten_ids.numel(), dim2, dim1, dim0, tile, nt2, nt1, nt0,
           layer_begin, layer_end, _ptr(stats), _stream(dev))
     return stats

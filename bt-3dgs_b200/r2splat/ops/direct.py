@@ -96,6 +96,8 @@ class VoxelForwardBuffers:
     conics: Optional[torch.Tensor] = None
     opacity: Optional[torch.Tensor] = None
     isect_ids: Optional[torch.Tensor] = None
+    # float32 8-voxel bricks: per-record row table of the binning (r2s_voxel_rows_f32)
+    rows: Optional[torch.Tensor] = None
 
 
 def _fast(*tensors: torch.Tensor) -> bool:
@@ -310,13 +312,15 @@ def _voxelize_forward(
                 nt1, nt0, eps3d, radius_clip)
             offsets, flatten_ids, _ = W.fused_bin(rects, nt0, N, nt1 * nt2, nt2, 1)
             tile_offsets = offsets.view(nt0, nt1, nt2)
+            rows = W.fused_voxel_rows(vsplats, tile_offsets, flatten_ids, N, dim2, dim1, dim0,
+                                      tile_size, nt2, nt1, nt0)
             output = W.fused_voxel_fwd(vsplats, tile_offsets, flatten_ids, N, dim2, dim1, dim0,
-                                       tile_size, nt2, nt1, nt0)
+                                       tile_size, nt2, nt1, nt0, rows=rows)
         return VoxelForwardBuffers(
             output=output, means3d=means3d, radii=radii, tile_offsets=tile_offsets,
             flatten_ids=flatten_ids, ranges=ranges_c, centers=centers_c, dim2=dim2, dim1=dim1,
             dim0=dim0, tile_size=tile_size, eps3d=float(eps3d), vsplats=vsplats, conics=conics,
-            opacity=opac)
+            opacity=opac, rows=rows)
 
     # reference operator chain (r2splat/ops/direct.py:284-326)
     means3d, conics, radii = W.world_to_volume_mapping_fwd(

@@ -237,7 +237,7 @@ def _explicit_backward_fused(state, means, quats, raw_scales, raw_opacities,
             vox_stats = W.fused_voxel_bwd(
                 vb.vsplats, vb.tile_offsets, vb.flatten_ids, vox.output.grad.contiguous(), N,
                 vb.dim2, vb.dim1, vb.dim0, vb.tile_size, vb.tile_offsets.size(2),
-                vb.tile_offsets.size(1), vb.tile_offsets.size(0))
+                vb.tile_offsets.size(1), vb.tile_offsets.size(0), rows=vb.rows)
 
         params = (means, quats, raw_scales, raw_opacities)
         accumulate = all(_inplace_grad_ok(p) for p in params)

@@ -393,17 +393,32 @@ R2S_API int r2s_map_vsplats_f32(const float* means, const float* covars, const f
                         uint32_t nt1, uint32_t nt0, double eps3d, double radius_clip,
                         float* means3d, float* conics, int32_t* radii, float* vsplats,
                         void* rects3, int32_t* tiles_per_gauss, r2s_stream_t stream);
-/* Voxelize bricks [z_begin/8 .. ) from voxel splat records; `volume` points
- * at voxel row z_begin of a [dim0,dim1,dim2] grid (z-slab output). */
-R2S_API int r2s_voxel_splats_fwd_f32(const float* vsplats, const int32_t* tile_offsets,
+/* Row table of the (record, brick) pairs of a 3D binning with 8-voxel bricks
+ * (the voxel path of VoxelizeToVoxelsFwd.cu / VoxelizeToVoxelsBwd.cu has no
+ * such table; it is this build's culling): rows[2 i], rows[2 i + 1] = for
+ * record i, byte k = first row | last row << 4 of z-slice k of its brick that
+ * its ellipsoid can reach, 0x0f for none.  Read by the two entry points
+ * below, which then skip their own culling of those records. */
+R2S_API int r2s_voxel_rows_f32(const float* vsplats, const int32_t* tile_offsets,
                              const int32_t* flatten_ids, int64_t N, int64_t n_isects,
                              uint32_t dim2, uint32_t dim1, uint32_t dim0, uint32_t tile_size,
                              uint32_t nt2, uint32_t nt1, uint32_t nt0, uint32_t layer_begin,
-                             uint32_t layer_end, float* volume, r2s_stream_t stream);
+                             uint32_t layer_end, uint32_t* rows, r2s_stream_t stream);
+/* Voxelize bricks [z_begin/8 .. ) from voxel splat records; `volume` points
+ * at voxel row z_begin of a [dim0,dim1,dim2] grid (z-slab output).  `rows`:
+ * the row table of the same binning, or NULL. */
+R2S_API int r2s_voxel_splats_fwd_f32(const float* vsplats, const int32_t* tile_offsets,
+                             const int32_t* flatten_ids, const uint32_t* rows, int64_t N,
+                             int64_t n_isects, uint32_t dim2, uint32_t dim1, uint32_t dim0,
+                             uint32_t tile_size, uint32_t nt2, uint32_t nt1, uint32_t nt0,
+                             uint32_t layer_begin, uint32_t layer_end, float* volume,
+                             r2s_stream_t stream);
 /* Voxel backward statistics [N, 12] = (S0, Sx, Sy, Sz, Sxx, Sxy, Sxz, Syy,
- * Syz, Szz, 0, 0), accumulated over bricks; zeroes `stats` first. */
+ * Syz, Szz, 0, 0), accumulated over bricks; zeroes `stats` first.  `rows`:
+ * the row table of the same binning, or NULL. */
 R2S_API int r2s_voxel_splats_bwd_f32(const float* vsplats, const int32_t* tile_offsets,
-                             const int32_t* flatten_ids, const float* v_volume, int64_t N,
+                             const int32_t* flatten_ids, const uint32_t* rows,
+                             const float* v_volume, int64_t N,
                              int64_t n_isects, uint32_t dim2, uint32_t dim1, uint32_t dim0,
                              uint32_t tile_size, uint32_t nt2, uint32_t nt1, uint32_t nt0,
                              uint32_t layer_begin, uint32_t layer_end, float* stats,
