@@ -655,14 +655,15 @@ def dominant_kernel_roofline(proj: OursProjection, hbm_peak, peak_kind, clock_mh
     C, N = pb.means2d.shape[:2]
     ntx, nty = pb.tile_offsets.size(2), pb.tile_offsets.size(1)
     batches = pb.view_batches or [(0, C, pb.flatten_ids)]
+    culls = pb.cull if isinstance(pb.cull, list) else [pb.cull]
     n_isects = sum(ids.numel() for _, _, ids in batches)
     stats = torch.empty((C * N, 8), dtype=torch.float32, device=pb.splats.device)
 
     def launch():
-        for c0, c1, ids in batches:
+        for (c0, c1, ids), cull in zip(batches, culls):
             W.fused_raster_bwd(pb.splats[c0:c1], pb.tile_offsets[c0:c1], ids, proj.v_img[c0:c1],
                                c1 - c0, N, proj.det, proj.det, wl.IMG_TILE, ntx, nty, True,
-                               out=stats[c0 * N:c1 * N])
+                               out=stats[c0 * N:c1 * N], cull=cull)
 
     launch()
     ms = kernel_time(launch)

@@ -463,6 +463,18 @@ __device__ __forceinline__ float s_threshold(float wmu) {
     return a >= 1.0f ? log2f(a) : -1.0f;  // negative: nothing passes
 }
 
+// Culling ranges of one (record, tile) pair after tile_cull, 4 bits each:
+// c_lo | c_hi << 4 | r_lo << 8 | r_hi << 12 (an empty range stays empty).
+__device__ __forceinline__ uint16_t pack_cull(int c_lo, int c_hi, int r_lo, int r_hi) {
+    return (uint16_t)((c_lo & 15) | ((c_hi & 15) << 4) | ((r_lo & 15) << 8) | ((r_hi & 15) << 12));
+}
+__device__ __forceinline__ void unpack_cull(uint16_t v, int& c_lo, int& c_hi, int& r_lo, int& r_hi) {
+    c_lo = v & 15;
+    c_hi = (v >> 4) & 15;
+    r_lo = (v >> 8) & 15;
+    r_hi = v >> 12;
+}
+
 constexpr int kFwd16Threads = 128;  // 4 warps, each covering the whole tile for a quarter of the list
 constexpr int kFwd16Batch = 256;
 
@@ -481,7 +493,8 @@ constexpr int kFwd16Batch = 256;
 __global__ void __launch_bounds__(kFwd16Threads, 10)
 raster_fwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict__ offsets,
                     const int32_t* __restrict__ flatten_ids, int64_t n_keys, int64_t n_isects,
-                    uint32_t W, uint32_t H, uint32_t ntx, uint32_t nty, float* __restrict__ image) {
+                    uint32_t W, uint32_t H, uint32_t ntx, uint32_t nty, float* __restrict__ image,
+                    uint16_t* __restrict__ cull_out) {
     __shared__ float4 s_p[kFwd16Batch];  // mx, my, A = a/2 log2e, B = b log2e
     __shared__ float4 s_q[kFwd16Batch];  // C = c/2 log2e, w*mu, s_thr, 0
     __shared__ float s_acc[kFwd16Threads / 32][256];
@@ -525,6 +538,7 @@ raster_fwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict
                 const int g0 = r_lo >> 2, g1 = r_hi >> 2;
                 pid[k] = g0 * 4 + g1 - (g0 * (g0 + 1)) / 2;
             }
+            if (cull_out != nullptr) cull_out[b0 + ti] = pack_cull(c_lo, c_hi, r_lo, r_hi);
             // negated coefficients: the packed chain yields -s exactly, so ex2
             // takes it as is; the cut-off test compares the bits of -s as
             // signed integers against INT_MIN + bits(s_thr)
@@ -643,7 +657,8 @@ __global__ void __launch_bounds__(kBwd16Threads)
 raster_bwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict__ offsets,
                     const int32_t* __restrict__ flatten_ids, int64_t n_keys, int64_t n_isects,
                     const float* __restrict__ v_image, uint32_t W, uint32_t H, uint32_t ntx,
-                    uint32_t nty, float* __restrict__ stats) {
+                    uint32_t nty, const uint16_t* __restrict__ cull_in,
+                    float* __restrict__ stats) {
     // upstream gradient of the tile, row-major and (16 floats further, so
     // that the two copies sit in different banks) column-major
     __shared__ __align__(16) float s_vv[2 * 256 + 16];
@@ -694,10 +709,14 @@ raster_bwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict
                 p = splats[2 * (int64_t)g];
                 q = splats[2 * (int64_t)g + 1];
                 int c_lo, c_hi, r_lo, r_hi;
-                cull_range(p.x, q.z, X0f, cmax, c_lo, c_hi);
-                cull_range(p.y, q.w, Y0f, rmax, r_lo, r_hi);
-                tile_cull(p.x, p.y, p.z, p.w, q.x, s_threshold(q.y), X0f, Y0f, c_lo, c_hi, r_lo,
-                          r_hi);
+                if (cull_in != nullptr) {  // the forward's ranges for this record
+                    unpack_cull(cull_in[i], c_lo, c_hi, r_lo, r_hi);
+                } else {
+                    cull_range(p.x, q.z, X0f, cmax, c_lo, c_hi);
+                    cull_range(p.y, q.w, Y0f, rmax, r_lo, r_hi);
+                    tile_cull(p.x, p.y, p.z, p.w, q.x, s_threshold(q.y), X0f, Y0f, c_lo, c_hi,
+                              r_lo, r_hi);
+                }
                 if (c_lo <= c_hi && r_lo <= r_hi) {
                     if (c_hi - c_lo < r_hi - r_lo) {
                         // fewer columns than rows: walk the columns, with the
@@ -865,28 +884,30 @@ int check_tiles(int64_t C, uint32_t W, uint32_t H, uint32_t T, uint32_t ntx, uin
 
 int launch_raster_fwd16(const float4* splats, const int32_t* offsets, const int32_t* flatten_ids,
                         int64_t C, int64_t n_isects, uint32_t W, uint32_t H, uint32_t ntx,
-                        uint32_t nty, float* image, cudaStream_t stream) {
+                        uint32_t nty, float* image, cudaStream_t stream,
+                        uint16_t* cull_out = nullptr) {
     const dim3 grid(ntx, nty, (unsigned)C);
     raster_fwd16_kernel<<<grid, kFwd16Threads, 0, stream>>>(
-        splats, offsets, flatten_ids, C * (int64_t)ntx * nty, n_isects, W, H, ntx, nty, image);
+        splats, offsets, flatten_ids, C * (int64_t)ntx * nty, n_isects, W, H, ntx, nty, image,
+        cull_out);
     return check_launch("rasterize_to_pixels_fwd");
 }
 
 int launch_raster_bwd16(const float4* splats, const int32_t* offsets, const int32_t* flatten_ids,
                         const float* v_image, int64_t C, int64_t N, int64_t n_isects, uint32_t W,
                         uint32_t H, uint32_t ntx, uint32_t nty, int with_abs, float* stats,
-                        cudaStream_t stream) {
+                        cudaStream_t stream, const uint16_t* cull_in = nullptr) {
     cudaMemsetAsync(stats, 0, (size_t)C * N * 8 * sizeof(float), stream);
     if (n_isects == 0) return check_launch("rasterize_to_pixels_bwd");
     const dim3 grid(ntx, nty, (unsigned)C);
     if (with_abs)
         raster_bwd16_kernel<true><<<grid, kBwd16Threads, 0, stream>>>(
             splats, offsets, flatten_ids, C * (int64_t)ntx * nty, n_isects, v_image, W, H, ntx,
-            nty, stats);
+            nty, cull_in, stats);
     else
         raster_bwd16_kernel<false><<<grid, kBwd16Threads, 0, stream>>>(
             splats, offsets, flatten_ids, C * (int64_t)ntx * nty, n_isects, v_image, W, H, ntx,
-            nty, stats);
+            nty, cull_in, stats);
     return check_launch("rasterize_to_pixels_bwd");
 }
 
@@ -1021,8 +1042,10 @@ extern "C" int r2s_raster_splats_fwd_f32(const float* splats, const int32_t* off
                                          const int32_t* flatten_ids, int64_t C, int64_t N,
                                          int64_t n_isects, uint32_t W, uint32_t H, uint32_t T,
                                          uint32_t ntx, uint32_t nty, float* image,
-                                         r2s_stream_t stream) {
+                                         uint16_t* cull_ranges, r2s_stream_t stream) {
     R2S_REQUIRE(C >= 0 && N >= 0 && n_isects >= 0, "raster_splats_fwd: negative size");
+    R2S_REQUIRE(cull_ranges == nullptr || T == 16,
+                "raster_splats_fwd: the culling table is built for 16-pixel tiles");
     if (C == 0 || (int64_t)W * H == 0) return R2S_OK;
     if (N == 0 || n_isects == 0) {
         cudaMemsetAsync(image, 0, (size_t)C * W * H * 4, stream);
@@ -1031,7 +1054,7 @@ extern "C" int r2s_raster_splats_fwd_f32(const float* splats, const int32_t* off
     if (int rc = check_tiles(C, W, H, T, ntx, nty)) return rc;
     if (T == 16)
         return launch_raster_fwd16((const float4*)splats, offsets, flatten_ids, C, n_isects, W, H,
-                                   ntx, nty, image, stream);
+                                   ntx, nty, image, stream, cull_ranges);
     RasterSrc<float> src{(const float4*)splats, nullptr, nullptr, nullptr, nullptr};
     return launch_raster_fwd<float, true>(src, offsets, flatten_ids, C, n_isects, W, H, T, ntx,
                                           nty, image, stream);
@@ -1041,8 +1064,11 @@ extern "C" int r2s_raster_splats_bwd_f32(const float* splats, const int32_t* off
                                          const int32_t* flatten_ids, const float* v_image,
                                          int64_t C, int64_t N, int64_t n_isects, uint32_t W,
                                          uint32_t H, uint32_t T, uint32_t ntx, uint32_t nty,
-                                         int with_abs, float* stats, r2s_stream_t stream) {
+                                         int with_abs, const uint16_t* cull_ranges, float* stats,
+                                         r2s_stream_t stream) {
     R2S_REQUIRE(C >= 0 && N >= 0 && n_isects >= 0, "raster_splats_bwd: negative size");
+    R2S_REQUIRE(cull_ranges == nullptr || T == 16,
+                "raster_splats_bwd: the culling table is built for 16-pixel tiles");
     if (C * N == 0) return R2S_OK;
     if ((int64_t)W * H == 0) {
         cudaMemsetAsync(stats, 0, (size_t)C * N * 32, stream);
@@ -1051,7 +1077,7 @@ extern "C" int r2s_raster_splats_bwd_f32(const float* splats, const int32_t* off
     if (int rc = check_tiles(C, W, H, T, ntx, nty)) return rc;
     if (T == 16)
         return launch_raster_bwd16((const float4*)splats, offsets, flatten_ids, v_image, C, N,
-                                   n_isects, W, H, ntx, nty, with_abs, stats, stream);
+                                   n_isects, W, H, ntx, nty, with_abs, stats, stream, cull_ranges);
     RasterSrc<float> src{(const float4*)splats, nullptr, nullptr, nullptr, nullptr};
     return launch_raster_bwd<float, true, 0>(src, offsets, flatten_ids, v_image, C, N, n_isects, W,
                                              H, T, ntx, nty, with_abs, stats, stream);

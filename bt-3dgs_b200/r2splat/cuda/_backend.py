@@ -96,9 +96,9 @@ _SIGNATURES = {
         [_p, _p, _p, _p, _p, _i64, _i64, _u32, _u32, _u32, _u32, _u32, _f64, _f64, _p, _p, _p, _p,
          _p, _p], _i32),
     "r2s_raster_splats_fwd_f32": (
-        [_p, _p, _p, _i64, _i64, _i64, _u32, _u32, _u32, _u32, _u32, _p, _p], _i32),
+        [_p, _p, _p, _i64, _i64, _i64, _u32, _u32, _u32, _u32, _u32, _p, _p, _p], _i32),
     "r2s_raster_splats_bwd_f32": (
-        [_p, _p, _p, _p, _i64, _i64, _i64, _u32, _u32, _u32, _u32, _u32, _i32, _p, _p], _i32),
+        [_p, _p, _p, _p, _i64, _i64, _i64, _u32, _u32, _u32, _u32, _u32, _i32, _p, _p, _p], _i32),
     "r2s_map_vsplats_f32": (
         [_p, _p, _p, _p, _p, _i64, _u32, _u32, _u32, _u32, _u32, _u32, _u32, _f64, _f64, _p, _p,
          _p, _p, _p, _p, _p], _i32),

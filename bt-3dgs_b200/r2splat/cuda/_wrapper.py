@@ -668,22 +668,26 @@ def fused_bin(rects, S, N, T, tiles_x, layered, want_keys=False, segment_base=0,
     return offsets[: S * T], flatten_ids, isect_ids
 
 
-def fused_raster_fwd(splats, offsets, flatten_ids, C, N, W, H, tile, ntx, nty, out=None):
+def fused_raster_fwd(splats, offsets, flatten_ids, C, N, W, H, tile, ntx, nty, out=None,
+                     cull=None):
+    """``cull``: an int16 [n_isects] tensor that receives the records'
+    culling ranges (16-pixel tiles only), or None."""
     dev = splats.device
     if out is None:
         out = torch.empty((C, H, W), dtype=torch.float32, device=dev)
     _call("r2s_raster_splats_fwd_f32", _ptr(splats), _ptr(offsets), _ptr(flatten_ids), C, N,
-          flatten_ids.numel(), W, H, tile, ntx, nty, _ptr(out), _stream(dev))
+          flatten_ids.numel(), W, H, tile, ntx, nty, _ptr(out), _ptr(cull), _stream(dev))
     return out
 
 
 def fused_raster_bwd(splats, offsets, flatten_ids, v_image, C, N, W, H, tile, ntx, nty, with_abs,
-                     out=None):
+                     out=None, cull=None):
+    """``cull``: the table fused_raster_fwd wrote for the same binning, or None."""
     dev = splats.device
     stats = torch.empty((C * N, 8), dtype=torch.float32, device=dev) if out is None else out
     _call("r2s_raster_splats_bwd_f32", _ptr(splats), _ptr(offsets), _ptr(flatten_ids),
           _ptr(v_image), C, N, flatten_ids.numel(), W, H, tile, ntx, nty, 1 if with_abs else 0,
-          _ptr(stats), _stream(dev))
+          _ptr(cull), _ptr(stats), _stream(dev))
     return stats
 
 

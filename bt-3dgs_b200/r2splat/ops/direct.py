@@ -69,6 +69,10 @@ class ProjectionForwardBuffers:
     # [(c0, c1, flatten_ids)] per contiguous view batch; the batch's rows of
     # tile_offsets index its own flatten_ids (flatten_ids above is then empty)
     view_batches: Optional[list] = None
+    # float32 16x16 tiles, explicit (training) renders: the records' culling
+    # ranges written by the forward for the backward (a tensor, or one per
+    # view batch)
+    cull: Optional[object] = None
     cov2d: Optional[torch.Tensor] = None
     conics: Optional[torch.Tensor] = None
     mus: Optional[torch.Tensor] = None
@@ -163,6 +167,7 @@ def _rasterize_forward(
     tile_size: int,
     eps2d: float,
     radius_clip: float,
+    keep_cull: bool = False,
 ) -> ProjectionForwardBuffers:
     from ..cuda import _wrapper as W
 
@@ -197,8 +202,10 @@ def _rasterize_forward(
             if binned is not None:
                 offsets, flatten_ids, _ = binned
                 tile_offsets = offsets.view(n_cameras, nty, ntx)
+                cull = (torch.empty(flatten_ids.shape, dtype=torch.int16, device=means_c.device)
+                        if keep_cull and tile_size == 16 else None)
                 output = W.fused_raster_fwd(splats, tile_offsets, flatten_ids, n_cameras, N,
-                                            img_w, img_h, tile_size, ntx, nty)
+                                            img_w, img_h, tile_size, ntx, nty, cull=cull)
                 view_batches = None
             else:
                 # more records than one int32 binning holds: bin and rasterize
@@ -209,6 +216,7 @@ def _rasterize_forward(
                 output = torch.empty((n_cameras, img_h, img_w), dtype=torch.float32,
                                      device=means_c.device)
                 view_batches = []
+                cull = [] if keep_cull and tile_size == 16 else None
                 for c0, c1 in batches:
                     rb = rects[c0 * N * 8:c1 * N * 8]
                     binned = W.fused_bin(rb, c1 - c0, N, T, ntx, 0,
@@ -219,14 +227,20 @@ def _rasterize_forward(
                             "intersection records (int32 tile offsets)")
                     offs_b, ids_b, _ = binned
                     tile_offsets[c0:c1] = offs_b.view(c1 - c0, nty, ntx)
+                    cull_b = (torch.empty(ids_b.shape, dtype=torch.int16, device=means_c.device)
+                              if cull is not None else None)
                     W.fused_raster_fwd(splats[c0:c1], tile_offsets[c0:c1], ids_b, c1 - c0, N,
-                                       img_w, img_h, tile_size, ntx, nty, out=output[c0:c1])
+                                       img_w, img_h, tile_size, ntx, nty, out=output[c0:c1],
+                                       cull=cull_b)
                     view_batches.append((c0, c1, ids_b))
+                    if cull is not None:
+                        cull.append(cull_b)
                 flatten_ids = torch.empty((0,), dtype=torch.int32, device=means_c.device)
         return ProjectionForwardBuffers(
             output=output, means2d=means2d, radii=radii, tile_offsets=tile_offsets,
             flatten_ids=flatten_ids, viewmats=viewmats_c, Ks=Ks_c, img_w=img_w, img_h=img_h,
-            tile_size=tile_size, eps2d=float(eps2d), splats=splats, view_batches=view_batches)
+            tile_size=tile_size, eps2d=float(eps2d), splats=splats, view_batches=view_batches,
+            cull=cull)
 
     # reference operator chain (r2splat/ops/direct.py:166-201)
     means2d, cov2d, radii = W.world_to_image_projection_fwd(

@@ -110,7 +110,7 @@ def explicit_rasterize(
         raise RuntimeError("An explicit Gaussian state can only be rasterized once.")
     buffers = _rasterize_forward(
         means, state.covars, state.opacities, viewmats, Ks, img_w=img_w, img_h=img_h,
-        tile_size=tile_size, eps2d=eps2d, radius_clip=radius_clip)
+        tile_size=tile_size, eps2d=eps2d, radius_clip=radius_clip, keep_cull=True)
     output = buffers.output.detach().requires_grad_(True)
     means2d = buffers.means2d.detach().requires_grad_(True)
     state.projection = ExplicitProjectionContext(
@@ -206,14 +206,15 @@ def _explicit_backward_fused(state, means, quats, raw_scales, raw_opacities,
             if pb.view_batches is None:
                 raster_stats = W.fused_raster_bwd(
                     pb.splats, pb.tile_offsets, pb.flatten_ids, v_image, C, N, pb.img_w,
-                    pb.img_h, pb.tile_size, ntx, nty, proj.absgrad)
+                    pb.img_h, pb.tile_size, ntx, nty, proj.absgrad, cull=pb.cull)
             else:
                 raster_stats = torch.empty((C * N, 8), dtype=torch.float32, device=dev)
-                for c0, c1, ids_b in pb.view_batches:
+                for k, (c0, c1, ids_b) in enumerate(pb.view_batches):
                     W.fused_raster_bwd(pb.splats[c0:c1], pb.tile_offsets[c0:c1], ids_b,
                                        v_image[c0:c1], c1 - c0, N, pb.img_w, pb.img_h,
                                        pb.tile_size, ntx, nty, proj.absgrad,
-                                       out=raster_stats[c0 * N:c1 * N])
+                                       out=raster_stats[c0 * N:c1 * N],
+                                       cull=pb.cull[k] if pb.cull is not None else None)
             v_means2d = torch.empty((C, N, 2), dtype=torch.float32, device=dev)
             v_means2d_abs = (torch.empty((C, N, 2), dtype=torch.float32, device=dev)
                              if proj.absgrad else None)

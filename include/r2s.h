@@ -366,21 +366,27 @@ R2S_API int r2s_bin_prepare(const void* rects, int64_t n_segments, int64_t n_ite
                     int64_t tiles_per_segment, uint32_t tiles_x, int layered,
                     int64_t segment_base, void* workspace, int64_t workspace_bytes,
                     int32_t* tile_offsets, int64_t* n_isects_dev, r2s_stream_t stream);
-/* Rasterize from splat records (float32, any tile size). */
+/* Rasterize from splat records (float32, any tile size).  With 16-pixel
+ * tiles, `cull_ranges` (nullable, [n_isects] uint16) receives each record's
+ * culling ranges inside its tile (first/last column, first/last row, 4 bits
+ * each; this build's culling, the reference has no such table) for the
+ * backward of the same binning to read instead of recomputing them. */
 R2S_API int r2s_raster_splats_fwd_f32(const float* splats, const int32_t* tile_offsets,
                               const int32_t* flatten_ids, int64_t C, int64_t N,
                               int64_t n_isects, uint32_t width, uint32_t height,
                               uint32_t tile_size, uint32_t n_tiles_w, uint32_t n_tiles_h,
-                              float* image, r2s_stream_t stream);
+                              float* image, uint16_t* cull_ranges, r2s_stream_t stream);
 /* Backward sufficient statistics per (view, Gaussian), accumulated over
- * tiles: stats [C*N, 8] = (S0, Sx, Sy, Sxx, Sxy, Syy, Ax, Ay) with
+ * tiles (`cull_ranges`: the table the forward of the same binning wrote, or
+ * NULL): stats [C*N, 8] = (S0, Sx, Sy, Sxx, Sxy, Syy, Ax, Ay) with
  * S* = sum over contributing pixels of v*exp(-sigma) * moments of the pixel
  * offset, A* = sum of |v*exp(-sigma)*(conic . d)|.  Zeroes `stats` first. */
 R2S_API int r2s_raster_splats_bwd_f32(const float* splats, const int32_t* tile_offsets,
                               const int32_t* flatten_ids, const float* v_image, int64_t C,
                               int64_t N, int64_t n_isects, uint32_t width, uint32_t height,
                               uint32_t tile_size, uint32_t n_tiles_w, uint32_t n_tiles_h,
-                              int with_abs, float* stats, r2s_stream_t stream);
+                              int with_abs, const uint16_t* cull_ranges, float* stats,
+                              r2s_stream_t stream);
 
 /* Volume mapping + voxel splat records + brick rectangles
  * (direct.py:289-314: world_to_volume_mapping_fwd and the first pass of
