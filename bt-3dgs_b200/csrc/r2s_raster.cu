@@ -636,7 +636,8 @@ constexpr int kBwd16Batch = 1024;   // records staged and sorted per batch (32 g
 //
 // The tile's upstream gradient sits in shared memory, row-major and
 // column-major.  Staging narrows each record's culling box to the ellipse
-// inside the tile (tile_cull) and picks the shorter axis to walk: a record
+// inside the tile (tile_cull, or the ranges the forward of the same binning
+// wrote to its culling table) and picks the shorter axis to walk: a record
 // with fewer columns than rows is stored transposed (x <-> y, a <-> c, its
 // index flagged in the sign bit) and walks the columns of the column-major
 // copy; its moments are swapped back at the end.  The CTA stages the tile's
