@@ -46,22 +46,43 @@ namespace r2s {
 
 constexpr float kCullLn2 = 0.69314718055994531f;
 
+// Quantities of a 2D splat that both strip passes of tile_cull share.
+struct StripConic {
+    float a, b, c;     // conic
+    float det, Sm;     // a c - b^2, widened level
+    float inv_a, inv_c, inv_det;
+    bool exact;        // false: degenerate or ill-conditioned, keep the box
+};
+
+R2S_HD StripConic strip_conic(float a, float b, float c, float S) {
+    StripConic k;
+    k.a = a;
+    k.b = b;
+    k.c = c;
+    k.det = a * c - b * b;
+    k.exact = a > 0.f && c > 0.f && k.det > 0.f && S >= 0.f && S < 1e30f;
+    k.inv_det = 1.0f / k.det;
+    const float cond = (a * c) * k.inv_det;
+    k.exact = k.exact && cond < 1e6f;
+    k.Sm = S * (1.0f + 2e-4f + 1e-6f * cond) + 2e-4f;
+    k.inv_a = 1.0f / a;
+    k.inv_c = 1.0f / c;
+    return k;
+}
+
 // Narrows the tile-local index range [lo, hi] of the walked axis v.  v0 is
 // the offset v of index 0 (pixel centre minus mean), [uL, uR] the offsets of
-// the first and last pixel centre of the strip on the other axis.  Leaves
-// the range as it is for a degenerate or ill-conditioned conic, a negative
-// or non-finite S, non-finite offsets or an already empty range; empties it
-// (lo > hi) when no pixel of the strip can pass.
-R2S_HD void strip_range(float a, float b, float c, float S, float uL, float uR, float v0, int& lo,
-                        int& hi) {
-    if (lo > hi || !(uL <= uR) || !(fabsf(v0) < 1e30f)) return;
-    const float det = a * c - b * b;
-    if (!(a > 0.f && c > 0.f && det > 0.f && S >= 0.f && S < 1e30f)) return;
-    const float cond = (a * c) / det;
-    if (!(cond < 1e6f)) return;
-    const float Sm = S * (1.0f + 2e-4f + 1e-6f * cond) + 2e-4f;
-    const float V = sqrtf(2.0f * Sm * (a / det));
-    const float ut = -b * V / a;  // u of the top point; the bottom point sits at -ut
+// the first and last pixel centre of the strip on the other axis; (a, c) are
+// the conic's u and v coefficients (k.a / k.c, or swapped with their
+// reciprocals for the column pass).  Leaves the range as it is for a
+// degenerate or ill-conditioned conic, non-finite offsets or an already empty
+// range; empties it (lo > hi) when no pixel of the strip can pass.
+R2S_HD void strip_range(const StripConic& k, float a, float c, float inv_a, float inv_c, float uL,
+                        float uR, float v0, int& lo, int& hi) {
+    if (lo > hi || !k.exact || !(uL <= uR) || !(fabsf(v0) < 1e30f)) return;
+    const float b = k.b, det = k.det, Sm = k.Sm;
+    const float V = sqrtf(2.0f * Sm * (a * k.inv_det));
+    const float ut = -b * V * inv_a;  // u of the top point; the bottom point sits at -ut
     float vhi, vlo, mhi, mlo;
     if (ut >= uL && ut <= uR) {
         vhi = V;
@@ -75,8 +96,8 @@ R2S_HD void strip_range(float a, float b, float c, float S, float uL, float uR, 
             return;
         }
         const float r = sqrtf(disc);
-        vhi = (r - b * u0) / c;
-        mhi = (fabsf(b * u0) + r) / c;
+        vhi = (r - b * u0) * inv_c;
+        mhi = (fabsf(b * u0) + r) * inv_c;
     }
     if (-ut >= uL && -ut <= uR) {
         vlo = -V;
@@ -90,8 +111,8 @@ R2S_HD void strip_range(float a, float b, float c, float S, float uL, float uR, 
             return;
         }
         const float r = sqrtf(disc);
-        vlo = (-r - b * u0) / c;
-        mlo = (fabsf(b * u0) + r) / c;
+        vlo = (-r - b * u0) * inv_c;
+        mlo = (fabsf(b * u0) + r) * inv_c;
     }
     // index i has offset v0 + i: keep i in [vlo - m - v0, vhi + m - v0]; the
     // margin also covers the rounding of offsets the caller shifted
@@ -112,16 +133,16 @@ R2S_HD void strip_range(float a, float b, float c, float S, float uL, float uR, 
 R2S_HD void tile_cull(float mx, float my, float a, float b, float c, float s_thr, float X0,
                       float Y0, int& c_lo, int& c_hi, int& r_lo, int& r_hi) {
     if (c_lo > c_hi || r_lo > r_hi) return;
-    const float S = s_thr * kCullLn2;
-    strip_range(a, b, c, S, (X0 + ((float)c_lo + 0.5f)) - mx, (X0 + ((float)c_hi + 0.5f)) - mx,
-                (Y0 + 0.5f) - my, r_lo, r_hi);
+    const StripConic k = strip_conic(a, b, c, s_thr * kCullLn2);
+    strip_range(k, k.a, k.c, k.inv_a, k.inv_c, (X0 + ((float)c_lo + 0.5f)) - mx,
+                (X0 + ((float)c_hi + 0.5f)) - mx, (Y0 + 0.5f) - my, r_lo, r_hi);
     if (r_lo > r_hi) {
         c_lo = 1;
         c_hi = 0;
         return;
     }
-    strip_range(c, b, a, S, (Y0 + ((float)r_lo + 0.5f)) - my, (Y0 + ((float)r_hi + 0.5f)) - my,
-                (X0 + 0.5f) - mx, c_lo, c_hi);
+    strip_range(k, k.c, k.a, k.inv_c, k.inv_a, (Y0 + ((float)r_lo + 0.5f)) - my,
+                (Y0 + ((float)r_hi + 0.5f)) - my, (X0 + 0.5f) - mx, c_lo, c_hi);
     if (c_lo > c_hi) {
         r_lo = 1;
         r_hi = 0;
