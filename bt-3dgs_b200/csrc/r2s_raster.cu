@@ -484,9 +484,10 @@ constexpr int kFwd16Batch = 256;
 // [g0, g1] of the four 4-row groups (its culling box narrowed to the ellipse,
 // tile_cull); staging (two records per thread, batches of 256) sorts each
 // batch by that range, one of ten patterns, with a deterministic counting
-// sort (ballots, slot order), and the warps
-// take every fourth record of each pattern's run through a loop compiled for
-// that pattern: no per-record group tests, straight-line group bodies.  Each
+// sort (ballots, slot order) and stores each record at its slot, and the
+// warps take every fourth record of each pattern's run through a loop
+// compiled for that pattern: no per-record group tests, straight-line group
+// bodies.  Each
 // group is 2 pixels per lane in packed pairs.  The four warps' partial sums
 // are added in shared memory at the end.  Ten resident CTAs per SM (48
 // registers) measured faster than the 63 registers the compiler picks alone.
@@ -495,12 +496,12 @@ raster_fwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict
                     const int32_t* __restrict__ flatten_ids, int64_t n_keys, int64_t n_isects,
                     uint32_t W, uint32_t H, uint32_t ntx, uint32_t nty, float* __restrict__ image,
                     uint16_t* __restrict__ cull_out) {
+    // staged records in pattern order
     __shared__ float4 s_p[kFwd16Batch];  // mx, my, A = a/2 log2e, B = b log2e
     __shared__ float4 s_q[kFwd16Batch];  // C = c/2 log2e, w*mu, s_thr, 0
     __shared__ float s_acc[kFwd16Threads / 32][256];
     __shared__ int s_wc[2 * kFwd16Threads / 32][11];  // per-(half, warp) pattern counts, then slots
     __shared__ int s_off[12];                     // first slot of each pattern's run
-    __shared__ uint16_t s_perm[kFwd16Batch];      // staged records in pattern order
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int64_t cam = blockIdx.z;
@@ -522,6 +523,8 @@ raster_fwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict
         const int n = min(kFwd16Batch, end - b0);
         __syncthreads();
         int pid[2] = {10, 10};  // row-group pattern of the records; 10: no pixel
+        float4 sp[2], sq[2];
+#pragma unroll
         for (int k = 0; k < 2; ++k) {
             const int ti = k * kFwd16Threads + tid;
             if (ti >= n) continue;
@@ -542,9 +545,9 @@ raster_fwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict
             // negated coefficients: the packed chain yields -s exactly, so ex2
             // takes it as is; the cut-off test compares the bits of -s as
             // signed integers against INT_MIN + bits(s_thr)
-            s_p[ti] = make_float4(p.x, p.y, -0.5f * kLog2e * p.z, -kLog2e * p.w);
-            s_q[ti] = make_float4(-0.5f * kLog2e * q.x, q.y,
-                                   __uint_as_float(__float_as_uint(s_thr) ^ 0x80000000u), 0.f);
+            sp[k] = make_float4(p.x, p.y, -0.5f * kLog2e * p.z, -kLog2e * p.w);
+            sq[k] = make_float4(-0.5f * kLog2e * q.x, q.y,
+                                __uint_as_float(__float_as_uint(s_thr) ^ 0x80000000u), 0.f);
         }
         {  // deterministic counting sort of the batch by pattern (ballots, slot order)
             const unsigned below = (1u << lane) - 1u;
@@ -573,17 +576,18 @@ raster_fwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict
             __syncthreads();
 #pragma unroll
             for (int k = 0; k < 2; ++k)
-                if (pid[k] < 10)
-                    s_perm[s_wc[k * (kFwd16Threads / 32) + warp][pid[k]] + rank[k]] =
-                        (uint16_t)(k * kFwd16Threads + tid);
+                if (pid[k] < 10) {
+                    const int slot = s_wc[k * (kFwd16Threads / 32) + warp][pid[k]] + rank[k];
+                    s_p[slot] = sp[k];
+                    s_q[slot] = sq[k];
+                }
         }
         __syncthreads();
         auto run = [&](auto c0, auto c1, int b, int e) {
             constexpr int G0 = decltype(c0)::value, G1 = decltype(c1)::value;
             for (int i = b + warp; i < e; i += kFwd16Threads / 32) {
-                const int t = s_perm[i];
-                const float4 Q = s_q[t];
-                const float4 P = s_p[t];
+                const float4 Q = s_q[i];
+                const float4 P = s_p[i];
                 const int thr_n = __float_as_int(Q.z);
                 const float dx = px - P.x;
                 const float xx = P.z * dx * dx;
