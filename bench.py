@@ -160,8 +160,9 @@ class OursProjection:
         m, q, s, o = wl.make_gaussians(cfg)
         self.host = [t.pin_memory() for t in (m, q, s, o)]
         self.params = [t.to(dev) for t in (m, q, s, o)]
-        first, count, total = shard.view_shard(cfg.n_views, rank, world)
-        vm, K = wl.make_cameras(count, cfg.detector, first=first, count=count, total=total)
+        first, count, total, stride = shard.view_shard(cfg.n_views, rank, world)
+        vm, K = wl.make_cameras(count, cfg.detector, first=first, count=count, total=total,
+                                stride=stride)
         self.vm, self.K = vm.to(dev), K.to(dev)
         self.host_cams = (vm.pin_memory(), K.pin_memory())
         g = torch.Generator(device=dev).manual_seed(100 + rank)

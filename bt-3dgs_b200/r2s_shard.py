@@ -1,7 +1,10 @@
 """Host-side sharding of the r2splat hot path over one process per GPU.
 
-Projection: every rank renders its own contiguous block of views of a shared
-orbit (weak scaling) and the raw-parameter gradients are summed across ranks;
+Projection: every rank renders its own views of a shared orbit (weak
+scaling), every world-th view starting at its rank, so that each rank's views
+span the whole circle and see the same amount of the scene (contiguous arcs
+differ by several per cent in intersection records); the raw-parameter
+gradients are summed across ranks;
 the gradient is linear in the per-view contributions, so the sum equals the
 single-process gradient over all views.  Voxelization: the brick layers of
 the grid are split into contiguous z-slabs, one per rank; a rank bins only its
@@ -15,11 +18,12 @@ from typing import List, Sequence, Tuple
 import torch
 
 
-def view_shard(views_per_rank: int, rank: int, world: int) -> Tuple[int, int, int]:
-    """(first view, view count, orbit size) of `rank`'s block of views."""
+def view_shard(views_per_rank: int, rank: int, world: int) -> Tuple[int, int, int, int]:
+    """(first view, view count, orbit size, stride) of `rank`'s views: views
+    first, first + stride, ... of the orbit."""
     if not 0 <= rank < world:
         raise ValueError(f"rank {rank} outside world of {world}")
-    return rank * views_per_rank, views_per_rank, views_per_rank * world
+    return rank, views_per_rank, views_per_rank * world, world
 
 
 def layer_range(n_layers: int, rank: int, world: int) -> Tuple[int, int]:

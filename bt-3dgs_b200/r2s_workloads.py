@@ -135,12 +135,13 @@ def invert_rigid(T: torch.Tensor) -> torch.Tensor:
 
 
 def make_cameras(n_views: int, detector: int, first: int = 0, count: Optional[int] = None,
-                 total: Optional[int] = None):
-    """viewmats [C,4,4] and Ks [C,3,3] (float32) for views first..first+count-1
-    of `total` views evenly spaced over 360 degrees."""
+                 total: Optional[int] = None, stride: int = 1):
+    """viewmats [C,4,4] and Ks [C,3,3] (float32) for views first,
+    first + stride, ... (count of them) of `total` views evenly spaced over 360
+    degrees."""
     total = n_views if total is None else total
     count = n_views if count is None else count
-    thetas = [2 * math.pi * (first + k) / total for k in range(count)]
+    thetas = [2 * math.pi * (first + k * stride) / total for k in range(count)]
     c2w = torch.stack([camtoworld(t) for t in thetas]) if thetas else torch.zeros(0, 4, 4, dtype=torch.float64)
     viewmats = invert_rigid(c2w).float().contiguous()
     f = DSD * detector / DETECTOR_SPAN

@@ -39,16 +39,16 @@ def _params():
     return [t.double().requires_grad_(True) for t in (m, q, s, o)]
 
 
-def _projection_grads(params, first, count, total):
+def _projection_grads(params, first, count, total, stride=1):
     import r2s_workloads as wl
     from oracle import r2s_oracle as O
 
-    vm, K = wl.make_cameras(count, DET, first=first, count=count, total=total)
+    vm, K = wl.make_cameras(count, DET, first=first, count=count, total=total, stride=stride)
     img, *_ = O.projection_forward(*params, vm.double(), K.double(), width=DET, height=DET,
                                    tile=wl.IMG_TILE, eps2d=wl.EPS2D, clip=wl.RADIUS_CLIP,
                                    smin=wl.SCALE_MIN, smax=wl.SCALE_MAX)
     g = torch.Generator().manual_seed(5)
-    v = torch.randn((total, DET, DET), generator=g, dtype=torch.float64)[first:first + count]
+    v = torch.randn((total, DET, DET), generator=g, dtype=torch.float64)[first::stride][:count]
     return torch.autograd.grad((img * v).sum(), params)
 
 
@@ -78,8 +78,8 @@ def _worker(rank, port, out_path):
     dist.init_process_group("gloo", rank=rank, world_size=WORLD)
     try:
         params = _params()
-        first, count, total = shard.view_shard(VIEWS_PER_RANK, rank, WORLD)
-        grads = [g.clone() for g in _projection_grads(params, first, count, total)]
+        first, count, total, stride = shard.view_shard(VIEWS_PER_RANK, rank, WORLD)
+        grads = [g.clone() for g in _projection_grads(params, first, count, total, stride)]
         shard.GradientAllReduce()(grads)
 
         l0, l1 = shard.layer_range(GRID // TILE3, rank, WORLD)
@@ -148,10 +148,10 @@ def test_view_shards_cover_the_orbit():
 
     seen = []
     for r in range(4):
-        first, count, total = shard.view_shard(75, r, 4)
-        assert total == 300 and count == 75
-        seen.extend(range(first, first + count))
-    assert seen == list(range(300))
+        first, count, total, stride = shard.view_shard(75, r, 4)
+        assert total == 300 and count == 75 and stride == 4
+        seen.extend(range(first, first + stride * count, stride))
+    assert sorted(seen) == list(range(300))
 
 
 def test_projection_gradient_allreduce_equals_single_process(sharded):
