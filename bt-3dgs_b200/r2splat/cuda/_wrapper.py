@@ -13,6 +13,7 @@ Besides the 18 operators this module holds the fused float32 helpers used by
 from __future__ import annotations
 
 import ctypes
+import os
 from typing import Optional, Tuple
 
 import torch
@@ -70,8 +71,21 @@ def _last_error() -> str:
     return buf.value.decode(errors="replace")
 
 
+# One NVTX range per library call, named after the C entry point, when the
+# environment sets R2S_NVTX to anything but "0" (read once, at import): every
+# stage of the path then shows up on profiler timelines.  Off by default.
+_NVTX = os.environ.get("R2S_NVTX", "0") not in ("", "0")
+
+
 def _call(fn_name: str, *args) -> None:
-    rc = getattr(_C, fn_name)(*args)
+    if _NVTX:
+        torch.cuda.nvtx.range_push(fn_name)
+        try:
+            rc = getattr(_C, fn_name)(*args)
+        finally:
+            torch.cuda.nvtx.range_pop()
+    else:
+        rc = getattr(_C, fn_name)(*args)
     if rc != 0:
         raise RuntimeError(_last_error() or f"{fn_name} failed with status {rc}")
 
