@@ -22,7 +22,9 @@
 // Gaussians and walks only the pixel rectangle that can contribute; the
 // float32 16x16 kernel gives each thread one Gaussian record and walks the
 // rows, or the columns when they are fewer, of its culling box narrowed to
-// the ellipse inside the tile.  Per (Gaussian, tile) both reduce
+// the ellipse inside the tile (the ranges that the forward of the same
+// binning wrote to its culling table, 2 bytes per record, or its own
+// tile_cull without one).  Per (Gaussian, tile) both reduce
 // six moments of the contributing pixels,
 //   S0 = sum v e,  Sx = sum v e dx,  Sy = sum v e dy,
 //   Sxx = sum v e dx^2,  Sxy = sum v e dx dy,  Syy = sum v e dy^2
