@@ -1103,6 +1103,7 @@ extern "C" int r2s_raster_splats_bwd_f32(const float* splats, const int32_t* off
 // pair -- in one static device array of the library, so the call allocates
 // nothing.  The array is part of the library's device image: every GPU that
 // loads the library holds its 8 MiB until the process exits.
+#include <cuda.h>
 #include <mutex>
 
 namespace r2s {
@@ -1114,13 +1115,52 @@ constexpr int kNoAllocMaxDevices = 64;
 
 static __device__ __align__(256) float g_noalloc_scratch[kNoAllocFloats];
 
+// Driver entry points (taken through the runtime, so the library does not
+// link libcuda): the current context and its process-unique id.
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long*);
+
+struct NoAllocSlot {
+    unsigned long long ctx_id;  // context the address belongs to (0: none yet)
+    float* ptr;
+};
+
 std::mutex g_noalloc_mutex;
-float* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+NoAllocSlot g_noalloc_slot[kNoAllocMaxDevices] = {};
+CtxGetCurrentFn g_ctx_get_current = nullptr;
+CtxGetIdFn g_ctx_get_id = nullptr;
+bool g_ctx_fns_loaded = false;
+
+int current_context_id(int dev, unsigned long long* id) {
+    if (!g_ctx_fns_loaded) {
+        g_ctx_fns_loaded = true;
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_ctx_get_current = reinterpret_cast<CtxGetCurrentFn>(f);
+        f = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_ctx_get_id = reinterpret_cast<CtxGetIdFn>(f);
+    }
+    if (g_ctx_get_current == nullptr || g_ctx_get_id == nullptr)
+        return fail(R2S_ERR_CUDA, "noalloc: driver entry points cuCtxGetCurrent/cuCtxGetId missing");
+    CUcontext ctx = nullptr;
+    if (g_ctx_get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr)
+        return fail(R2S_ERR_CUDA, "noalloc: no current CUDA context on device %d", dev);
+    if (g_ctx_get_id(ctx, id) != CUDA_SUCCESS)
+        return fail(R2S_ERR_CUDA, "noalloc: cuCtxGetId failed on device %d", dev);
+    return R2S_OK;
+}
 
 // Device address of the static scratch on the current device.  The host-side
 // name g_noalloc_scratch is only a stand-in for the symbol, so the address is
-// looked up once per device with cudaGetSymbolAddress while that device is
-// current (the first call on each device does this) and cached.
+// looked up with cudaGetSymbolAddress while that device is current -- by the
+// first call on each device -- and cached together with the id of the
+// device's context.  A call from another context of the same ordinal (after
+// cudaDeviceReset, or a context the caller made current) looks it up again,
+// so a stale address is never used.
 int noalloc_scratch(float** out) {
     int dev = -1;
     cudaError_t err = cudaGetDevice(&dev);
@@ -1128,16 +1168,25 @@ int noalloc_scratch(float** out) {
         return fail(R2S_ERR_CUDA, "noalloc: cudaGetDevice failed (%s)", cudaGetErrorString(err));
     if (dev < 0 || dev >= kNoAllocMaxDevices)
         return fail(R2S_ERR_UNSUPPORTED, "noalloc: device ordinal %d out of range", dev);
+    // makes the device's primary context current if no context is (CUDA 12)
+    err = cudaSetDevice(dev);
+    if (err != cudaSuccess)
+        return fail(R2S_ERR_CUDA, "noalloc: cudaSetDevice(%d) failed (%s)", dev,
+                    cudaGetErrorString(err));
     std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-    if (g_noalloc_ptr[dev] == nullptr) {
+    unsigned long long ctx_id = 0;
+    if (int rc = current_context_id(dev, &ctx_id)) return rc;
+    NoAllocSlot& slot = g_noalloc_slot[dev];
+    if (slot.ptr == nullptr || slot.ctx_id != ctx_id) {
         void* p = nullptr;
         err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
         if (err != cudaSuccess || p == nullptr)
             return fail(R2S_ERR_CUDA, "noalloc: cudaGetSymbolAddress failed on device %d (%s)", dev,
                         cudaGetErrorString(err));
-        g_noalloc_ptr[dev] = static_cast<float*>(p);
+        slot.ptr = static_cast<float*>(p);
+        slot.ctx_id = ctx_id;
     }
-    *out = g_noalloc_ptr[dev];
+    *out = slot.ptr;
     return R2S_OK;
 }
 
@@ -1151,12 +1200,14 @@ extern "C" int r2s_rasterize_to_pixels_bwd_noalloc_f32(
     float* v_means2d_abs, float* v_means2d, float* v_conics, float* v_opacities, float* v_mus,
     r2s_stream_t stream) {
     R2S_REQUIRE(C >= 0 && N >= 0, "rasterize_to_pixels_bwd_noalloc: negative size");
-    if (C * N > r2s::kNoAllocMaxPairs)
+    // C * N is compared by division: the product of two large sizes could
+    // overflow int64 and wrap to a small value
+    if (N > 0 && C > r2s::kNoAllocMaxPairs / N)
         return r2s::fail(R2S_ERR_UNSUPPORTED,
-                         "rasterize_to_pixels_bwd_noalloc: %lld (view, Gaussian) pairs exceed the "
-                         "static scratch of %lld pairs; use r2s_rasterize_to_pixels_bwd with "
-                         "caller scratch",
-                         (long long)(C * N), (long long)r2s::kNoAllocMaxPairs);
+                         "rasterize_to_pixels_bwd_noalloc: %lld views x %lld Gaussians exceed the "
+                         "static scratch of %lld (view, Gaussian) pairs; use "
+                         "r2s_rasterize_to_pixels_bwd with caller scratch",
+                         (long long)C, (long long)N, (long long)r2s::kNoAllocMaxPairs);
     float* scratch = nullptr;
     if (int rc = r2s::noalloc_scratch(&scratch)) return rc;
     float* stats = scratch;

@@ -122,16 +122,23 @@ class GradientAllReduce:
 
 
 def data_parallel_objective(out: dict, w_l1: float, w_ssim: float, w_tv: float,
-                            n_local_views: int, n_total_views: int, world: int) -> torch.Tensor:
+                            n_local_views: int, n_total_views: int, world: int,
+                            w_hierarchy: float = 0.0) -> torch.Tensor:
     """The scalar a rank backpropagates so that the sum of the ranks'
     gradients equals the one-process gradient of the training loss
-    (BinaryTreeLossComputer, src/utils/loss.py:125-172) over all the step's
-    views.  ``out`` is the loss computer's dict for this rank's views.
+    (BinaryTreeLossComputer, src/utils/loss.py:125-172, including its
+    ``w_hierarchy * hierarchy`` term) over all the step's views.  ``out`` is
+    the loss computer's dict for this rank's views.
 
     L1, SSIM and the edge term are means over (view, pixel) with per-view
     SSIM windows, so a rank's mean over its own views weighted by
     n_local / n_total sums to the mean over all views.  Every rank evaluates
-    the same TV sub-volume, so TV is weighted 1 / world."""
+    the same TV sub-volume, so TV is weighted 1 / world; the hierarchy loss
+    (src/utils/loss.py:27-60) depends only on the replicated parameters and
+    the archived parents, so it is weighted 1 / world as well."""
     frac = float(n_local_views) / float(n_total_views)
     proj = w_l1 * out["proj_l1"] + w_ssim * out["proj_ssim"] + out["edge_weight"] * out["edge"]
-    return frac * proj + (w_tv / float(world)) * out["vol_tv"]
+    total = frac * proj + (w_tv / float(world)) * out["vol_tv"]
+    if w_hierarchy and "hierarchy" in out:
+        total = total + (float(w_hierarchy) / float(world)) * out["hierarchy"]
+    return total

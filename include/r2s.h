@@ -298,7 +298,9 @@ R2S_API int r2s_rasterize_to_pixels_bwd(int dtype, int mode, const void* means2d
  * library, so C*N is limited to 131072 (view, Gaussian) pairs (larger calls
  * return R2S_ERR_UNSUPPORTED).  Works on the current device; its first call
  * on each device looks the array up with cudaGetSymbolAddress and should come
- * before any stream capture.  Every call reuses the same array: calls that
+ * before any stream capture (the address is cached per device together with
+ * the id of the device's context, so after cudaDeviceReset the next call
+ * looks it up again).  Every call reuses the same array: calls that
  * overlap on the GPU (other streams, other threads) race and must be
  * serialized by the caller. */
 R2S_API int r2s_rasterize_to_pixels_bwd_noalloc_f32(

@@ -215,34 +215,50 @@ def test_layer_weights_from_packed_rects():
 def test_data_parallel_objective_sums_to_the_single_process_gradient(split):
     """Ranks holding view blocks of one training step backpropagate
     data_parallel_objective; the summed gradients equal the gradients of the
-    full loss (BinaryTreeLossComputer over all views, TV once)."""
+    full loss (BinaryTreeLossComputer over all views, TV once, and the
+    hierarchy term of the replicated parameters with the reference trainer's
+    default weight 0.05, configs/trainer/binary_tree.yaml:25)."""
     import r2s_shard as shard
     from oracle import r2s_oracle as O
 
     w = dict(w_l1=0.8, w_ssim=0.2, w_tv=0.05, w_edge=0.1)
+    w_h = 0.05
     g = torch.Generator().manual_seed(4)
     C, H = sum(split), 24
     renders = torch.rand(C, H, H, 1, generator=g, dtype=torch.float64)
     targets = torch.rand(C, H, H, 1, generator=g, dtype=torch.float64)
     edge = (torch.rand(C, H, H, 1, generator=g) < 0.3).double()
     vol = torch.rand(10, 10, 10, generator=g, dtype=torch.float64)
+    means = torch.rand(50, 3, generator=g, dtype=torch.float64)
+    parents = torch.rand(50, 3, generator=g, dtype=torch.float64)
+
+    def hierarchy(m):  # a nonzero penalty of the replicated parameters
+        return torch.relu((m - parents).norm(dim=-1) - 0.3).square().mean()
 
     r_full = renders.clone().requires_grad_(True)
     v_full = vol.clone().requires_grad_(True)
-    O.binary_tree_losses(r_full, targets, edge, v_full, **w)["total"].backward()
+    m_full = means.clone().requires_grad_(True)
+    assert hierarchy(means) > 0
+    (O.binary_tree_losses(r_full, targets, edge, v_full, **w)["total"]
+     + w_h * hierarchy(m_full)).backward()
 
     grad_r = torch.zeros_like(renders)
     grad_v = torch.zeros_like(vol)
+    grad_m = torch.zeros_like(means)
     v0 = 0
     for n in split:
         r = renders[v0:v0 + n].clone().requires_grad_(True)
         v = vol.clone().requires_grad_(True)
+        m = means.clone().requires_grad_(True)
         out = O.binary_tree_losses(r, targets[v0:v0 + n], edge[v0:v0 + n], v, **w)
         out["edge_weight"] = torch.tensor(w["w_edge"], dtype=torch.float64)
+        out["hierarchy"] = hierarchy(m)
         shard.data_parallel_objective(out, w["w_l1"], w["w_ssim"], w["w_tv"], n, C,
-                                      len(split)).backward()
+                                      len(split), w_hierarchy=w_h).backward()
         grad_r[v0:v0 + n] = r.grad
         grad_v += v.grad
+        grad_m += m.grad
         v0 += n
     torch.testing.assert_close(grad_r, r_full.grad, rtol=1e-12, atol=1e-15)
     torch.testing.assert_close(grad_v, v_full.grad, rtol=1e-12, atol=1e-15)
+    torch.testing.assert_close(grad_m, m_full.grad, rtol=1e-12, atol=1e-15)

@@ -95,3 +95,9 @@ def test_noalloc_backward_rejects_sizes_beyond_its_scratch():
                                                     None, None, None, stream)
     assert rc == 4  # R2S_ERR_UNSUPPORTED
     assert "static scratch" in W._last_error()
+    # sizes whose product overflows int64 are rejected too, not wrapped
+    rc = _C.r2s_rasterize_to_pixels_bwd_noalloc_f32(1, None, None, None, None, None, None, None,
+                                                    2 ** 40, 2 ** 40, 1, 64, 64, 16, 4, 4, None,
+                                                    None, None, None, None, stream)
+    assert rc == 4
+    assert "static scratch" in W._last_error()
