@@ -7,7 +7,14 @@ The reference keeps its parameters as four raw (pre-activation) tensors of
 * **checkpoint** (``save_ckpt`` / ``load_ckpt``, :556-581): ``torch.save`` of
   ``{"step": int, "model": state_dict, **extra}`` where the state dict holds
   ``means`` [N,3], ``scales`` [N,3] (raw), ``quats`` [N,4] and ``opacities``
-  [N] (raw), float32, in that registration order (:182-185);
+  [N] (raw), float32, in that registration order (:182-185).  The
+  binary-tree model (src/models/binary_tree_gaussian_model.py:37-44,
+  207-259) adds eight buffers after the parameters in its state dict --
+  ``parent`` and ``level`` [N] int32, ``history_means`` [H,3],
+  ``history_scales`` [H,3], ``history_quats`` [H,4], ``history_opacities``
+  [H], ``history_parent`` and ``history_level`` [H] int32 -- and the same
+  tensors again under a top-level ``"history"`` key (``save_ckpt(...,
+  tree=...)``, ``load_tree_ckpt``);
 * **pickle ``.ply``** (``save_ply`` / ``load_ply``, :583-641): a pickled dict
   of numpy arrays ``xyz``, ``density`` [N,1], ``scale``, ``rotation``, plus
   ``scale_bound`` (``[min, max]`` or a [2,3] array, ``None`` for exp scales)
@@ -37,6 +44,10 @@ import numpy as np
 import torch
 
 PARAM_NAMES = ("means", "scales", "quats", "opacities")
+# binary-tree buffers in registration order (binary_tree_gaussian_model.py:37-44)
+TREE_NAMES = ("parent", "level", "history_means", "history_scales", "history_quats",
+              "history_opacities", "history_parent", "history_level")
+_TREE_INT32 = ("parent", "level", "history_parent", "history_level")
 _PLY_KEYS = {"means": ("xyz", "means"), "scales": ("scale", "scales"),
              "quats": ("rotation", "quats"), "opacities": ("density", "opacities")}
 
@@ -64,13 +75,31 @@ def _check_params(params: Mapping[str, torch.Tensor]) -> None:
         raise ValueError(f"missing Gaussian parameters: {missing}")
 
 
+def _check_tree(tree: Mapping[str, torch.Tensor]) -> None:
+    missing = [k for k in TREE_NAMES if k not in tree]
+    if missing:
+        raise ValueError(f"missing binary-tree buffers: {missing}")
+
+
 def save_ckpt(path: str, step: int, params: Mapping[str, torch.Tensor],
-              extra: Optional[Dict[str, Any]] = None) -> None:
+              extra: Optional[Dict[str, Any]] = None,
+              tree: Optional[Mapping[str, torch.Tensor]] = None) -> None:
     """``torch.save({"step", "model": state_dict, **extra})`` with the
-    reference's state-dict keys and order (gaussian_model.py:556-567)."""
+    reference's state-dict keys and order (gaussian_model.py:556-567).
+
+    With ``tree`` (the eight binary-tree buffers of TREE_NAMES), the layout
+    of ``BinaryTreeGaussianModel.save_ckpt``
+    (binary_tree_gaussian_model.py:207-229): the buffers follow the
+    parameters in the state dict and are stored again under ``"history"``,
+    before the extra entries."""
     _check_params(params)
     model = OrderedDict((k, params[k].detach()) for k in PARAM_NAMES)
     payload: Dict[str, Any] = {"step": step, "model": model}
+    if tree is not None:
+        _check_tree(tree)
+        for k in TREE_NAMES:
+            model[k] = tree[k].detach()
+        payload["history"] = {k: tree[k] for k in TREE_NAMES}
     if extra:
         payload.update(extra)
     torch.save(payload, path)
@@ -80,20 +109,40 @@ def load_ckpt(path: str, device: Union[str, torch.device] = "cpu",
               strict: bool = True) -> Tuple[Dict[str, torch.Tensor], int]:
     """Parameters and step of a checkpoint (gaussian_model.py:569-581).
 
-    ``strict`` requires exactly the four parameter keys, as
-    ``load_state_dict(strict=True)`` does (``RuntimeError`` otherwise); the
-    step is -1 when absent."""
+    ``strict`` requires exactly the keys of the model that wrote it, as
+    ``load_state_dict(strict=True)`` does (``RuntimeError`` otherwise): the
+    four parameters, plus the eight binary-tree buffers when the checkpoint
+    has the binary-tree layout (a ``"history"`` entry).  The buffers
+    themselves are returned by ``load_tree_ckpt``.  The step is -1 when
+    absent."""
     ckpt = torch.load(path, map_location=device, weights_only=True)
     model = ckpt["model"]
     if strict:
+        expected = set(PARAM_NAMES) | (set(TREE_NAMES) if "history" in ckpt else set())
         keys = set(model.keys())
-        if keys != set(PARAM_NAMES):
-            missing = sorted(set(PARAM_NAMES) - keys)
-            unexpected = sorted(keys - set(PARAM_NAMES))
+        if keys != expected:
+            missing = sorted(expected - keys)
+            unexpected = sorted(keys - expected)
             raise RuntimeError(f"Error(s) in loading state_dict: missing keys {missing}, "
                                f"unexpected keys {unexpected}")
     params = {k: model[k] for k in PARAM_NAMES if k in model}
     return params, int(ckpt.get("step", -1))
+
+
+def load_tree_ckpt(path: str, device: Union[str, torch.device] = "cpu"
+                   ) -> Tuple[Dict[str, torch.Tensor], Dict[str, torch.Tensor], int]:
+    """Parameters, binary-tree buffers and step of a binary-tree checkpoint,
+    as ``BinaryTreeGaussianModel.load_ckpt`` restores them
+    (binary_tree_gaussian_model.py:231-259): parameters from the state dict,
+    buffers from ``"history"`` (``KeyError`` when the checkpoint has none)
+    with parent/level ids cast to int32."""
+    ckpt = torch.load(path, map_location=device, weights_only=True)
+    state = ckpt["model"]
+    params = {k: state[k].to(device) for k in PARAM_NAMES}
+    h = ckpt["history"]
+    tree = {k: (h[k].to(device, dtype=torch.int32) if k in _TREE_INT32 else h[k].to(device))
+            for k in TREE_NAMES}
+    return params, tree, int(ckpt.get("step", -1))
 
 
 def save_ply(path: str, params: Mapping[str, torch.Tensor],

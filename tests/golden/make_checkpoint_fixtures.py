@@ -11,6 +11,12 @@ parameters and the scale-bound attributes, and writes what they produce for
 three seeded models: scalar sigmoid bounds, per-axis bounds, and exp scales
 (no bounds).
 
+The binary-tree checkpoint fixture (``tree.ckpt``, tensors in ``tree.pt``) is
+written by the reference's ``BinaryTreeGaussianModel.save_ckpt`` itself
+(src/models/binary_tree_gaussian_model.py:207-229): the class is executed
+unchanged from the reference install in ``baseline/_ref`` by
+``oracle/ref_stock.py`` (no GPU needed to save).
+
 Usage: ``python tests/golden/make_checkpoint_fixtures.py [reference_root]``
 """
 from __future__ import annotations
@@ -86,7 +92,34 @@ def main(root: str) -> None:
         m.export_ply(os.path.join(HERE, f"{name}_export.ply"))
         params[name] = {k: getattr(m, k).detach().clone() for k in ("means", "scales", "quats", "opacities")}
     torch.save(params, os.path.join(HERE, "params.pt"))
+    write_tree_fixture()
     print("wrote", sorted(os.listdir(HERE)))
+
+
+def write_tree_fixture() -> None:
+    from oracle import ref_stock
+
+    mod = ref_stock.load_binary_tree_model("stock")
+    m = mod.BinaryTreeGaussianModel(device="cpu", min_scale=5e-4, max_scale=1.0, scale_eps=1e-5)
+    g = torch.Generator().manual_seed(14)
+    n, h = 6, 3
+    m.means = torch.nn.Parameter(torch.rand(n, 3, generator=g) - 0.5)
+    m.scales = torch.nn.Parameter(torch.randn(n, 3, generator=g))
+    m.quats = torch.nn.Parameter(torch.randn(n, 4, generator=g))
+    m.opacities = torch.nn.Parameter(torch.randn(n, generator=g))
+    m.parent = torch.tensor([-1, -1, 0, 0, 1, 1], dtype=torch.int32)
+    m.level = torch.tensor([0, 0, 1, 1, 1, 1], dtype=torch.int32)
+    m.history_means = torch.rand(h, 3, generator=g) - 0.5
+    m.history_scales = torch.randn(h, 3, generator=g)
+    m.history_quats = torch.randn(h, 4, generator=g)
+    m.history_opacities = torch.randn(h, generator=g)
+    m.history_parent = torch.tensor([-1, 0, 0], dtype=torch.int32)
+    m.history_level = torch.tensor([0, 1, 1], dtype=torch.int32)
+    m.save_ckpt(os.path.join(HERE, "tree.ckpt"), step=321, extra={"note": "tree"})
+    names = ("means", "scales", "quats", "opacities", "parent", "level", "history_means",
+             "history_scales", "history_quats", "history_opacities", "history_parent",
+             "history_level")
+    torch.save({k: getattr(m, k).detach().clone() for k in names}, os.path.join(HERE, "tree.pt"))
 
 
 if __name__ == "__main__":

@@ -113,3 +113,59 @@ def test_ascii_export_is_byte_identical(tmp_path, params, name):
         assert f.read() == g.read()
     with pytest.raises(ValueError, match="Unsupported color_mode"):
         ck.export_ply(path, params[name]["means"], params[name]["opacities"], color_mode="rgb")
+
+
+@pytest.fixture(scope="module")
+def tree():
+    return torch.load(os.path.join(GOLD, "tree.pt"), weights_only=True)
+
+
+def test_load_reference_binary_tree_checkpoint(tree):
+    """tree.ckpt was written by BinaryTreeGaussianModel.save_ckpt: a strict
+    load accepts its buffers, load_tree_ckpt returns them as the reference's
+    load_ckpt restores them (binary_tree_gaussian_model.py:231-259)."""
+    path = os.path.join(GOLD, "tree.ckpt")
+    params, step = ck.load_ckpt(path, strict=True)
+    assert step == 321 and list(params) == list(ck.PARAM_NAMES)
+    p2, buffers, step2 = ck.load_tree_ckpt(path)
+    assert step2 == 321
+    for k in ck.PARAM_NAMES:
+        assert torch.equal(params[k], tree[k]) and torch.equal(p2[k], tree[k])
+    for k in ck.TREE_NAMES:
+        assert torch.equal(buffers[k], tree[k]), k
+        if k in ("parent", "level", "history_parent", "history_level"):
+            assert buffers[k].dtype == torch.int32
+
+
+def test_saved_binary_tree_checkpoint_matches_the_reference_layout(tmp_path, tree):
+    path = str(tmp_path / "t.ckpt")
+    ck.save_ckpt(path, 321, {k: tree[k] for k in ck.PARAM_NAMES},
+                 extra={"note": "tree"}, tree={k: tree[k] for k in ck.TREE_NAMES})
+    payload = torch.load(path, weights_only=True)
+    ref = torch.load(os.path.join(GOLD, "tree.ckpt"), weights_only=True)
+    assert list(payload) == list(ref)  # step, model, history, extra
+    assert list(payload["model"]) == list(ref["model"])
+    assert list(payload["history"]) == list(ref["history"])
+    for k in ref["model"]:
+        assert torch.equal(payload["model"][k], ref["model"][k])
+        assert payload["model"][k].dtype == ref["model"][k].dtype
+    for k in ref["history"]:
+        assert torch.equal(payload["history"][k], ref["history"][k])
+    assert payload["note"] == "tree"
+    _, buffers, _ = ck.load_tree_ckpt(path)
+    assert all(torch.equal(buffers[k], tree[k]) for k in ck.TREE_NAMES)
+
+
+def test_binary_tree_checkpoint_errors(tmp_path, tree):
+    with pytest.raises(ValueError, match="missing binary-tree buffers"):
+        ck.save_ckpt(str(tmp_path / "x.ckpt"), 1, {k: tree[k] for k in ck.PARAM_NAMES},
+                     tree={"parent": tree["parent"]})
+    # a base-model checkpoint has no history: the tree loader fails like the reference's
+    with pytest.raises(KeyError):
+        ck.load_tree_ckpt(os.path.join(GOLD, "scalar.ckpt"))
+    # tree buffers without the history entry are unexpected keys for a strict load
+    path = str(tmp_path / "y.ckpt")
+    model = {k: tree[k] for k in ck.PARAM_NAMES + ck.TREE_NAMES}
+    torch.save({"step": 1, "model": model}, path)
+    with pytest.raises(RuntimeError, match="unexpected keys"):
+        ck.load_ckpt(path, strict=True)
