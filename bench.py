@@ -5,23 +5,31 @@ Metric: Gaussian*views/s of projection forward+backward
 benchmark config 2 by default: 500,000 Gaussians, 75 views over 360 degrees,
 512x512 detector, 256^3 grid (seeded synthetic inputs, r2s_workloads.py).
 
-One step of the projection path is the reference's explicit training step
-without the loss: prepare (parameter transform + softplus), explicit
-rasterize (projection, binning, rasterizer), then explicit backward with a
-seeded N(0,1) upstream image gradient, all through ``r2splat.ops``.  One
-voxel step is prepare, voxelize of the grid and the voxel VJP chain down to
-the raw parameters.
+One projection step is the reference's explicit training step without the
+loss, through the public op API ``r2splat.ops.explicit`` as callers use it:
+prepare (parameter transform + softplus), explicit rasterize (projection,
+binning, rasterizer), then explicit backward with a seeded N(0,1) upstream
+image gradient.  One voxel step is prepare, explicit rasterize of no view
+(the op layer requires a projection pass before its backward,
+r2splat/ops/explicit.py:255-256 of the reference), explicit voxelize of the
+grid and explicit backward with a seeded N(0,1) upstream volume gradient.
+The projection pass renders zero views: both op layers return empty buffers
+for it without a launch, so the voxel step times voxelization alone.
 
-Multi-GPU (torchrun, one process per GPU): every rank renders its own 75
-views of a 75*N-view orbit of the same Gaussians (weak scaling) and the
-per-Gaussian gradients are summed with one NCCL all-reduce per step; the
-voxel grid is split into N z-slabs (strong scaling of that secondary
-metric).  ``value`` is the whole job: N*75*500k Gaussian*views / max-over-
-ranks step time.
+Multi-GPU (torchrun, one process per GPU, NCCL): by default the job's 75
+views are dealt to the ranks, every N-th view starting at the rank
+(``--scaling strong``: the same job split over the GPUs), and the
+per-Gaussian gradients are summed with one NCCL all-reduce per step;
+``--scaling weak`` gives every rank 75 views of a 75*N-view orbit instead.
+The voxel grid is split into N z-slabs of whole brick layers, balanced by
+records per layer (strong scaling).  ``value`` is the whole job's
+Gaussian*views over the max-over-ranks step time.
 
-``--impl reference`` times the reference implementation of the path -- the
-reference's own CUDA sources built for sm_100a (``oracle/_ref``) driven in
-the reference op layer's call order -- on rank 0 with the same workload.
+``--impl reference`` runs the reference implementation of the path on rank 0:
+its own Python op layer, unchanged (``baseline/_ref``), over its own CUDA
+sources built for sm_100a (``oracle/_ref``), through the same public calls
+and on the same workload (config 3 in batches of 20 views, past its int32
+record limit, as its callers must).
 """
 from __future__ import annotations
 
@@ -45,6 +53,10 @@ import r2s_shard as shard  # noqa: E402
 import r2s_workloads as wl  # noqa: E402
 
 L2_FLUSH_BYTES = 256 << 20
+# the projection pass of the voxel step: zero views (the op layer requires a
+# projection pass before its backward; with no view it is empty)
+VOXEL_STEP_VIEWS = 0
+VOXEL_STEP_DETECTOR = 16
 
 
 def _peaks():
@@ -146,73 +158,35 @@ def max_over_ranks(world, value: float) -> float:
     return float(t.item())
 
 
-# ---------------------------------------------------------------------------
-# our implementation
-# ---------------------------------------------------------------------------
-class OursProjection:
-    def __init__(self, cfg, world, rank, dev):
-        from r2splat.ops import explicit as E
+def job_config(cfg, views: int) -> dict:
+    """The workload keys both arms print (same dict for the same job)."""
+    return {"workload": cfg.name, "n_gaussians": cfg.n_gaussians, "views": views,
+            "detector": cfg.detector, "grid": cfg.grid, "l2": "256MiB flush between steps"}
 
-        self.E = E
-        self.world = world
-        self.cfg = cfg
-        self.det = cfg.detector
-        m, q, s, o = wl.make_gaussians(cfg)
-        self.host = [t.pin_memory() for t in (m, q, s, o)]
-        self.params = [t.to(dev) for t in (m, q, s, o)]
-        first, count, total, stride = shard.view_shard(cfg.n_views, rank, world)
-        vm, K = wl.make_cameras(count, cfg.detector, first=first, count=count, total=total,
-                                stride=stride)
-        self.vm, self.K = vm.to(dev), K.to(dev)
-        self.host_cams = (vm.pin_memory(), K.pin_memory())
-        g = torch.Generator(device=dev).manual_seed(100 + rank)
-        self.v_img = torch.randn((cfg.n_views, self.det, self.det), generator=g, device=dev)
-        self.host_vimg = self.v_img.cpu().pin_memory()
-        self.allreduce = shard.GradientAllReduce()
 
-    def step(self, params=None, vm=None, K=None, v_img=None):
-        E = self.E
-        params = self.params if params is None else params
-        vm = self.vm if vm is None else vm
-        K = self.K if K is None else K
-        v_img = self.v_img if v_img is None else v_img
-        for p in params:
-            p.grad = None
-            p.requires_grad_(True)
-        st = E.prepare_explicit_gaussians(params[1], params[2], params[3],
-                                          scale_min=wl.SCALE_MIN, scale_max=wl.SCALE_MAX)
-        res = E.explicit_rasterize(st, params[0], vm, K, img_w=self.det, img_h=self.det,
-                                   tile_size=wl.IMG_TILE, eps2d=wl.EPS2D,
-                                   radius_clip=wl.RADIUS_CLIP, absgrad=True)
-        res.image.grad = v_img
-        E.explicit_backward(st, *params)
-        if self.world > 1:
-            self.allreduce([p.grad for p in params])
-        return res
+# ---------------------------------------------------------------------------
+# end-to-end pipeline: host inputs -> device step -> host outputs
+# ---------------------------------------------------------------------------
+class HostPipeline:
+    """Runs a step on inputs copied from pinned host memory and copies its
+    result back, every step inside the timed region.  The copies run on a copy
+    stream: the next step's inputs upload while this step computes (a
+    double-buffered input pipeline) and the outputs download behind the next
+    step.  Subclasses set ``self.host`` (pinned host inputs) and implement
+    ``step(*device_inputs)`` returning the device tensors to download."""
 
     def _upload(self):
-        """H2D of one step's inputs (raw parameters, cameras, upstream image
-        gradient) on the copy stream; returns the device tensors and an event."""
-        dev = self.params[0].device
         with torch.cuda.stream(self.copy_stream):
-            ins = [h.to(dev, non_blocking=True) for h in self.host]
-            ins += [c.to(dev, non_blocking=True) for c in self.host_cams]
-            ins.append(self.host_vimg.to(dev, non_blocking=True))
+            ins = [h.to(self.dev, non_blocking=True) for h in self.host]
             ev = torch.cuda.Event()
             ev.record(self.copy_stream)
         return ins, ev
 
     def reset_pipeline(self):
-        self.copy_stream = torch.cuda.Stream(device=self.params[0].device)
+        self.copy_stream = torch.cuda.Stream(device=self.dev)
         self.prefetched = None
 
     def step_e2e(self, prefetch_next=True):
-        """Same step with host-resident inputs and outputs: H2D of the raw
-        parameters, cameras and upstream image gradient, D2H of the four
-        parameter gradients.  The copies run on a copy stream: the next step's
-        inputs upload while this step computes (a double-buffered input
-        pipeline) and the gradients download behind the next step; every copy
-        of a timed step happens inside the timed region."""
         if getattr(self, "copy_stream", None) is None:
             self.reset_pipeline()
         compute = torch.cuda.current_stream()
@@ -223,84 +197,230 @@ class OursProjection:
             t.record_stream(compute)
         if prefetch_next:
             self.prefetched = self._upload()
-        params, (vm, K, v_img) = ins[:4], ins[4:]
-        self.step(params, vm, K, v_img)
+        results = self.step(*ins)
         done = torch.cuda.Event()
         done.record(compute)
         self.copy_stream.wait_event(done)
         with torch.cuda.stream(self.copy_stream):
-            outs = [p.grad.to("cpu", non_blocking=True) for p in params]
-            for p in params:
-                p.grad.record_stream(self.copy_stream)
+            outs = [r.to("cpu", non_blocking=True) for r in results]
+            for r in results:
+                r.record_stream(self.copy_stream)
         return outs
 
     def bytes_e2e(self):
-        h2d = sum(t.numel() * t.element_size() for t in self.host) + sum(
-            t.numel() * t.element_size() for t in self.host_cams) + self.host_vimg.numel() * 4
-        d2h = sum(t.numel() * t.element_size() for t in self.host)
-        return h2d, d2h
+        h2d = sum(t.numel() * t.element_size() for t in self.host)
+        return h2d, self.d2h_bytes
 
 
-class OursVoxel:
-    def __init__(self, cfg, world, rank, dev, params):
-        from r2splat.cuda import _wrapper as W
+# ---------------------------------------------------------------------------
+# this build
+# ---------------------------------------------------------------------------
+class OursProjection(HostPipeline):
+    def __init__(self, cfg, world, rank, dev, scaling):
+        from r2splat.ops import explicit as E
 
-        self.W = W
-        self.world = world
-        self.G = cfg.grid
-        self.nt = (self.G + wl.VOL_TILE - 1) // wl.VOL_TILE
-        self.params = params
-        rng, ctr = wl.unit_cube_box()
-        self.rng, self.ctr = rng.to(dev), ctr.to(dev)
-        # z-slabs balanced by records per brick layer (every rank computes the
-        # same ranges from the same mapping)
-        with torch.no_grad():
-            m, q, s, o = params
-            cov, _, op = W.fused_prepare(q, s, o, wl.SCALE_MIN, wl.SCALE_MAX)
-            rects = W.fused_map(m, cov, op, self.rng, self.ctr, self.G, self.G, self.G,
-                                wl.VOL_TILE, self.nt, self.nt, self.nt, wl.EPS3D,
-                                wl.RADIUS_CLIP)[4]
-        self.l0, self.l1 = shard.balanced_layer_ranges(shard.layer_weights(rects, self.nt),
-                                                       world)[rank]
-        z0, z1 = shard.slab_rows(self.l0, self.l1, wl.VOL_TILE, self.G)
-        g = torch.Generator(device=dev).manual_seed(200 + rank)
-        self.v_vol = torch.randn((z1 - z0, self.G, self.G), generator=g, device=dev)
+        self.E, self.world, self.cfg, self.dev = E, world, cfg, dev
+        self.det = cfg.detector
+        m, q, s, o = wl.make_gaussians(cfg)
+        self.params = [t.to(dev) for t in (m, q, s, o)]
+        if scaling == "weak":
+            first, count, total, stride = shard.view_shard(cfg.n_views, rank, world)
+        else:
+            first, count, total, stride = shard.view_split(cfg.n_views, rank, world)
+        self.views = count
+        vm, K = wl.make_cameras(count, cfg.detector, first=first, count=count, total=total,
+                                stride=stride)
+        self.vm, self.K = vm.to(dev), K.to(dev)
+        g = torch.Generator(device=dev).manual_seed(100 + rank)
+        self.v_img = torch.randn((count, self.det, self.det), generator=g, device=dev)
+        self.host = [t.pin_memory() for t in (m, q, s, o, vm, K)] + [self.v_img.cpu().pin_memory()]
+        self.d2h_bytes = sum(t.numel() * t.element_size() for t in (m, q, s, o))
         self.allreduce = shard.GradientAllReduce()
 
-    def step(self):
-        W = self.W
+    def step(self, m=None, q=None, s=None, o=None, vm=None, K=None, v_img=None):
+        E = self.E
+        if m is None:
+            m, q, s, o = self.params
+            vm, K, v_img = self.vm, self.K, self.v_img
+        params = (m, q, s, o)
+        for p in params:
+            p.grad = None
+        st = E.prepare_explicit_gaussians(q, s, o, scale_min=wl.SCALE_MIN, scale_max=wl.SCALE_MAX)
+        res = E.explicit_rasterize(st, m, vm, K, img_w=self.det, img_h=self.det,
+                                   tile_size=wl.IMG_TILE, eps2d=wl.EPS2D,
+                                   radius_clip=wl.RADIUS_CLIP, absgrad=True)
+        res.image.grad = v_img
+        E.explicit_backward(st, *params)
+        grads = [p.grad for p in params]
+        if self.world > 1:
+            self.allreduce(grads)
+        return grads
+
+    def phases(self):
+        """Per-phase device time of one step (CUDA events between the same
+        calls the op layer makes), ms."""
+        from r2splat.cuda import _wrapper as W
+
         m, q, s, o = self.params
-        G, nt = self.G, self.nt
+        C, N, det = self.views, m.size(0), self.det
+        nt = (det + wl.IMG_TILE - 1) // wl.IMG_TILE
+        T = PhaseTimer()
         with torch.no_grad():
             cov, ms, op = W.fused_prepare(q, s, o, wl.SCALE_MIN, wl.SCALE_MAX)
+            T.mark("prepare")
+            m2, radii, splats, rects, _ = W.fused_project(m, cov, op, self.vm, self.K, det, det,
+                                                          wl.IMG_TILE, nt, nt, wl.EPS2D,
+                                                          wl.RADIUS_CLIP)
+            T.mark("project")
+            offs, ids, _ = W.fused_bin(rects, C, N, nt * nt, nt, 0)
+            T.mark("binning (incl. host read of the record count)")
+            cull = torch.empty(ids.shape, dtype=torch.int16, device=self.dev)
+            W.fused_raster_fwd(splats, offs, ids, C, N, det, det, wl.IMG_TILE, nt, nt, cull=cull)
+            T.mark("raster forward")
+            stats = W.fused_raster_bwd(splats, offs, ids, self.v_img, C, N, det, det,
+                                       wl.IMG_TILE, nt, nt, True, cull=cull)
+            T.mark("raster backward")
+            outs = [torch.empty_like(t) for t in (m, q, s, o)]
+            v2 = torch.empty((C, N, 2), device=self.dev)
+            v2a = torch.empty((C, N, 2), device=self.dev)
+            W.fused_explicit_backward(m, q, s, o, wl.SCALE_MIN, wl.SCALE_MAX, self.vm, self.K, det,
+                                      det, wl.EPS2D, stats, v2, v2a, None, None, 0, 0, 0, 0.0,
+                                      None, False, outs)
+            T.mark("explicit backward")
+            if self.world > 1:
+                self.allreduce(outs)
+            T.mark("gradient all-reduce")
+        return T.result()
+
+
+class OursVoxel(HostPipeline):
+    def __init__(self, cfg, world, rank, dev, host_params):
+        from r2splat.ops import explicit as E
+
+        self.E, self.world, self.dev = E, world, dev
+        self.G = G = cfg.grid
+        self.nt = (G + wl.VOL_TILE - 1) // wl.VOL_TILE
+        rng, ctr = wl.unit_cube_box()
+        self.rng, self.ctr = rng.to(dev), ctr.to(dev)
+        self.params = [t.to(dev) for t in host_params]
+        vm1, K1 = wl.make_cameras(VOXEL_STEP_VIEWS, VOXEL_STEP_DETECTOR)
+        self.vm1, self.K1 = vm1.to(dev), K1.to(dev)
+        if world > 1:
+            # z-slabs balanced by records per brick layer (every rank computes
+            # the same ranges from the same mapping)
+            from r2splat.cuda import _wrapper as W
+
+            with torch.no_grad():
+                m, q, s, o = self.params
+                cov, _, op = W.fused_prepare(q, s, o, wl.SCALE_MIN, wl.SCALE_MAX)
+                rects = W.fused_map(m, cov, op, self.rng, self.ctr, G, G, G, wl.VOL_TILE,
+                                    self.nt, self.nt, self.nt, wl.EPS3D, wl.RADIUS_CLIP)[4]
+            self.layers = shard.balanced_layer_ranges(shard.layer_weights(rects, self.nt),
+                                                      world)[rank]
+        else:
+            self.layers = None
+        l0, l1 = self.layers or (0, self.nt)
+        z0, z1 = shard.slab_rows(l0, l1, wl.VOL_TILE, G)
+        g = torch.Generator(device=dev).manual_seed(200 + rank)
+        self.v_vol = torch.randn((z1 - z0, G, G), generator=g, device=dev)
+        self.host = [t.pin_memory() for t in host_params] + [self.v_vol.cpu().pin_memory()]
+        self.d2h_bytes = sum(t.numel() * t.element_size() for t in host_params)
+        self.allreduce = shard.GradientAllReduce()
+
+    def step(self, m=None, q=None, s=None, o=None, v_vol=None):
+        E, G = self.E, self.G
+        if m is None:
+            m, q, s, o = self.params
+            v_vol = self.v_vol
+        params = (m, q, s, o)
+        for p in params:
+            p.grad = None
+        st = E.prepare_explicit_gaussians(q, s, o, scale_min=wl.SCALE_MIN, scale_max=wl.SCALE_MAX)
+        E.explicit_rasterize(st, m, self.vm1, self.K1, img_w=VOXEL_STEP_DETECTOR,
+                             img_h=VOXEL_STEP_DETECTOR, tile_size=wl.IMG_TILE, eps2d=wl.EPS2D,
+                             radius_clip=wl.RADIUS_CLIP, absgrad=False)
+        vr = E.explicit_voxelize(st, m, self.rng, self.ctr, dim2=G, dim1=G, dim0=G,
+                                 tile_size=wl.VOL_TILE, eps3d=wl.EPS3D,
+                                 radius_clip=wl.RADIUS_CLIP, z_layers=self.layers)
+        vr.volume.grad = v_vol
+        E.explicit_backward(st, *params)
+        grads = [p.grad for p in params]
+        if self.world > 1:
+            self.allreduce(grads)
+        return grads
+
+    def phases(self):
+        """Per-phase device time of one voxel step, ms (the same calls the op
+        layer makes, without the empty projection pass)."""
+        from r2splat.cuda import _wrapper as W
+
+        m, q, s, o = self.params
+        G, nt, N = self.G, self.nt, m.size(0)
+        l0, l1 = self.layers or (0, nt)
+        T = PhaseTimer()
+        with torch.no_grad():
+            cov, ms, op = W.fused_prepare(q, s, o, wl.SCALE_MIN, wl.SCALE_MAX)
+            T.mark("prepare")
             m3, c3, r3, vs, rects, _ = W.fused_map(m, cov, op, self.rng, self.ctr, G, G, G,
                                                    wl.VOL_TILE, nt, nt, nt, wl.EPS3D,
                                                    wl.RADIUS_CLIP)
-            S = self.l1 - self.l0
-            offs, fids, _ = W.fused_bin(rects, S, m.size(0), nt * nt, nt, 1, segment_base=self.l0)
-            rows = W.fused_voxel_rows(vs, offs, fids, m.size(0), G, G, G, wl.VOL_TILE, nt, nt, nt,
-                                      self.l0, self.l1)
-            vol = W.fused_voxel_fwd(vs, offs, fids, m.size(0), G, G, G, wl.VOL_TILE, nt, nt, nt,
-                                    self.l0, self.l1, rows=rows)
-            stats = W.fused_voxel_bwd(vs, offs, fids, self.v_vol, m.size(0), G, G, G,
-                                      wl.VOL_TILE, nt, nt, nt, self.l0, self.l1, rows=rows)
+            T.mark("volume mapping")
+            offs, fids, _ = W.fused_bin(rects, l1 - l0, N, nt * nt, nt, 1, segment_base=l0)
+            T.mark("3D binning (incl. host read of the record count)")
+            rows = W.fused_voxel_rows(vs, offs, fids, N, G, G, G, wl.VOL_TILE, nt, nt, nt, l0, l1)
+            T.mark("row table")
+            W.fused_voxel_fwd(vs, offs, fids, N, G, G, G, wl.VOL_TILE, nt, nt, nt, l0, l1,
+                              rows=rows)
+            T.mark("voxel forward")
+            stats = W.fused_voxel_bwd(vs, offs, fids, self.v_vol, N, G, G, G, wl.VOL_TILE, nt, nt,
+                                      nt, l0, l1, rows=rows)
+            T.mark("voxel backward")
             outs = [torch.empty_like(t) for t in (m, q, s, o)]
             W.fused_explicit_backward(m, q, s, o, wl.SCALE_MIN, wl.SCALE_MAX, None, None, 0, 0,
                                       wl.EPS2D, None, None, None, self.rng, self.ctr, G, G, G,
                                       wl.EPS3D, stats, False, outs)
+            T.mark("explicit backward")
             if self.world > 1:
                 self.allreduce(outs)
-        return vol
+            T.mark("gradient all-reduce")
+        res = T.result()
+        res["layers"] = [l0, l1]
+        res["records"] = int(fids.numel())
+        return res
+
+
+class PhaseTimer:
+    """CUDA events between consecutive phases on the current stream."""
+
+    def __init__(self):
+        torch.cuda.synchronize()
+        self.events = [("start", self._ev())]
+
+    @staticmethod
+    def _ev():
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        return e
+
+    def mark(self, name):
+        self.events.append((name, self._ev()))
+
+    def result(self):
+        torch.cuda.synchronize()
+        out = {}
+        for (_, a), (name, b) in zip(self.events, self.events[1:]):
+            out[name] = round(a.elapsed_time(b), 4)
+        return {"ms": out, "total_ms": round(sum(out.values()), 4)}
 
 
 # ---------------------------------------------------------------------------
-# reference implementation (the reference's CUDA build, reference call order)
+# the reference: its unchanged op layer over its own CUDA build
 # ---------------------------------------------------------------------------
 class RefProjection:
     def __init__(self, cfg, dev):
-        from oracle.ref_harness import ReferencePipeline
+        from oracle import ref_stock
 
-        self.ref = ReferencePipeline()
+        self.S = ref_stock.stock_r2splat().explicit
         self.cfg = cfg
         self.det = cfg.detector
         m, q, s, o = wl.make_gaussians(cfg)
@@ -311,41 +431,52 @@ class RefProjection:
         self.v_img = torch.randn((cfg.n_views, self.det, self.det), generator=g, device=dev)
 
     # the reference's int32 tile offsets overflow past 2^31 records (config 3):
-    # there it runs in batches of 20 views, as its users must
+    # there its callers must render in batches; 20 views per batch fit
 
     def step(self):
+        S = self.S
         m, q, s, o = self.params
-        cov, ms, op = self.ref.prepare(q, s, o, wl.SCALE_MIN, wl.SCALE_MAX)
+        for p in self.params:
+            p.grad = None
         C = self.vm.shape[0]
         per = 20 if self.cfg.name.startswith("cfg3") else C
         for c0 in range(0, C, per):
             c1 = min(C, c0 + per)
-            p = self.ref.rasterize_forward(m, cov, op, self.vm[c0:c1], self.K[c0:c1], self.det,
-                                           self.det, wl.IMG_TILE, wl.EPS2D, wl.RADIUS_CLIP)
-            self.ref.explicit_backward(p, self.v_img[c0:c1], None, None, m, q, s, o, cov, op,
-                                       wl.SCALE_MIN, wl.SCALE_MAX, absgrad=True)
-        return p
+            st = S.prepare_explicit_gaussians(q, s, o, scale_min=wl.SCALE_MIN,
+                                              scale_max=wl.SCALE_MAX)
+            res = S.explicit_rasterize(st, m, self.vm[c0:c1], self.K[c0:c1], img_w=self.det,
+                                       img_h=self.det, tile_size=wl.IMG_TILE, eps2d=wl.EPS2D,
+                                       radius_clip=wl.RADIUS_CLIP, absgrad=True)
+            res.image.grad = self.v_img[c0:c1]
+            S.explicit_backward(st, m, q, s, o)
 
 
 class RefVoxel:
     def __init__(self, cfg, dev, proj: RefProjection):
-        self.ref = proj.ref
+        self.S = proj.S
         self.params = proj.params
         self.G = cfg.grid
         rng, ctr = wl.unit_cube_box()
         self.rng, self.ctr = rng.to(dev), ctr.to(dev)
+        vm1, K1 = wl.make_cameras(VOXEL_STEP_VIEWS, VOXEL_STEP_DETECTOR)
+        self.vm1, self.K1 = vm1.to(dev), K1.to(dev)
         g = torch.Generator(device=dev).manual_seed(200)
         self.v_vol = torch.randn((self.G,) * 3, generator=g, device=dev)
 
     def step(self):
+        S, G = self.S, self.G
         m, q, s, o = self.params
-        G = self.G
-        cov, ms, op = self.ref.prepare(q, s, o, wl.SCALE_MIN, wl.SCALE_MAX)
-        v = self.ref.voxelize_forward(m, cov, ms, op, self.rng, self.ctr, G, G, G, wl.VOL_TILE,
-                                      wl.EPS3D, wl.RADIUS_CLIP)
-        self.ref.explicit_backward(None, None, v, self.v_vol, m, q, s, o, cov, op, wl.SCALE_MIN,
-                                   wl.SCALE_MAX)
-        return v
+        for p in self.params:
+            p.grad = None
+        st = S.prepare_explicit_gaussians(q, s, o, scale_min=wl.SCALE_MIN, scale_max=wl.SCALE_MAX)
+        S.explicit_rasterize(st, m, self.vm1, self.K1, img_w=VOXEL_STEP_DETECTOR,
+                             img_h=VOXEL_STEP_DETECTOR, tile_size=wl.IMG_TILE, eps2d=wl.EPS2D,
+                             radius_clip=wl.RADIUS_CLIP, absgrad=False)
+        vr = S.explicit_voxelize(st, m, self.rng, self.ctr, dim2=G, dim1=G, dim0=G,
+                                 tile_size=wl.VOL_TILE, eps3d=wl.EPS3D,
+                                 radius_clip=wl.RADIUS_CLIP)
+        vr.volume.grad = self.v_vol
+        S.explicit_backward(st, m, q, s, o)
 
 
 # ---------------------------------------------------------------------------
@@ -461,21 +592,28 @@ class OursTrain:
 
 
 class RefTrain:
-    """The same step through the reference's kernels (oracle/_ref in its op
-    layer's order) and its PyTorch code: BinaryTreeLossComputer with autograd,
-    the strategy's _update_state, torch.optim.Adam."""
+    """The same step through the reference's own code: its op layer
+    (unchanged, baseline/_ref) over its CUDA build (oracle/_ref), its
+    BinaryTreeLossComputer (src/utils/loss.py, unchanged) with autograd, the
+    strategy's _update_state (restated in the oracle) and torch.optim.Adam."""
 
     def __init__(self, cfg, dev):
         from oracle import r2s_oracle as O
-        from oracle.ref_harness import ReferencePipeline
+        from oracle import ref_stock
 
-        self.O, self.ref, self.cfg, self.dev = O, ReferencePipeline(), cfg, dev
+        self.O, self.cfg, self.dev = O, cfg, dev
+        self.S = ref_stock.stock_r2splat().explicit
+        self.loss = ref_stock.load_loss_module().BinaryTreeLossComputer(**TRAIN_WEIGHTS)
+        S = self.S
         tm, tq, ts, to = (t.to(dev) for t in _teacher(cfg))
 
         def render(vm, K):
-            cov, ms, op = self.ref.prepare(tq, ts, to, wl.SCALE_MIN, wl.SCALE_MAX)
-            return self.ref.rasterize_forward(tm, cov, op, vm, K, cfg.detector, cfg.detector,
-                                              wl.IMG_TILE, wl.EPS2D, wl.RADIUS_CLIP)["output"]
+            st = S.prepare_explicit_gaussians(tq, ts, to, scale_min=wl.SCALE_MIN,
+                                              scale_max=wl.SCALE_MAX)
+            return S.explicit_rasterize(st, tm, vm, K, img_w=cfg.detector, img_h=cfg.detector,
+                                        tile_size=wl.IMG_TILE, eps2d=wl.EPS2D,
+                                        radius_clip=wl.RADIUS_CLIP,
+                                        absgrad=False).image.detach().clone()
 
         self.data = TrainData(cfg, dev, render)
         m, q, s, o = wl.make_gaussians(cfg)
@@ -487,27 +625,23 @@ class RefTrain:
         self.step_no = 0
 
     def step(self):
-        d, P, R, O = self.data, self.params, self.ref, self.O
+        d, P, S, O = self.data, self.params, self.S, self.O
         views = d.step_views(self.step_no, 0, 1).to(self.dev)
         rng, ctr = d.step_box(self.step_no, self.dev)
         self.step_no += 1
-        m, q, s, o = (P[k].detach() for k in ("means", "quats", "scales", "opacities"))
-        cov, ms, op = R.prepare(q, s, o, wl.SCALE_MIN, wl.SCALE_MAX)
-        p = R.rasterize_forward(m, cov, op, d.vm[views], d.K[views], d.det, d.det, wl.IMG_TILE,
-                                wl.EPS2D, wl.RADIUS_CLIP)
-        v = R.voxelize_forward(m, cov, ms, op, rng, ctr, TRAIN_TV, TRAIN_TV, TRAIN_TV,
-                               wl.VOL_TILE, wl.EPS3D, wl.RADIUS_CLIP)
-        image = p["output"].detach().requires_grad_(True)
-        volume = v["output"].detach().requires_grad_(True)
-        out = O.binary_tree_losses(image[..., None], d.targets[views][..., None],
-                                   d.edge[views][..., None], volume, **TRAIN_WEIGHTS)
+        st = S.prepare_explicit_gaussians(P["quats"], P["scales"], P["opacities"],
+                                          scale_min=wl.SCALE_MIN, scale_max=wl.SCALE_MAX)
+        res = S.explicit_rasterize(st, P["means"], d.vm[views], d.K[views], img_w=d.det,
+                                   img_h=d.det, tile_size=wl.IMG_TILE, eps2d=wl.EPS2D,
+                                   radius_clip=wl.RADIUS_CLIP, absgrad=True)
+        vox = S.explicit_voxelize(st, P["means"], rng, ctr, dim2=TRAIN_TV, dim1=TRAIN_TV,
+                                  dim0=TRAIN_TV, tile_size=wl.VOL_TILE, eps3d=wl.EPS3D,
+                                  radius_clip=wl.RADIUS_CLIP)
+        out = self.loss(res.image[..., None], d.targets[views][..., None],
+                        d.edge[views][..., None], vox.volume)
         out["total"].backward()
-        g = R.explicit_backward(p, image.grad, v, volume.grad, m, q, s, o, cov, op,
-                                wl.SCALE_MIN, wl.SCALE_MAX, absgrad=True)
-        for k, gk in (("means", "means"), ("quats", "quats"), ("scales", "scales"),
-                      ("opacities", "opacities")):
-            P[k].grad = g[gk]
-        O.densify_state_update(self.densify, g["means2d_abs"], p["radii"].amax(dim=-1), d.det,
+        S.explicit_backward(st, P["means"], P["quats"], P["scales"], P["opacities"])
+        O.densify_state_update(self.densify, res.means2d.absgrad, res.radii.amax(dim=-1), d.det,
                                d.det, len(views))
         for opt in self.opts.values():
             opt.step()
@@ -521,11 +655,11 @@ def run_train_bench(args, cfg, dev, world, rank, local, flush):
     ref = args.impl == "reference"
     if ref:
         try:
-            from oracle.ref_harness import reference_available
+            from oracle.ref_stock import stock_available
 
-            if not reference_available():
+            if not stock_available():
                 print(json.dumps({"impl": "reference", "unavailable":
-                                  "reference sm_100a build oracle/_ref missing"}))
+                                  "reference install baseline/_ref or build oracle/_ref missing"}))
                 return
             trainer = RefTrain(cfg, dev)
         except Exception as exc:
@@ -548,7 +682,7 @@ def run_train_bench(args, cfg, dev, world, rank, local, flush):
                    "views_per_step": TRAIN_VIEWS_PER_STEP, "detector": cfg.detector,
                    "tv_subvolume": TRAIN_TV, "loss": TRAIN_WEIGHTS,
                    "step": "prepare + rasterize + 64^3 voxelize + L1/SSIM/edge/TV losses + "
-                           "backward with fused densify stats + grad all-reduce + Adam",
+                           "backward with densify stats + grad all-reduce + Adam",
                    "split": "binary split every 100 steps lies outside the timed window",
                    "l2": "256MiB flush between steps"},
         "clocks": clk.summary(),
@@ -588,22 +722,22 @@ def time_steps(fn, steps, warmup, world, flush):
     return max_over_ranks(world, ms)
 
 
-def time_e2e(proj, steps, warmup, world, flush):
+def time_e2e(pipe: HostPipeline, steps, warmup, world, flush):
     """Wall time per step of the end-to-end step, inputs uploaded from and
-    gradients downloaded to pinned host memory inside the timed region (the
+    outputs downloaded to pinned host memory inside the timed region (the
     pipeline is emptied before it, so the first step's upload is timed and no
     upload past the last step is)."""
     for _ in range(warmup):
         flush.zero_()
-        proj.step_e2e(prefetch_next=False)
+        pipe.step_e2e(prefetch_next=False)
         torch.cuda.synchronize()
-    proj.reset_pipeline()
+    pipe.reset_pipeline()
     barrier(world)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     for i in range(steps):
         flush.zero_()
-        proj.step_e2e(prefetch_next=i + 1 < steps)
+        pipe.step_e2e(prefetch_next=i + 1 < steps)
     torch.cuda.synchronize()
     dt = (time.perf_counter() - t0) * 1e3 / steps
     barrier(world)
@@ -625,25 +759,78 @@ def kernel_time(fn, reps=3):
     return sum(ts) / len(ts)
 
 
-# DRAM traffic of one raster_bwd16_kernel launch per view, from the ncu
-# capture of `bench.py --views 8` (dram__bytes_read.sum + dram__bytes_write.sum
-# = 441.2 MB + 103.9 MB for 8 views; traffic grows with the views).
-BWD16_DRAM_BYTES_PER_VIEW = (441.213952e6 + 103.907328e6) / 8
+def pipe_peaks(dev):
+    """FP32 (FFMA) and MUFU ex2 throughput of this GPU at its current clock,
+    from the library's calibration kernels (r2s_calib_ffma_f32 /
+    r2s_calib_ex2_f32: 148 x 8 CTAs of 256 threads, 8 independent chains per
+    thread), best of three CUDA-event timings."""
+    import ctypes
+
+    from r2splat.cuda._backend import _C
+
+    n_sm = torch.cuda.get_device_properties(dev).multi_processor_count
+    blocks = n_sm * 8
+    out = torch.empty(blocks * 256, device=dev)
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    res = {}
+    for name, fn, iters, per in (("ffma", _C.r2s_calib_ffma_f32, 16384, 2.0),
+                                 ("ex2", _C.r2s_calib_ex2_f32, 4096, 1.0)):
+        def launch():
+            rc = fn(ctypes.c_void_p(out.data_ptr()), iters, blocks, st)
+            if rc:
+                raise RuntimeError(f"calibration {name} failed ({rc})")
+
+        launch()
+        best = min(kernel_time(launch, 1) for _ in range(3))
+        ops = blocks * 256 * 8 * iters
+        res[name] = ops * per / (best * 1e-3)
+    return {"fp32_tflops": round(res["ffma"] / 1e12, 2),
+            "ex2_per_s": round(res["ex2"], -8), "sm_count": n_sm,
+            "how": "r2s_calib_*: 8 CTAs of 256 threads per SM, 8 independent FFMA (2 FLOP) or "
+                   "FMUL+ex2.approx chains per thread, best of 3 CUDA-event timings"}
 
 
-def dominant_kernel_roofline(proj: OursProjection, hbm_peak, peak_kind, clock_mhz):
-    """Raster backward (the largest share of the step) on its own launch.
+# DRAM traffic of one raster_bwd16_kernel launch per view: the ncu capture of
+# `bench.py --views 8` in profiles/raster_bwd16_cfg2_8views.md,
+# dram__bytes_read.sum + dram__bytes_write.sum = 530.674 MB + 105.416 MB for 8
+# views (traffic grows with the views).
+BWD16_DRAM_BYTES_PER_VIEW = (530.674176e6 + 105.415936e6) / 8
+# FP32 work per evaluated pixel of raster_bwd16_kernel<true> (absolute
+# gradients on), counted from its inner loop: 7 FFMA (the exponent: 2; the row
+# moment R1; the two conic products a dx + b dy, b dx + c dy; the two absolute
+# sums), 1 FMUL (v e) and 2 FADD (the column and row sums): 10 FP32-pipe
+# instructions, 17 FLOP, and 1 MUFU ex2.
+BWD16_FLOP_PER_PAIR = 17
+BWD16_FP32_INST_PER_PAIR = 10
 
-    Algorithmic (compulsory) bytes per launch: the flatten ids (4 B per
-    intersection record), every (view, Gaussian) splat record once (32 B) and
-    its statistics once (32 B), the upstream image (4 B per pixel) and the
-    tile offsets (4 B per tile).  The kernel is bound by the SM pipes, not by
-    HBM.  `sfu` and `fp32` count the algorithmic pairs P2 = n_isects x
-    tile_size^2 (the reference evaluates every pixel of a record's tile, one
-    exponential and 30 FP32 flops each) against 16 ex2 per clock per SM at
-    the sampled SM clock and against the nominal FP32 peak.  The kernel
-    itself evaluates fewer pairs (only the rows or columns a record's
-    ellipse reaches inside the tile), so these fractions can exceed 1."""
+
+def evaluated_pairs(cull: torch.Tensor) -> int:
+    """Pixels raster_bwd16_kernel evaluates for the records of one binning:
+    16 per walked line, where a record walks the rows or the columns of its
+    culled box inside the tile, whichever are fewer (the culling table of the
+    forward: c_lo | c_hi << 4 | r_lo << 8 | r_hi << 12)."""
+    v = cull.to(torch.int32) & 0xFFFF
+    cols = ((v >> 4) & 15) - (v & 15) + 1
+    rows = ((v >> 12) & 15) - ((v >> 8) & 15) + 1
+    live = (cols > 0) & (rows > 0)
+    lines = torch.minimum(cols, rows).clamp_min(0) * live
+    return int(lines.sum(dtype=torch.int64).item()) * 16
+
+
+def dominant_kernel_roofline(proj: OursProjection, hbm_peak, peak_kind, peaks):
+    """The raster backward (the largest share of the step) on its own launch.
+
+    It is bound by the SM's FP32 pipe and instruction issue, not by HBM:
+    ``achieved`` is the FP32 work on the pixels it evaluates (the walked lines
+    of each record's culled box, ``evaluated_pairs``; 17 FLOP each) per second,
+    against the FFMA throughput this bench measures on the same GPU
+    (``pipe_peaks``).  The reference's pair count (every pixel of every
+    record's tile, n_isects x 256) is reported beside it, as are the MUFU ex2
+    rate (one ex2 per evaluated pair) and the HBM view: compulsory bytes per
+    launch (flatten ids 4 B per record, splat record 32 B and statistics 32 B
+    per (view, Gaussian), upstream image 4 B per pixel, offsets 4 B per tile)
+    against the measured copy bandwidth, and the DRAM traffic of the ncu
+    capture."""
     from r2splat.cuda import _wrapper as W
 
     E = proj.E
@@ -658,6 +845,7 @@ def dominant_kernel_roofline(proj: OursProjection, hbm_peak, peak_kind, clock_mh
     batches = pb.view_batches or [(0, C, pb.flatten_ids)]
     culls = pb.cull if isinstance(pb.cull, list) else [pb.cull]
     n_isects = sum(ids.numel() for _, _, ids in batches)
+    pairs_eval = sum(evaluated_pairs(c) for c in culls)
     stats = torch.empty((C * N, 8), dtype=torch.float32, device=pb.splats.device)
 
     def launch():
@@ -668,36 +856,39 @@ def dominant_kernel_roofline(proj: OursProjection, hbm_peak, peak_kind, clock_mh
 
     launch()
     ms = kernel_time(launch)
+    t = ms * 1e-3
     alg_bytes = (n_isects * 4 + C * N * (32 + 32) + C * proj.det * proj.det * 4
                  + C * ntx * nty * 4)
     cfg2_shaped = proj.cfg.name.startswith("cfg2")
-    achieved = alg_bytes / (ms * 1e-3) / 1e9
-    pairs = n_isects * wl.IMG_TILE * wl.IMG_TILE
-    mhz = clock_mhz or 1965.0
-    sfu_peak = 148 * 16 * mhz * 1e6
-    fp32_peak = 148 * 128 * 2 * mhz * 1e6 / 1e12
-    tflops = pairs * 30 / (ms * 1e-3) / 1e12
+    tflops = pairs_eval * BWD16_FLOP_PER_PAIR / t / 1e12
+    fp32_peak = peaks["fp32_tflops"]
+    lane_ops_peak = fp32_peak * 1e12 / 2  # FFMA lane-instructions per second
     return {
         "kernel": "raster_bwd16_kernel<true>",
-        "bound": "hbm",
-        "achieved": round(achieved, 1),
-        "peak": hbm_peak,
-        "unit": "GB/s",
-        "frac": round(achieved / hbm_peak, 4),
-        "peak_source": peak_kind,
+        "bound": "fp32",
+        "achieved": round(tflops, 2),
+        "peak": fp32_peak,
+        "unit": "TFLOP/s",
+        "frac": round(tflops / fp32_peak, 4),
+        "peak_source": "measured in this run (FFMA calibration kernel, same GPU and clock)",
         "traffic": round(BWD16_DRAM_BYTES_PER_VIEW * C) if cfg2_shaped else None,
+        "traffic_source": ("ncu capture at 8 views (profiles/raster_bwd16_cfg2_8views.md), "
+                           "scaled by views" if cfg2_shaped else "no ncu capture of this "
+                           "configuration"),
         "alg_bytes": alg_bytes,
-        "traffic_source": ("ncu capture at 8 views, scaled by views" if cfg2_shaped
-                           else "no ncu capture of this configuration"),
         "launches": len(batches),
         "ms_per_launch": round(ms, 3),
         "n_isects": n_isects,
-        "sfu": {"achieved_ex2_per_s": round(pairs / (ms * 1e-3), -6),
-                "peak_ex2_per_s": round(sfu_peak, -6), "frac": round(pairs / (ms * 1e-3) / sfu_peak, 4),
-                "pairs": pairs, "pairs_basis": "algorithmic n_isects x 256; the kernel culls",
-                "clock_mhz": mhz},
-        "fp32": {"achieved_tflops": round(tflops, 2), "peak_tflops_nominal": round(fp32_peak, 1),
-                 "frac": round(tflops / fp32_peak, 4), "flops_per_pair": 30},
+        "pairs_evaluated": pairs_eval,
+        "pairs_reference": n_isects * wl.IMG_TILE * wl.IMG_TILE,
+        "flop_per_pair": BWD16_FLOP_PER_PAIR,
+        "fp32_pipe": {"inst_per_pair": BWD16_FP32_INST_PER_PAIR,
+                      "frac": round(pairs_eval * BWD16_FP32_INST_PER_PAIR / t / lane_ops_peak, 4)},
+        "sfu": {"achieved_ex2_per_s": round(pairs_eval / t, -6),
+                "peak_ex2_per_s": peaks["ex2_per_s"],
+                "frac": round(pairs_eval / t / peaks["ex2_per_s"], 4)},
+        "hbm": {"achieved_gbs": round(alg_bytes / t / 1e9, 1), "peak_gbs": hbm_peak,
+                "peak_source": peak_kind, "frac": round(alg_bytes / t / 1e9 / hbm_peak, 4)},
     }
 
 
@@ -737,6 +928,9 @@ def training_rows(cfg, dev, reference: bool, reps: int = 10):
     weights = dict(w_l1=0.8, w_ssim=0.2, w_tv=0.05, w_edge=0.1)
     if reference:
         from oracle import r2s_oracle as O
+        from oracle import ref_stock
+
+        computer = ref_stock.load_loss_module().BinaryTreeLossComputer(**weights)
 
         def adam():
             for o in opts.values():
@@ -748,7 +942,7 @@ def training_rows(cfg, dev, reference: bool, reps: int = 10):
 
         def loss():
             renders.grad = vol.grad = None
-            O.binary_tree_losses(renders, targets, edge_mask, vol, **weights)["total"].backward()
+            computer(renders, targets, edge_mask, vol)["total"].backward()
     else:
         from r2splat.ops import training as T
 
@@ -799,9 +993,52 @@ def cpu_baseline(cfg, seconds_budget=15.0):
         n *= 2
     return {"value": round(n / dt, 1), "unit": "Gaussian*views/s", "cores": threads,
             "kind": "port",
-            "sample": f"{n} Gaussians of config-{2} distributions x 1 view at {cfg.detector}^2, "
+            "sample": f"{n} Gaussians of {cfg.name} distributions x 1 view at {cfg.detector}^2, "
                       f"dense over all pixels with tile-membership mask, fwd+autograd bwd, "
                       f"{dt:.1f} s"}
+
+
+def run_reference(args, cfg, dev, local, flush):
+    try:
+        from oracle.ref_stock import stock_available
+
+        if not stock_available():
+            print(json.dumps({"impl": "reference", "unavailable":
+                              "reference install baseline/_ref or build oracle/_ref missing"}))
+            return
+        proj = RefProjection(cfg, dev)
+        vox = RefVoxel(cfg, dev, proj)
+    except Exception as exc:  # the reference cannot be loaded
+        print(json.dumps({"impl": "reference", "unavailable": f"{type(exc).__name__}: {exc}"}))
+        return
+    with ClockSampler(local) as clk:
+        ms = time_steps(proj.step, args.steps, args.warmup, 1, flush)
+        vms = time_steps(vox.step, args.steps, args.warmup, 1, flush)
+    del proj, vox
+    torch.cuda.empty_cache()
+    train = training_rows(cfg, dev, reference=True)
+    value = cfg.n_gaussians * cfg.n_views / (ms * 1e-3)
+    line = {
+        "metric": "Gaussian*views/s projection fwd+bwd (and Mvoxels/s voxelize fwd+bwd)",
+        "impl": "reference", "value": round(value, 1), "unit": "Gaussian*views/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, r2s_workloads)",
+        "config": job_config(cfg, cfg.n_views),
+        "voxelize": {"value": round(cfg.grid ** 3 / (vms * 1e-3) / 1e6, 2),
+                     "unit": "Mvoxels/s", "ms_per_step": round(vms, 3)},
+        "cpu_baseline": {"value": round(value, 1), "unit": "Gaussian*views/s", "cores": 0,
+                         "kind": "reference",
+                         "sample": "the reference's op layer over its CUDA build (it ships no "
+                                   "CPU implementation), full workload on GPU 0"},
+        "e2e": {"value": round(value, 1), "unit": "Gaussian*views/s",
+                "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "implementation": "reference r2splat.ops (baseline/_ref, unchanged) over its CUDA "
+                          "sources built for sm_100a (oracle/_ref)",
+        "training": train,
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line))
 
 
 def main():
@@ -811,8 +1048,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--config", type=int, default=2)
+    ap.add_argument("--scaling", choices=("strong", "weak"), default="strong",
+                    help="strong: the job's views split over the GPUs; weak: every GPU "
+                         "renders the config's views of a larger orbit")
     ap.add_argument("--views", type=int, default=None,
-                    help="override the views per GPU (small profiling cases)")
+                    help="override the job's views (small profiling cases)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.impl == "reference" and int(os.environ.get("RANK", "0")) != 0:
@@ -832,70 +1072,46 @@ def main():
     if args.config == 4:
         run_train_bench(args, cfg, dev, world, rank, local, flush)
         return
-
     if args.impl == "reference":
-        try:
-            from oracle.ref_harness import reference_available
-
-            if not reference_available():
-                print(json.dumps({"impl": "reference", "unavailable":
-                                  "reference sm_100a build oracle/_ref missing"}))
-                return
-            proj = RefProjection(cfg, dev)
-            vox = RefVoxel(cfg, dev, proj)
-        except Exception as exc:  # reference build cannot be loaded
-            print(json.dumps({"impl": "reference", "unavailable": f"{type(exc).__name__}: {exc}"}))
-            return
-        with ClockSampler(local) as clk:
-            ms = time_steps(proj.step, args.steps, args.warmup, 1, flush)
-            vms = time_steps(vox.step, args.steps, args.warmup, 1, flush)
-        del proj, vox
-        torch.cuda.empty_cache()
-        train = training_rows(cfg, dev, reference=True)
-        value = cfg.n_gaussians * cfg.n_views / (ms * 1e-3)
-        line = {
-            "metric": "Gaussian*views/s projection fwd+bwd (and Mvoxels/s voxelize fwd+bwd)",
-            "impl": "reference", "value": round(value, 1), "unit": "Gaussian*views/s",
-            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, r2s_workloads)",
-            "config": {"workload": cfg.name, "n_gaussians": cfg.n_gaussians,
-                       "views": cfg.n_views, "detector": cfg.detector, "grid": cfg.grid,
-                       "l2": "256MiB flush between steps"},
-            "voxelize": {"value": round(cfg.grid ** 3 / (vms * 1e-3) / 1e6, 2),
-                         "unit": "Mvoxels/s", "ms_per_step": round(vms, 3)},
-            "cpu_baseline": {"value": round(value, 1), "unit": "Gaussian*views/s", "cores": 0,
-                             "kind": "reference",
-                             "sample": "the reference's CUDA build (it ships no CPU "
-                                       "implementation), full workload on GPU 0"},
-            "e2e": {"value": round(value, 1), "unit": "Gaussian*views/s",
-                    "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-            "training": train,
-            "clocks": clk.summary(),
-        }
-        print(json.dumps(line))
+        run_reference(args, cfg, dev, local, flush)
         return
 
-    proj = OursProjection(cfg, world, rank, dev)
+    proj = OursProjection(cfg, world, rank, dev, args.scaling)
+    job_views = cfg.n_views * (world if args.scaling == "weak" else 1)
     with ClockSampler(local) as clk:
         ms = time_steps(proj.step, args.steps, args.warmup, world, flush)
         e2e_ms = time_e2e(proj, args.steps, max(1, args.warmup // 2), world, flush)
-        roof = dominant_kernel_roofline(proj, hbm_peak, peak_kind, clk.summary()["sm_mhz"]) \
-            if rank == 0 else None
-        vox = OursVoxel(cfg, world, rank, dev, proj.params)
+        peaks = pipe_peaks(dev)
+        roof = (dominant_kernel_roofline(proj, hbm_peak, peak_kind, peaks)
+                if rank == 0 else None)
+        proj_phases = proj.phases()
+        h2d, d2h = proj.bytes_e2e()
+        del proj
         torch.cuda.empty_cache()
+        vox = OursVoxel(cfg, world, rank, dev, wl.make_gaussians(cfg))
         vms = time_steps(vox.step, args.steps, args.warmup, world, flush)
+        v_e2e_ms = time_e2e(vox, args.steps, max(1, args.warmup // 2), world, flush)
+        vox_phases = vox.phases()
+        vh2d, vd2h = vox.bytes_e2e()
     del vox
     torch.cuda.empty_cache()
+    phases = {"projection": proj_phases, "voxelize": vox_phases}
+    if world > 1:
+        import torch.distributed as dist
+
+        gathered = [None] * world
+        dist.all_gather_object(gathered, phases)
+        phases = {"per_rank": gathered}
     train = training_rows(cfg, dev, reference=False) if rank == 0 else None
-    value = world * cfg.n_gaussians * cfg.n_views / (ms * 1e-3)
-    e2e_value = world * cfg.n_gaussians * cfg.n_views / (e2e_ms * 1e-3)
-    h2d, d2h = proj.bytes_e2e()
+    value = cfg.n_gaussians * job_views / (ms * 1e-3)
+    e2e_value = cfg.n_gaussians * job_views / (e2e_ms * 1e-3)
+    vox_value = cfg.grid ** 3 / (vms * 1e-3) / 1e6
     barrier(world)
     # our kernels per timed step: projection = prepare, project_splats, binning
     # (count, column scan, scan, place), raster forward, raster backward,
-    # explicit backward; voxel = prepare, map, binning (4), row table, voxel
-    # forward, voxel backward, explicit backward
+    # explicit backward; voxel = prepare, map, binning (count, column scan,
+    # scan, place), row table, voxel forward, voxel backward, explicit
+    # backward (the zero-view projection pass launches nothing)
     gpu_launches = args.steps * 9
     vox_launches = args.steps * 10
     if rank != 0:
@@ -904,19 +1120,23 @@ def main():
         "metric": "Gaussian*views/s projection fwd+bwd (and Mvoxels/s voxelize fwd+bwd)",
         "value": round(value, 1), "unit": "Gaussian*views/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded, r2s_workloads)",
-        "config": {"workload": cfg.name, "n_gaussians": cfg.n_gaussians,
-                   "views_per_gpu": cfg.n_views, "detector": cfg.detector, "grid": cfg.grid,
-                   "parallelism": f"views x{world} (weak) + grad all-reduce; voxel z-slabs x{world}",
-                   "l2": "256MiB flush between steps"},
-        "voxelize": {"value": round(cfg.grid ** 3 / (vms * 1e-3) / 1e6, 2), "unit": "Mvoxels/s",
+        "config": job_config(cfg, job_views),
+        "parallelism": (f"{job_views} views dealt over {world} GPU(s) + NCCL gradient all-reduce; "
+                        f"voxel grid in {world} balanced z-slab(s)"),
+        "voxelize": {"value": round(vox_value, 2), "unit": "Mvoxels/s",
                      "ms_per_step": round(vms, 3), "scaling": "strong (z-slabs)",
-                     "gpu_launches": vox_launches},
+                     "gpu_launches": vox_launches,
+                     "e2e": {"value": round(cfg.grid ** 3 / (v_e2e_ms * 1e-3) / 1e6, 2),
+                             "unit": "Mvoxels/s", "h2d_bytes_per_step": vh2d,
+                             "d2h_bytes_per_step": vd2h, "ms_per_step": round(v_e2e_ms, 3)}},
         "e2e": {"value": round(e2e_value, 1), "unit": "Gaussian*views/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": round(e2e_ms, 3)},
         "roofline": roof,
+        "pipe_peaks": peaks,
+        "phases": phases,
         "training": train,
         "gpu_launches": gpu_launches,
         "clocks": clk.summary(),

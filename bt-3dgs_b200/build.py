@@ -3,7 +3,8 @@
 Every CUDA source under ``csrc/`` is compiled with nvcc for sm_100a
 (``-gencode arch=compute_100a,code=sm_100a``) with the arithmetic flags of
 the reference build (``-O3 --use_fast_math``: the integer binning outputs
-depend on the same float rounding), then linked into
+depend on the same float rounding) -- except ``*_precise.cu``, compiled
+without fast math to reproduce torch's float kernels -- then linked into
 ``r2splat/_lib/libr2s.so``.  Objects are cached in ``_build/`` and rebuilt
 when a source or header is newer.
 
@@ -74,7 +75,12 @@ def build(jobs: int | None = None, force: bool = False, verbose: bool = False) -
 
     def compile_one(item):
         src, obj = item
-        cmd = [nvcc, *NVCC_FLAGS, "-I", INCLUDE, "-c", src, "-o", obj]
+        flags = NVCC_FLAGS
+        if src.endswith("_precise.cu"):
+            # accurate libm and IEEE division/sqrt, no flush-to-zero: these
+            # kernels reproduce torch's float arithmetic bit for bit
+            flags = [f for f in NVCC_FLAGS if f != "--use_fast_math"]
+        cmd = [nvcc, *flags, "-I", INCLUDE, "-c", src, "-o", obj]
         if src.endswith(".cpp"):
             cmd = [nvcc, "-O3", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler",
                    "-fvisibility=hidden", "-I", INCLUDE, "-c", src, "-o", obj]

@@ -22,6 +22,9 @@ constexpr int kThreads = 256;
 // ---------------------------------------------------------------------------
 int fail(int code, const char* fmt, ...);
 int check_launch(const char* what);
+// torch.nn.functional.softplus in float, bit for bit (r2s_precise.cu, built
+// without fast math)
+int launch_softplus_f32(const float* x, float* y, int64_t n, cudaStream_t stream);
 
 // Opt a kernel in to `bytes` of dynamic shared memory; R2S_ERR_CUDA on failure.
 template <typename Kernel>

@@ -179,10 +179,12 @@ __device__ __forceinline__ float sigmoid_f(float x) {
     return static_cast<float>(1.0 / (1.0 + exp(-static_cast<double>(x))));
 }
 
+// Parameter transform of the fused path (covariances and max scales); the
+// opacities come from launch_softplus_f32 (r2s_precise.cu), which matches
+// torch.nn.functional.softplus bit for bit.
 __global__ void prepare_kernel(const float* __restrict__ quats, const float* __restrict__ so,
-                               const float* __restrict__ raw_opac, float smin, float smax,
-                               float* __restrict__ covars, float* __restrict__ max_scales,
-                               float* __restrict__ opac, int64_t n) {
+                               float smin, float smax, float* __restrict__ covars,
+                               float* __restrict__ max_scales, int64_t n) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     RotScale<float> o;
@@ -192,7 +194,6 @@ __global__ void prepare_kernel(const float* __restrict__ quats, const float* __r
     covar_from(o, cov);
 #pragma unroll
     for (int k = 0; k < 6; ++k) covars[i * 6 + k] = cov[k];
-    opac[i] = softplus_f(raw_opac[i]);
 }
 
 // ===========================================================================
@@ -1087,10 +1088,10 @@ extern "C" int r2s_prepare_gaussians_f32(const float* quats, const float* raw_sc
                                          int64_t n, r2s_stream_t stream) {
     R2S_REQUIRE(n >= 0, "prepare_gaussians: negative N");
     if (n == 0) return R2S_OK;
-    prepare_kernel<<<grid_for(n), kThreads, 0, stream>>>(quats, raw_scales, raw_opacities,
-                                                          (float)smin, (float)smax, covars,
-                                                          max_scales, opacities, n);
-    return check_launch("prepare_gaussians");
+    prepare_kernel<<<grid_for(n), kThreads, 0, stream>>>(quats, raw_scales, (float)smin,
+                                                          (float)smax, covars, max_scales, n);
+    if (int rc = check_launch("prepare_gaussians")) return rc;
+    return launch_softplus_f32(raw_opacities, opacities, n, stream);
 }
 
 extern "C" int r2s_world_to_image_projection_fwd(int dtype, const void* means, const void* covars,

@@ -1,9 +1,11 @@
 """Host-side sharding of the r2splat hot path over one process per GPU.
 
-Projection: every rank renders its own views of a shared orbit (weak
-scaling), every world-th view starting at its rank, so that each rank's views
-span the whole circle and see the same amount of the scene (contiguous arcs
-differ by several per cent in intersection records); the raw-parameter
+Projection: the views of one orbit are dealt to the ranks, every world-th view
+starting at the rank's index (``view_split``: the job's views split across
+the GPUs, strong scaling; ``view_shard``: every rank renders the same number
+of views of a world-times-larger orbit, weak scaling), so that each rank's
+views span the whole circle and see the same amount of the scene (contiguous
+arcs differ by several per cent in intersection records); the raw-parameter
 gradients are summed across ranks;
 the gradient is linear in the per-view contributions, so the sum equals the
 single-process gradient over all views.  Voxelization: the brick layers of
@@ -24,6 +26,15 @@ def view_shard(views_per_rank: int, rank: int, world: int) -> Tuple[int, int, in
     if not 0 <= rank < world:
         raise ValueError(f"rank {rank} outside world of {world}")
     return rank, views_per_rank, views_per_rank * world, world
+
+
+def view_split(n_views: int, rank: int, world: int) -> Tuple[int, int, int, int]:
+    """(first view, view count, orbit size, stride) of `rank`'s share of a job
+    of `n_views` views: views rank, rank + world, ... of that orbit (ranks
+    hold ceil or floor of n_views / world views)."""
+    if not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside world of {world}")
+    return rank, len(range(rank, n_views, world)), n_views, world
 
 
 def layer_range(n_layers: int, rank: int, world: int) -> Tuple[int, int]:

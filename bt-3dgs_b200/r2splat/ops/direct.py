@@ -102,6 +102,11 @@ class VoxelForwardBuffers:
     isect_ids: Optional[torch.Tensor] = None
     # float32 8-voxel bricks: per-record row table of the binning (r2s_voxel_rows_f32)
     rows: Optional[torch.Tensor] = None
+    # brick layers [layer_begin, layer_end) along dim0 that were voxelized (a
+    # z-slab; the whole grid by default): tile_offsets then holds those layers
+    # only, indexing this slab's flatten_ids, and output their voxel rows
+    layer_begin: int = 0
+    layer_end: Optional[int] = None
 
 
 def _fast(*tensors: torch.Tensor) -> bool:
@@ -300,11 +305,18 @@ def _voxelize_forward(
     tile_size: int,
     eps3d: float,
     radius_clip: float,
+    z_layers: Optional[tuple] = None,
 ) -> VoxelForwardBuffers:
     from ..cuda import _wrapper as W
 
     dim2, dim1, dim0, tile_size = int(dim2), int(dim1), int(dim0), int(tile_size)
     nt2, nt1, nt0 = _tile_grid_3d(dim2, dim1, dim0, tile_size)
+    if z_layers is None:
+        l0, l1 = 0, nt0
+    else:
+        l0, l1 = (int(v) for v in z_layers)
+        if not 0 <= l0 <= l1 <= nt0:
+            raise ValueError(f"z_layers must satisfy 0 <= begin <= end <= {nt0} brick layers.")
     means_c = means.contiguous()
     covars_c = covars.contiguous()
     ranges_c = ranges.contiguous()
@@ -324,18 +336,22 @@ def _voxelize_forward(
             means3d, conics, radii, vsplats, rects, _ = W.fused_map(
                 means_c, covars_c, opac, ranges_c, centers_c, dim2, dim1, dim0, tile_size, nt2,
                 nt1, nt0, eps3d, radius_clip)
-            offsets, flatten_ids, _ = W.fused_bin(rects, nt0, N, nt1 * nt2, nt2, 1)
-            tile_offsets = offsets.view(nt0, nt1, nt2)
+            # binning of layers [l0, l1) in the global key space (segment l0 first)
+            offsets, flatten_ids, _ = W.fused_bin(rects, l1 - l0, N, nt1 * nt2, nt2, 1,
+                                                  segment_base=l0)
+            tile_offsets = offsets.view(l1 - l0, nt1, nt2)
             rows = W.fused_voxel_rows(vsplats, tile_offsets, flatten_ids, N, dim2, dim1, dim0,
-                                      tile_size, nt2, nt1, nt0)
+                                      tile_size, nt2, nt1, nt0, l0, l1)
             output = W.fused_voxel_fwd(vsplats, tile_offsets, flatten_ids, N, dim2, dim1, dim0,
-                                       tile_size, nt2, nt1, nt0, rows=rows)
+                                       tile_size, nt2, nt1, nt0, l0, l1, rows=rows)
         return VoxelForwardBuffers(
             output=output, means3d=means3d, radii=radii, tile_offsets=tile_offsets,
             flatten_ids=flatten_ids, ranges=ranges_c, centers=centers_c, dim2=dim2, dim1=dim1,
             dim0=dim0, tile_size=tile_size, eps3d=float(eps3d), vsplats=vsplats, conics=conics,
-            opacity=opac, rows=rows)
+            opacity=opac, rows=rows, layer_begin=l0, layer_end=l1)
 
+    if z_layers is not None and (l0, l1) != (0, nt0):
+        raise RuntimeError("z_layers (a z-slab of the grid) needs float32 inputs")
     # reference operator chain (r2splat/ops/direct.py:284-326)
     means3d, conics, radii = W.world_to_volume_mapping_fwd(
         means_c, covars_c, max_scales.contiguous(), ranges_c, centers_c, dim2, dim1, dim0,

@@ -130,13 +130,23 @@ def explicit_voxelize(
     tile_size: int,
     eps3d: float,
     radius_clip: float,
+    z_layers: Optional[tuple] = None,
 ) -> MappingVoxelizationResult:
-    """Run the Gaussian mapping/voxelization forward path explicitly."""
+    """Run the Gaussian mapping/voxelization forward path explicitly.
+
+    ``z_layers`` is an extension of this build (the reference has no such
+    argument; leaving it out gives the reference's behaviour): a brick-layer
+    range ``(begin, end)`` along dim0 voxelizes only that z-slab of the grid,
+    in the grid's own key space -- one rank's share of a multi-GPU split.
+    The volume is then the slab's voxel rows ``[min(end*tile, dim0) -
+    begin*tile, dim1, dim2]`` and the backward takes that slab's gradient.
+    float32 only."""
     if state.voxel is not None:
         raise RuntimeError("An explicit Gaussian state can only be voxelized once.")
     buffers = _voxelize_forward(
         means, state.covars, state.max_scales, state.opacities, ranges, centers, dim2=dim2,
-        dim1=dim1, dim0=dim0, tile_size=tile_size, eps3d=eps3d, radius_clip=radius_clip)
+        dim1=dim1, dim0=dim0, tile_size=tile_size, eps3d=eps3d, radius_clip=radius_clip,
+        z_layers=z_layers)
     output = buffers.output.detach().requires_grad_(True)
     state.voxel = ExplicitVoxelContext(output=output, buffers=buffers)
     return MappingVoxelizationResult(volume=output, means3d=buffers.means3d, radii=buffers.radii)
@@ -235,10 +245,12 @@ def _explicit_backward_fused(state, means, quats, raw_scales, raw_opacities,
         vb = None
         if vox is not None and vox.output.grad is not None:
             vb = vox.buffers
+            nt0 = (vb.dim0 + vb.tile_size - 1) // vb.tile_size
             vox_stats = W.fused_voxel_bwd(
                 vb.vsplats, vb.tile_offsets, vb.flatten_ids, vox.output.grad.contiguous(), N,
                 vb.dim2, vb.dim1, vb.dim0, vb.tile_size, vb.tile_offsets.size(2),
-                vb.tile_offsets.size(1), vb.tile_offsets.size(0), rows=vb.rows)
+                vb.tile_offsets.size(1), nt0, vb.layer_begin,
+                nt0 if vb.layer_end is None else vb.layer_end, rows=vb.rows)
 
         params = (means, quats, raw_scales, raw_opacities)
         accumulate = all(_inplace_grad_ok(p) for p in params)

@@ -128,6 +128,15 @@ R2S_API const char* r2s_version(void);
  * truncated to len-1 bytes); returns the full message length. */
 R2S_API size_t r2s_last_error(char* buf, size_t len);
 
+/* Pipe calibration (measurement support; no counterpart in the reference).
+ * `blocks` CTAs of 256 threads each run 8 independent chains of `iters`
+ * FFMAs (2 FLOP each) or of `iters` FMUL + ex2.approx steps, and write one
+ * float per thread to out [blocks * 256].  Timed with CUDA events they give
+ * the FP32 and MUFU ex2 throughput of this GPU at its current clock, the
+ * denominators of the rasterizer's roofline fractions. */
+R2S_API int r2s_calib_ffma_f32(float* out, int64_t iters, int blocks, r2s_stream_t stream);
+R2S_API int r2s_calib_ex2_f32(float* out, int64_t iters, int blocks, r2s_stream_t stream);
+
 /* ------------------------------------------------------------------------
  * Parameter transform: quats [N,4] (w,x,y,z; normalized in-kernel), raw
  * scales [N,3] -> covars [N,6] upper triangle (00,01,02,11,12,22),

@@ -185,5 +185,20 @@ def load_binary_tree_model(backend: str):
     return mod
 
 
+def load_loss_module():
+    """The reference's training losses (src/utils/loss.py, unchanged:
+    ``BinaryTreeLossComputer``, ``LossComputer``, ``compute_tv_loss``) with
+    ``src.utils.math`` and ``src.utils.metric`` from the same install."""
+    if "loss" in _cache:
+        return _cache["loss"]
+    if "metric" not in _cache:
+        _cache["metric"] = _load_file("ref_src_utils_metric",
+                                      os.path.join(REF_PY, "src", "utils", "metric.py"))
+    with _bound_modules(_src_stubs({"src.utils.metric": _cache["metric"]})):
+        mod = _load_file("ref_src_utils_loss", os.path.join(REF_PY, "src", "utils", "loss.py"))
+    _cache["loss"] = mod
+    return mod
+
+
 __all__ = ["REF_PY", "stock_available", "stock_r2splat", "load_gaussian_model",
-           "load_binary_tree_model"]
+           "load_binary_tree_model", "load_loss_module"]

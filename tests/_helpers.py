@@ -9,14 +9,19 @@ GOLDEN = os.path.join(ROOT, "tests", "golden", "kat.pt")
 # float32 parity bar of the hot path (rel-L2 against the reference build)
 REL_L2_F32 = 1e-5
 
-# Parameter gradients of workloads where one Gaussian sums ~1e4 pixels of a
-# random-sign upstream gradient: two float32 evaluations that differ only in
-# rounding differ by ~1e-5 (the reference's own "pixel" and "primitive"
-# backward modes differ by 5e-6 at config-2 scale, and each is 6-8e-6 from a
-# float64 evaluation of the same float32 forward values).  A gradient that
-# misses REL_L2_F32 against the reference passes only if (a) it is within
-# GRAD_NOISE_F32 of the reference and (b) it is no less accurate than the
-# reference against the float64 evaluation.
+# Parameter gradients at config-2 scale: two float32 evaluations that differ
+# only in rounding differ by ~1e-5.  The difference comes from pixels within
+# rounding of the |alpha| cut-off, which each evaluation decides its own way:
+# the quaternion, scale and opacity gradients of faint Gaussians run through
+# mu and w, where one pixel at the cut-off is a large share of the total.
+# Measured at config 2 (4 views) on the reference build itself: nudging its
+# alpha by 1e-7 (relative) moves its quaternion gradient by 5.5e-6 and its
+# voxel-path quaternion gradient by 5.2e-6 (rel-L2), although every forward
+# input of both builds (covariances, 2D and 3D conics, mu, opacities, means)
+# is bit-identical.  A gradient that misses REL_L2_F32 against the reference
+# passes only if (a) it is within GRAD_NOISE_F32 of the reference and (b) it
+# is no less accurate than the reference against a float64 evaluation of the
+# same float32 forward values.
 GRAD_NOISE_F32 = 2e-5
 
 

@@ -15,6 +15,7 @@ from _helpers import ROOT
 
 WORLD = 2
 VIEWS_PER_RANK = 2
+STRONG_VIEWS = 3  # an odd job: ranks hold 2 and 1 views
 DET = 32
 GRID = 32
 TILE3 = 8
@@ -81,6 +82,10 @@ def _worker(rank, port, out_path):
         first, count, total, stride = shard.view_shard(VIEWS_PER_RANK, rank, WORLD)
         grads = [g.clone() for g in _projection_grads(params, first, count, total, stride)]
         shard.GradientAllReduce()(grads)
+        # strong split: a job of STRONG_VIEWS views dealt over the ranks
+        first, count, total, stride = shard.view_split(STRONG_VIEWS, rank, WORLD)
+        sgrads = [g.clone() for g in _projection_grads(params, first, count, total, stride)]
+        shard.GradientAllReduce()(sgrads)
 
         l0, l1 = shard.layer_range(GRID // TILE3, rank, WORLD)
         slab = _voxel_slab(params, l0, l1)
@@ -94,7 +99,8 @@ def _worker(rank, port, out_path):
         slabs = [torch.zeros((int(n), GRID, GRID), dtype=torch.float64) for n in sizes]
         dist.all_gather(slabs, slab.detach().contiguous())
         if rank == 0:
-            torch.save({"grads": grads, "vgrads": vgrads, "volume": torch.cat(slabs)}, out_path)
+            torch.save({"grads": grads, "sgrads": sgrads, "vgrads": vgrads,
+                        "volume": torch.cat(slabs)}, out_path)
     finally:
         dist.destroy_process_group()
 
@@ -152,6 +158,31 @@ def test_view_shards_cover_the_orbit():
         assert total == 300 and count == 75 and stride == 4
         seen.extend(range(first, first + stride * count, stride))
     assert sorted(seen) == list(range(300))
+
+
+def test_view_splits_partition_the_job():
+    _setup_paths()
+    import r2s_shard as shard
+
+    for n_views, world in ((75, 1), (75, 2), (75, 8), (3, 2), (5, 8)):
+        seen, counts = [], []
+        for r in range(world):
+            first, count, total, stride = shard.view_split(n_views, r, world)
+            assert total == n_views and stride == world
+            seen.extend(range(first, first + stride * count, stride))
+            counts.append(count)
+        assert sorted(seen) == list(range(n_views))
+        assert max(counts) - min(counts) <= 1
+    with pytest.raises(ValueError):
+        shard.view_split(75, 8, 8)
+
+
+def test_strong_split_gradient_allreduce_equals_single_process(sharded):
+    _setup_paths()
+    params = _params()
+    full = _projection_grads(params, 0, STRONG_VIEWS, STRONG_VIEWS)
+    for a, b in zip(sharded["sgrads"], full):
+        torch.testing.assert_close(a, b, rtol=1e-10, atol=1e-12)
 
 
 def test_projection_gradient_allreduce_equals_single_process(sharded):
