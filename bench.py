@@ -488,6 +488,42 @@ TRAIN_TV = 64            # edge of the random TV sub-volume (voxels)
 TRAIN_GRID = 256         # full-grid resolution that fixes the sub-volume's voxel size
 TRAIN_WEIGHTS = dict(w_l1=0.8, w_ssim=0.2, w_tv=0.05, w_edge=0.1)
 TRAIN_LRS = {"means": 1.6e-4, "quats": 1e-3, "scales": 5e-3, "opacities": 5e-2}
+TRAIN_KEYS = ["means", "scales", "quats", "opacities"]
+TRAIN_SPLIT_EVERY = 100   # binary split of a seeded subset every 100 steps
+TRAIN_SPLIT_FRAC = 0.05
+TRAIN_SCALE_EPS = 1e-5    # configs/model/binary_tree.yaml:8
+
+
+def split_mask(step, n, dev):
+    """The seeded 5 % subset split at `step` (the same on every rank)."""
+    g = torch.Generator(device=dev).manual_seed(5000 + step)
+    return torch.rand(n, generator=g, device=dev) < TRAIN_SPLIT_FRAC
+
+
+def first_train_step(steps, warmup):
+    """Number of the first (warm-up) step, chosen so that the split at step
+    TRAIN_SPLIT_EVERY falls inside the timed window."""
+    return max(1, TRAIN_SPLIT_EVERY - warmup - steps // 2)
+
+
+class TreeParams:
+    """The four raw parameters and the binary-tree buffers of a model (the
+    attributes the split reads and replaces)."""
+
+    def __init__(self, m, q, s, o, dev):
+        self.means = torch.nn.Parameter(m.to(dev))
+        self.quats = torch.nn.Parameter(q.to(dev))
+        self.scales = torch.nn.Parameter(s.to(dev))
+        self.opacities = torch.nn.Parameter(o.to(dev))
+        n = m.shape[0]
+        self.parent = torch.full((n,), -1, dtype=torch.int32, device=dev)
+        self.level = torch.zeros((n,), dtype=torch.int32, device=dev)
+        self.history_means = torch.empty((0, 3), device=dev)
+        self.history_scales = torch.empty((0, 3), device=dev)
+        self.history_quats = torch.empty((0, 4), device=dev)
+        self.history_opacities = torch.empty((0,), device=dev)
+        self.history_parent = torch.empty((0,), dtype=torch.int32, device=dev)
+        self.history_level = torch.empty((0,), dtype=torch.int32, device=dev)
 
 
 class TrainData:
@@ -545,21 +581,23 @@ class OursTrain:
                                             absgrad=False).image.detach().clone()
 
         self.data = TrainData(cfg, dev, render)
-        m, q, s, o = wl.make_gaussians(cfg)
-        self.params = {k: torch.nn.Parameter(t.to(dev)) for k, t in
-                       zip(("means", "quats", "scales", "opacities"), (m, q, s, o))}
-        self.opts = {k: torch.optim.Adam([{"params": p, "name": k}], lr=TRAIN_LRS[k], eps=1e-15)
-                     for k, p in self.params.items()}
+        self.model = TreeParams(*wl.make_gaussians(cfg), dev)
+        self.opts = {k: torch.optim.Adam([{"params": getattr(self.model, k), "name": k}],
+                                         lr=TRAIN_LRS[k], eps=1e-15) for k in TRAIN_KEYS}
         self.loss = T.FusedBinaryTreeLossComputer(**TRAIN_WEIGHTS)
         self.densify = {"grad2d": None, "count": None}
         self.allreduce = shard.GradientAllReduce()
         self.step_no = 0
+        self.sizes = []  # Gaussians rendered per step
 
     def step(self):
-        E, T, d, P = self.E, self.T, self.data, self.params
+        E, T, d, M = self.E, self.T, self.data, self.model
+        P = {k: getattr(M, k) for k in TRAIN_KEYS}
         views = d.step_views(self.step_no, self.rank, self.world).to(self.dev)
         rng, ctr = d.step_box(self.step_no, self.dev)
+        step_no = self.step_no
         self.step_no += 1
+        self.sizes.append(P["means"].shape[0])
         st = E.prepare_explicit_gaussians(P["quats"], P["scales"], P["opacities"],
                                           scale_min=wl.SCALE_MIN, scale_max=wl.SCALE_MAX)
         res = E.explicit_rasterize(st, P["means"], d.vm[views], d.K[views], img_w=d.det,
@@ -585,6 +623,14 @@ class OursTrain:
                                                          n_cameras=TRAIN_VIEWS_PER_STEP))
         if self.world > 1:
             self.allreduce([p.grad for p in P.values()])
+        if step_no % TRAIN_SPLIT_EVERY == 0:
+            # the strategy's split after the backward, before the optimizer
+            # step (src/trainers/binary_tree.py:193-206): the new parameters
+            # have no gradient, so that Adam step skips them, as torch's does
+            T.binary_split(M, self.opts, self.densify, split_mask(step_no, P["means"].shape[0],
+                                                                  self.dev),
+                           TRAIN_KEYS, revised_opacity=True, scale_min=wl.SCALE_MIN,
+                           scale_max=wl.SCALE_MAX, scale_eps=TRAIN_SCALE_EPS)
         T.adam_step(self.opts)
         for o in self.opts.values():
             o.zero_grad(set_to_none=True)
@@ -595,7 +641,9 @@ class RefTrain:
     """The same step through the reference's own code: its op layer
     (unchanged, baseline/_ref) over its CUDA build (oracle/_ref), its
     BinaryTreeLossComputer (src/utils/loss.py, unchanged) with autograd, the
-    strategy's _update_state (restated in the oracle) and torch.optim.Adam."""
+    strategy's _update_state (restated in the oracle), its split()
+    (src/strategies/binary_tree.py, unchanged) on its BinaryTreeGaussianModel,
+    and torch.optim.Adam."""
 
     def __init__(self, cfg, dev):
         from oracle import r2s_oracle as O
@@ -616,19 +664,32 @@ class RefTrain:
                                         absgrad=False).image.detach().clone()
 
         self.data = TrainData(cfg, dev, render)
-        m, q, s, o = wl.make_gaussians(cfg)
-        self.params = {k: torch.nn.Parameter(t.to(dev)) for k, t in
-                       zip(("means", "quats", "scales", "opacities"), (m, q, s, o))}
-        self.opts = {k: torch.optim.Adam([{"params": p, "name": k}], lr=TRAIN_LRS[k], eps=1e-15)
-                     for k, p in self.params.items()}
+        # the reference's BinaryTreeGaussianModel holds the parameters and the
+        # tree, its strategy module's split() splits them
+        btm = ref_stock.load_binary_tree_model("stock")
+        self.split = ref_stock.load_strategy_module("stock").split
+        self.model = btm.BinaryTreeGaussianModel(device=str(dev), min_scale=wl.SCALE_MIN,
+                                                 max_scale=wl.SCALE_MAX,
+                                                 scale_eps=TRAIN_SCALE_EPS)
+        tree = TreeParams(*wl.make_gaussians(cfg), dev)
+        for name in ("means", "quats", "scales", "opacities", "parent", "level", "history_means",
+                     "history_scales", "history_quats", "history_opacities", "history_parent",
+                     "history_level"):
+            setattr(self.model, name, getattr(tree, name))
+        self.model.trainable_param_keys = list(TRAIN_KEYS)
+        self.opts = self.model.build_optimizers(TRAIN_LRS)
         self.densify = {"grad2d": None, "count": None}
         self.step_no = 0
+        self.sizes = []
 
     def step(self):
-        d, P, S, O = self.data, self.params, self.S, self.O
+        d, S, O, M = self.data, self.S, self.O, self.model
+        P = {k: getattr(M, k) for k in TRAIN_KEYS}
         views = d.step_views(self.step_no, 0, 1).to(self.dev)
         rng, ctr = d.step_box(self.step_no, self.dev)
+        step_no = self.step_no
         self.step_no += 1
+        self.sizes.append(P["means"].shape[0])
         st = S.prepare_explicit_gaussians(P["quats"], P["scales"], P["opacities"],
                                           scale_min=wl.SCALE_MIN, scale_max=wl.SCALE_MAX)
         res = S.explicit_rasterize(st, P["means"], d.vm[views], d.K[views], img_w=d.det,
@@ -643,6 +704,10 @@ class RefTrain:
         S.explicit_backward(st, P["means"], P["quats"], P["scales"], P["opacities"])
         O.densify_state_update(self.densify, res.means2d.absgrad, res.radii.amax(dim=-1), d.det,
                                d.det, len(views))
+        if step_no % TRAIN_SPLIT_EVERY == 0:
+            self.split(M, self.opts, self.densify, split_mask(step_no, P["means"].shape[0],
+                                                             self.dev),
+                       list(TRAIN_KEYS), revised_opacity=True)
         for opt in self.opts.values():
             opt.step()
             opt.zero_grad(set_to_none=True)
@@ -667,11 +732,15 @@ def run_train_bench(args, cfg, dev, world, rank, local, flush):
             return
     else:
         trainer = OursTrain(cfg, world, rank, dev)
+    trainer.step_no = first_train_step(args.steps, args.warmup)
     with ClockSampler(local) as clk:
         ms = time_steps(trainer.step, args.steps, args.warmup, 1 if ref else world, flush)
     if rank != 0:
         return
-    value = cfg.n_gaussians * TRAIN_VIEWS_PER_STEP / (ms * 1e-3)
+    timed_sizes = trainer.sizes[-args.steps:]
+    timed_first = trainer.step_no - args.steps
+    splits = [k for k in range(timed_first, trainer.step_no) if k % TRAIN_SPLIT_EVERY == 0]
+    value = sum(timed_sizes) * TRAIN_VIEWS_PER_STEP / (args.steps * ms * 1e-3)
     line = {
         "metric": "Gaussian*views/s training step (config 4)",
         "value": round(value, 1), "unit": "Gaussian*views/s", "n_gpus": 1 if ref else world,
@@ -682,8 +751,12 @@ def run_train_bench(args, cfg, dev, world, rank, local, flush):
                    "views_per_step": TRAIN_VIEWS_PER_STEP, "detector": cfg.detector,
                    "tv_subvolume": TRAIN_TV, "loss": TRAIN_WEIGHTS,
                    "step": "prepare + rasterize + 64^3 voxelize + L1/SSIM/edge/TV losses + "
-                           "backward with densify stats + grad all-reduce + Adam",
-                   "split": "binary split every 100 steps lies outside the timed window",
+                           "backward with densify stats + grad all-reduce + binary split "
+                           "every 100 steps + Adam",
+                   "split": f"{TRAIN_SPLIT_FRAC:.0%} seeded subset every {TRAIN_SPLIT_EVERY} "
+                            f"steps (longest axis, revised opacity); timed steps "
+                            f"{timed_first}-{trainer.step_no - 1} include split(s) at {splits}",
+                   "gaussians_per_timed_step": timed_sizes,
                    "l2": "256MiB flush between steps"},
         "clocks": clk.summary(),
     }

@@ -19,6 +19,10 @@ interchangeable.
   losses (``BinaryTreeLossComputer``, src/utils/loss.py:125-172;
   ``LossComputer``, loss.py:72-109): L1, SSIM and edge terms of the
   projections in one kernel each way, volume TV in one.
+* ``binary_split(model, optimizers, state, mask, trainable_param_keys,
+  revised_opacity)`` -- the binary-tree strategy's split
+  (``split``, src/strategies/binary_tree.py:92-149) with the children's
+  parameters computed in one launch (``r2s_split_children_f32``).
 """
 from __future__ import annotations
 
@@ -32,7 +36,7 @@ from ..cuda import _wrapper as W
 from ..cuda._backend import AdamGroup
 
 __all__ = ["DensifyAccumulator", "FusedBinaryTreeLossComputer", "FusedLossComputer", "adam_step",
-           "projection_losses", "tv_loss", "update_densify_state"]
+           "binary_split", "projection_losses", "tv_loss", "update_densify_state"]
 
 _MAX_GROUPS = 8
 
@@ -377,3 +381,110 @@ class FusedLossComputer:
         out["vol_tv"] = tv
         out["total"] = self.w_l1 * l1 + self.w_ssim * out["proj_ssim"] + self.w_tv * tv
         return out
+
+
+# ---------------------------------------------------------------------------
+# binary-tree split (src/strategies/binary_tree.py:17-149)
+# ---------------------------------------------------------------------------
+_TREE_HISTORY = (("history_means", "means"), ("history_scales", "scales"),
+                 ("history_quats", "quats"), ("history_opacities", "opacities"),
+                 ("history_parent", "parent"), ("history_level", "level"))
+
+
+def _scale_bounds(model, scale_min, scale_max, scale_eps):
+    lo = getattr(model, "_scale_min", None) if scale_min is None else scale_min
+    hi = getattr(model, "_scale_max", None) if scale_max is None else scale_max
+    eps = getattr(model, "_scale_eps", None) if scale_eps is None else scale_eps
+    if lo is None or hi is None or eps is None:
+        raise ValueError("binary_split needs sigmoid scale bounds (scale_min, scale_max, scale_eps)")
+    lo, hi = torch.as_tensor(lo), torch.as_tensor(hi)
+    if lo.numel() != 1 or hi.numel() != 1:
+        raise ValueError("binary_split supports scalar scale bounds only")
+    return float(lo.reshape(())), float(hi.reshape(())), float(eps)
+
+
+@torch.no_grad()
+def binary_split(model, optimizers: Dict[str, torch.optim.Optimizer], state: dict,
+                 mask: torch.Tensor, trainable_param_keys: List[str],
+                 revised_opacity: bool = False, *, scale_min: Optional[float] = None,
+                 scale_max: Optional[float] = None, scale_eps: Optional[float] = None) -> None:
+    """Split every Gaussian of ``mask`` into two children along its longest
+    axis, in place, with the effects of the reference's ``split``
+    (src/strategies/binary_tree.py:92-149) on the same objects:
+
+    * ``model`` (anything with the raw parameters ``means``, ``scales``,
+      ``quats``, ``opacities`` and the binary-tree buffers ``parent``,
+      ``level``, ``history_*`` as attributes, e.g. the reference's
+      ``BinaryTreeGaussianModel``): the selected nodes are archived at the end
+      of the history (``_append_history``, :17-56), the parameters become
+      [unselected rows; the S children at mean + offset; the S children at
+      mean - offset], the children's parent is the archived node and their
+      level its level + 1;
+    * ``optimizers``: every moment buffer of a parameter keeps its rows of the
+      unselected Gaussians and gets zeros for the children; the state moves
+      to the new parameter (``_update_param_with_optimizer``,
+      src/utils/ops.py:62-102);
+    * ``state``: every tensor becomes [unselected rows; selected rows twice].
+
+    The children's values come from one kernel (``r2s_split_children_f32``,
+    float32, scalar sigmoid scale bounds taken from the model's
+    ``_scale_min`` / ``_scale_max`` / ``_scale_eps`` unless given)."""
+    lo, hi, eps = _scale_bounds(model, scale_min, scale_max, scale_eps)
+    means = model.means
+    dev = means.device
+    sel = torch.where(mask)[0]
+    rest = torch.where(~mask)[0]
+    S = int(sel.numel())
+    raw = {name: getattr(model, name) for name in ("means", "scales", "quats", "opacities")}
+    for name, t in raw.items():
+        if t.dtype != torch.float32 or not t.is_cuda:
+            raise RuntimeError(f"binary_split: {name} must be a float32 CUDA tensor")
+    children = {"means": torch.empty((2 * S, 3), dtype=torch.float32, device=dev),
+                "scales": torch.empty((2 * S, 3), dtype=torch.float32, device=dev),
+                "quats": torch.empty((2 * S, 4), dtype=torch.float32, device=dev),
+                "opacities": torch.empty((2 * S,), dtype=torch.float32, device=dev)}
+    sel64 = sel.to(torch.int64).contiguous()
+    with torch.cuda.device(dev):
+        W._call("r2s_split_children_f32", W._ptr(raw["means"].detach().contiguous()),
+                W._ptr(raw["scales"].detach().contiguous()),
+                W._ptr(raw["quats"].detach().contiguous()),
+                W._ptr(raw["opacities"].detach().contiguous()), W._ptr(sel64), S, lo, hi, eps,
+                1 if revised_opacity else 0, W._ptr(children["means"]),
+                W._ptr(children["scales"]), W._ptr(children["quats"]),
+                W._ptr(children["opacities"]), W._stream(dev))
+
+    # archive the selected nodes (their current values) at the end of the history
+    start = model.history_parent.shape[0]
+    hist_idx = torch.arange(start, start + S, device=dev, dtype=torch.int32)
+    if S:
+        for hist, cur in _TREE_HISTORY:
+            setattr(model, hist, torch.cat([getattr(model, hist),
+                                            getattr(model, cur).index_select(0, sel).detach().clone()],
+                                           dim=0))
+    split_level = model.level.index_select(0, sel) + 1
+    model.parent = torch.cat([model.parent.index_select(0, rest), hist_idx.repeat(2)], dim=0)
+    model.level = torch.cat([model.level.index_select(0, rest), split_level.repeat(2)], dim=0)
+
+    for name in trainable_param_keys:
+        old = getattr(model, name)
+        child = children.get(name)
+        if child is None:
+            child = old[sel].repeat([2] + [1] * (old.dim() - 1))
+        new = torch.nn.Parameter(torch.cat([old[rest], child.to(old.dtype)]),
+                                 requires_grad=old.requires_grad)
+        setattr(model, name, new)
+        if name not in optimizers:
+            continue
+        opt = optimizers[name]
+        for group in opt.param_groups:
+            pstate = opt.state.pop(old, {})
+            for key in list(pstate.keys()):
+                if key != "step":
+                    v = pstate[key]
+                    pstate[key] = torch.cat([v[rest], torch.zeros((2 * S, *v.shape[1:]),
+                                                                  device=dev, dtype=v.dtype)])
+            group["params"] = [new]
+            opt.state[new] = pstate
+    for k, v in state.items():
+        if isinstance(v, torch.Tensor):
+            state[k] = torch.cat((v[rest], v[sel].repeat([2] + [1] * (v.dim() - 1))))

@@ -76,6 +76,24 @@ typedef struct r2s_adam_group {
 R2S_API int r2s_adam_step_f32(const r2s_adam_group* groups, int n_groups, double beta1,
                               double beta2, double eps, r2s_stream_t stream);
 
+/* Children of a binary-tree split (replaces the tensor arithmetic of split(),
+ * src/strategies/binary_tree.py:92-149, for scalar sigmoid scale bounds).
+ * For each of the S Gaussians whose indices are in sel [S] (int64): the
+ * longest activated-scale axis k, offset R[:, k] s_k of its normalized
+ * quaternion's rotation; child_means [2S,3] = mean + offset (rows 0..S-1) and
+ * mean - offset (rows S..2S-1); child_scales [2S,3] = the raw scales of the
+ * activated scales with s_k / 1.6 (inverse bounded sigmoid with scale_eps);
+ * child_quats [2S,4] = the raw quaternion; child_opacities [2S] = the raw
+ * opacity, or with revised_opacity != 0 softplus^-1(1 - sqrt(1 - min(
+ * softplus(raw), 0.9999))).  Float operations round one by one, as the
+ * reference's elementwise torch ops. */
+R2S_API int r2s_split_children_f32(const float* means, const float* raw_scales,
+                                   const float* quats, const float* raw_opacities,
+                                   const int64_t* sel, int64_t S, double scale_min,
+                                   double scale_max, double scale_eps, int revised_opacity,
+                                   float* child_means, float* child_scales, float* child_quats,
+                                   float* child_opacities, r2s_stream_t stream);
+
 /* Densification statistics of one training step: for every (view, Gaussian)
  * with radius > 0, grad2d[g] += |(gx * scale_x, gy * scale_y)|, count[g] += 1,
  * and, when max_radii is not NULL, max_radii[g] = max(max_radii[g],

@@ -200,5 +200,36 @@ def load_loss_module():
     return mod
 
 
+def load_strategy_module(backend: str = "stock"):
+    """The reference's binary-tree strategy module
+    (src/strategies/binary_tree.py, unchanged: ``split``, ``duplicate``,
+    ``remove``, ``_append_history``, ``BinaryTreeStrategy``) with its imports
+    (src/strategies/base.py, src/utils/ops.py, src/utils/math.py and the
+    ``GaussianModel`` of ``load_gaussian_model(backend)``) from the same
+    install."""
+    key = "strategy_" + backend
+    if key in _cache:
+        return _cache[key]
+    gm = load_gaussian_model(backend)
+    models = types.ModuleType("src.models")
+    models.__path__ = []
+    strategies = types.ModuleType("src.strategies")
+    strategies.__path__ = []
+    binds = _src_stubs({"src.models": models, "src.models.gaussian_model": gm,
+                        "src.strategies": strategies})
+    with _bound_modules(binds):
+        ops = _load_file("src.utils.ops", os.path.join(REF_PY, "src", "utils", "ops.py"))
+        base = _load_file("src.strategies.base",
+                          os.path.join(REF_PY, "src", "strategies", "base.py"))
+        with _bound_modules({"src.utils.ops": ops, "src.strategies.base": base}):
+            mod = _load_file("src.strategies.binary_tree",
+                             os.path.join(REF_PY, "src", "strategies", "binary_tree.py"))
+    # the modules stay reachable from the returned module's globals only
+    for name in ("src.utils.ops", "src.strategies.base", "src.strategies.binary_tree"):
+        sys.modules.pop(name, None)
+    _cache[key] = mod
+    return mod
+
+
 __all__ = ["REF_PY", "stock_available", "stock_r2splat", "load_gaussian_model",
-           "load_binary_tree_model", "load_loss_module"]
+           "load_binary_tree_model", "load_loss_module", "load_strategy_module"]
