@@ -500,6 +500,27 @@ def split_mask(step, n, dev):
     return torch.rand(n, generator=g, device=dev) < TRAIN_SPLIT_FRAC
 
 
+def warm_split_path(split_fn, model_cls_or_none, dev):
+    """Run one split of a small throwaway model so that the kernels the
+    split uses (the library's and torch's, loaded lazily on first launch) are
+    loaded before the timed window, as they are in a long training run."""
+    tree = TreeParams(*wl.make_gaussians(wl.CONFIGS[0], n=1000), dev)
+    if model_cls_or_none is not None:
+        m = model_cls_or_none(device=str(dev), min_scale=wl.SCALE_MIN, max_scale=wl.SCALE_MAX,
+                              scale_eps=TRAIN_SCALE_EPS)
+        for name in vars(tree):
+            setattr(m, name, getattr(tree, name))
+        tree = m
+    opts = {k: torch.optim.Adam([{"params": getattr(tree, k), "name": k}], lr=1e-3, eps=1e-15)
+            for k in TRAIN_KEYS}
+    for k in TRAIN_KEYS:
+        getattr(tree, k).grad = torch.zeros_like(getattr(tree, k))
+        opts[k].step()
+    state = {"grad2d": torch.zeros(1000, device=dev), "count": torch.zeros(1000, device=dev)}
+    split_fn(tree, opts, state, split_mask(0, 1000, dev))
+    torch.cuda.synchronize()
+
+
 def first_train_step(steps, warmup):
     """Number of the first (warm-up) step, chosen so that the split at step
     TRAIN_SPLIT_EVERY falls inside the timed window."""
@@ -589,6 +610,9 @@ class OursTrain:
         self.allreduce = shard.GradientAllReduce()
         self.step_no = 0
         self.sizes = []  # Gaussians rendered per step
+        warm_split_path(lambda m, o, st, mask: T.binary_split(
+            m, o, st, mask, TRAIN_KEYS, revised_opacity=True, scale_min=wl.SCALE_MIN,
+            scale_max=wl.SCALE_MAX, scale_eps=TRAIN_SCALE_EPS), None, dev)
 
     def step(self):
         E, T, d, M = self.E, self.T, self.data, self.model
@@ -681,6 +705,9 @@ class RefTrain:
         self.densify = {"grad2d": None, "count": None}
         self.step_no = 0
         self.sizes = []
+        warm_split_path(lambda m, o, st, mask: self.split(m, o, st, mask, list(TRAIN_KEYS),
+                                                          revised_opacity=True),
+                        btm.BinaryTreeGaussianModel, dev)
 
     def step(self):
         d, S, O, M = self.data, self.S, self.O, self.model

@@ -352,9 +352,15 @@ def test_fused_voxel_gradients_alone_match_reference(ref, case):
 def test_explicit_voxelize_z_slab_matches_full_grid_and_reference(ref, case):
     """explicit_voxelize(..., z_layers=(l0, l1)) -- this build's extension for
     a rank's z-slab -- voxelizes exactly the rows of those brick layers of the
-    full grid (bit-identical: same records, same order per brick), and the
-    backward of a slab gradient equals the reference's backward of that
-    gradient placed in a zero volume."""
+    full grid (bit-identical: same records, same order per brick), and its
+    backward of a slab gradient equals the backward of the full grid with
+    that gradient placed in a zero volume (the same per-brick moments; only
+    the order of the per-Gaussian float additions differs, so the float bar
+    applies).  The full-grid
+    backward is compared with the reference at the plain bar here for configs
+    0 and 1 and by test_fused_voxel_gradients_alone_match_reference at config
+    2, where the slab's smaller gradient is dominated by cut-off decisions
+    (see tests/_helpers.py)."""
     name, d = case
     import r2s_shard as shard
     import r2s_workloads as wl
@@ -364,42 +370,40 @@ def test_explicit_voxelize_z_slab_matches_full_grid_and_reference(ref, case):
     nt = G // wl.VOL_TILE
     l0, l1 = nt // 4, nt // 4 + max(1, nt // 3)
     z0, z1 = shard.slab_rows(l0, l1, wl.VOL_TILE, G)
-    vols = []
-    for layers in (None, (l0, l1)):
+    g = torch.Generator(device="cuda").manual_seed(13)
+    v_slab = torch.randn((z1 - z0, G, G), generator=g, device="cuda")
+    v_full = torch.zeros((G, G, G), device="cuda")
+    v_full[z0:z1] = v_slab
+    vols, grads = [], []
+    for layers, v_vol in ((None, v_full), ((l0, l1), v_slab)):
         params = {k: d[k].clone().requires_grad_(True) for k in ("means", "quats", "scales", "opac")}
         st = E.prepare_explicit_gaussians(params["quats"], params["scales"], params["opac"],
                                           scale_min=wl.SCALE_MIN, scale_max=wl.SCALE_MAX)
-        E.explicit_rasterize(st, params["means"], d["viewmats"][:1], d["Ks"][:1], img_w=16,
+        E.explicit_rasterize(st, params["means"], d["viewmats"][:0], d["Ks"][:0], img_w=16,
                              img_h=16, tile_size=wl.IMG_TILE, eps2d=wl.EPS2D,
                              radius_clip=wl.RADIUS_CLIP, absgrad=False)
         vr = E.explicit_voxelize(st, params["means"], d["ranges"], d["centers"], dim2=G, dim1=G,
                                  dim0=G, tile_size=wl.VOL_TILE, eps3d=wl.EPS3D,
                                  radius_clip=wl.RADIUS_CLIP, z_layers=layers)
         vols.append(vr.volume.detach())
-        if layers is not None:
-            g = torch.Generator(device="cuda").manual_seed(13)
-            v_slab = torch.randn(vr.volume.shape, generator=g, device="cuda")
-            vr.volume.grad = v_slab
-            E.explicit_backward(st, params["means"], params["quats"], params["scales"],
-                                params["opac"])
+        vr.volume.grad = v_vol
+        E.explicit_backward(st, params["means"], params["quats"], params["scales"], params["opac"])
+        grads.append({k: params[k].grad for k in params})
     assert vols[1].shape == (z1 - z0, G, G)
     assert torch.equal(vols[1], vols[0][z0:z1]), f"{name}: slab rows differ from the full grid"
-    covars, max_s, opac = ref.prepare(d["quats"], d["scales"], d["opac"], wl.SCALE_MIN,
-                                      wl.SCALE_MAX)
-    v = ref.voxelize_forward(d["means"], covars, max_s, opac, d["ranges"], d["centers"], G, G, G,
-                             wl.VOL_TILE, wl.EPS3D, wl.RADIUS_CLIP)
-    v_full = torch.zeros_like(v["output"])
-    v_full[z0:z1] = v_slab
-    theirs = ref.explicit_backward(None, None, v, v_full, d["means"], d["quats"], d["scales"],
-                                   d["opac"], covars, opac, wl.SCALE_MIN, wl.SCALE_MAX)
-    pairs = (("means", "means"), ("quats", "quats"), ("scales", "scales"), ("opac", "opacities"))
-    if name in NOISE_LIMITED:
-        truth = _float64_gradients(ref, d, None, None, v, v_full, covars)
-        check_grad_accuracy(name + "-slab", {k: params[k].grad for k, _ in pairs},
-                            {k: theirs[pk] for k, pk in pairs}, truth)
-    else:
-        for key, pk in pairs:
-            e = rel_l2(params[key].grad, theirs[pk])
+    for key in grads[0]:
+        e = rel_l2(grads[1][key], grads[0][key])
+        assert e < REL_L2_F32, f"{name}: slab grad {key} vs full-grid grad rel-L2 {e:.3e}"
+    if name not in NOISE_LIMITED:
+        covars, max_s, opac = ref.prepare(d["quats"], d["scales"], d["opac"], wl.SCALE_MIN,
+                                          wl.SCALE_MAX)
+        v = ref.voxelize_forward(d["means"], covars, max_s, opac, d["ranges"], d["centers"], G, G,
+                                 G, wl.VOL_TILE, wl.EPS3D, wl.RADIUS_CLIP)
+        theirs = ref.explicit_backward(None, None, v, v_full, d["means"], d["quats"], d["scales"],
+                                       d["opac"], covars, opac, wl.SCALE_MIN, wl.SCALE_MAX)
+        for key, pk in (("means", "means"), ("quats", "quats"), ("scales", "scales"),
+                        ("opac", "opacities")):
+            e = rel_l2(grads[1][key], theirs[pk])
             assert e < REL_L2_F32, f"{name}: slab grad {key} rel-L2 {e:.3e}"
     with pytest.raises(ValueError):
         st = E.prepare_explicit_gaussians(d["quats"], d["scales"], d["opac"],
