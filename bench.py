@@ -390,10 +390,15 @@ class OursVoxel(HostPipeline):
 
 
 class PhaseTimer:
-    """CUDA events between consecutive phases on the current stream."""
+    """CUDA events between consecutive phases on the current stream (ranks
+    start together: a barrier first, so no phase absorbs another rank's
+    lateness)."""
 
     def __init__(self):
         torch.cuda.synchronize()
+        if torch.distributed.is_available() and torch.distributed.is_initialized():
+            torch.distributed.barrier()
+            torch.cuda.synchronize()
         self.events = [("start", self._ev())]
 
     @staticmethod
