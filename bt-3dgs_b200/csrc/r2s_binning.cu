@@ -27,6 +27,7 @@
 // contains the layer, rects [N]).
 #include "r2s_common.cuh"
 #include "r2s_tiles.cuh"
+#include "r2s_debug.cuh"
 
 namespace r2s {
 
@@ -178,7 +179,7 @@ __global__ void bin_place_kernel(const void* __restrict__ rects, int64_t S, int6
                                  uint32_t tiles_x, int64_t seg_base, int64_t chunk,
                                  int64_t n_chunks, const int32_t* __restrict__ hist,
                                  const int32_t* __restrict__ offsets,
-                                 int32_t* __restrict__ flatten_ids) {
+                                 int32_t* __restrict__ flatten_ids, int64_t n_isects) {
     extern __shared__ int32_t smem[];
     const int warps = blockDim.x >> 5;
     const int warp = threadIdx.x >> 5;
@@ -219,7 +220,7 @@ __global__ void bin_place_kernel(const void* __restrict__ rects, int64_t S, int6
             for (int q = lane; q < n; q += 32) {
                 const int tile = (y0 + dy) * (int)tiles_x + x0 + dx;
                 const int pos = cnt[tile];
-                flatten_ids[pos] = id;
+                if (!R2S_DBG_BAD(pos >= 0 && pos < n_isects, R2S_DBG_SLOT)) flatten_ids[pos] = id;
                 cnt[tile] = pos + 1;
                 dy += sdy;
                 dx += sdx;
@@ -348,7 +349,7 @@ __global__ void __launch_bounds__(kStagedWarps * 32)
 bin_place_staged_kernel(const void* __restrict__ rects, int64_t N, int T, uint32_t tiles_x,
                         int64_t seg_base, int64_t chunk, int64_t n_chunks,
                         const int32_t* __restrict__ hist, const int32_t* __restrict__ offsets,
-                        int32_t* __restrict__ flatten_ids, int cap) {
+                        int32_t* __restrict__ flatten_ids, int cap, int64_t n_isects) {
     extern __shared__ __align__(16) int32_t smem[];
     __shared__ int32_t s_scan[33];
     const int tid = threadIdx.x, nthr = blockDim.x, warp = tid >> 5, lane = tid & 31;
@@ -400,13 +401,17 @@ bin_place_staged_kernel(const void* __restrict__ rects, int64_t N, int T, uint32
             const int n = tot[t];
             const uint16_t* src = stage + lofs[t];
             int32_t* dst = flatten_ids + gpos[t];
-            for (int j = lane; j < n; j += 32) dst[j] = (int32_t)(id0 + src[j]);
+            for (int j = lane; j < n; j += 32)
+                if (!R2S_DBG_BAD(gpos[t] >= 0 && (int64_t)gpos[t] + j < n_isects, R2S_DBG_SLOT))
+                    dst[j] = (int32_t)(id0 + src[j]);
         }
     } else {
         walk_items<LAYERED>(rects, s, N, layer, w0, w1, i0, tiles_x, [&](int tile, int local) {
             const int p = mine[tile];
             mine[tile] = (uint16_t)(p + 1);
-            flatten_ids[gpos[tile] + p] = (int32_t)(id0 + local);
+            if (!R2S_DBG_BAD(gpos[tile] + p >= 0 && (int64_t)gpos[tile] + p < n_isects,
+                             R2S_DBG_SLOT))
+                flatten_ids[gpos[tile] + p] = (int32_t)(id0 + local);
         });
     }
 }
@@ -556,13 +561,13 @@ int bin_place_impl(const void* rects, int64_t S, int64_t N, int64_t T, uint32_t 
                 return rc;
             bin_place_staged_kernel<true><<<blocks, kStagedWarps * 32, smem, stream>>>(
                 rects, N, (int)T, tiles_x, seg_base, p.chunk, p.n_chunks, w.hist, offsets,
-                flatten_ids, (int)cap);
+                flatten_ids, (int)cap, n_isects);
         } else {
             if (int rc = set_dynamic_smem(bin_place_staged_kernel<false>, smem, "bin_place"))
                 return rc;
             bin_place_staged_kernel<false><<<blocks, kStagedWarps * 32, smem, stream>>>(
                 rects, N, (int)T, tiles_x, seg_base, p.chunk, p.n_chunks, w.hist, offsets,
-                flatten_ids, (int)cap);
+                flatten_ids, (int)cap, n_isects);
         }
         if (isect_ids != nullptr) {
             const int64_t n_keys = S * T;
@@ -581,12 +586,12 @@ int bin_place_impl(const void* rects, int64_t S, int64_t N, int64_t T, uint32_t 
         if (int rc = set_dynamic_smem(bin_place_kernel<true>, smem, "bin_place")) return rc;
         bin_place_kernel<true><<<blocks, warps * 32, smem, stream>>>(
             rects, S, N, (int)T, tiles_x, seg_base, p.chunk, p.n_chunks, w.hist, offsets,
-            flatten_ids);
+            flatten_ids, n_isects);
     } else {
         if (int rc = set_dynamic_smem(bin_place_kernel<false>, smem, "bin_place")) return rc;
         bin_place_kernel<false><<<blocks, warps * 32, smem, stream>>>(
             rects, S, N, (int)T, tiles_x, seg_base, p.chunk, p.n_chunks, w.hist, offsets,
-            flatten_ids);
+            flatten_ids, n_isects);
     }
     if (isect_ids != nullptr) {
         const int64_t n_keys = S * T;
@@ -674,3 +679,7 @@ extern "C" int r2s_isect_offset_encode(const int64_t* isect_ids, int64_t n_isect
                                                                     offsets);
     return check_launch("isect_offset_encode");
 }
+
+namespace r2s {
+R2S_DBG_DEFINE_READER(debug_flags_binning)
+}  // namespace r2s

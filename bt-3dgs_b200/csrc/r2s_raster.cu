@@ -39,6 +39,7 @@
 
 #include "r2s_common.cuh"
 #include "r2s_cull.cuh"
+#include "r2s_debug.cuh"
 
 namespace r2s {
 
@@ -496,8 +497,8 @@ constexpr int kFwd16Batch = 256;
 __global__ void __launch_bounds__(kFwd16Threads, 10)
 raster_fwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict__ offsets,
                     const int32_t* __restrict__ flatten_ids, int64_t n_keys, int64_t n_isects,
-                    uint32_t W, uint32_t H, uint32_t ntx, uint32_t nty, float* __restrict__ image,
-                    uint16_t* __restrict__ cull_out) {
+                    int64_t n_splats, uint32_t W, uint32_t H, uint32_t ntx, uint32_t nty,
+                    float* __restrict__ image, uint16_t* __restrict__ cull_out) {
     // staged records in pattern order
     __shared__ float4 s_p[kFwd16Batch];  // mx, my, A = a/2 log2e, B = b log2e
     __shared__ float4 s_q[kFwd16Batch];  // C = c/2 log2e, w*mu, s_thr, 0
@@ -511,6 +512,8 @@ raster_fwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict
     const int64_t key = cam * (int64_t)ntx * nty + (int64_t)blockIdx.y * ntx + blockIdx.x;
     const int start = offsets[key];
     const int end = key + 1 < n_keys ? offsets[key + 1] : (int)n_isects;
+    if (R2S_DBG_BAD(start >= 0 && start <= end && end <= n_isects, R2S_DBG_TILE_RANGE))
+        return;  // uniform over the CTA
     const int cmax = min(15, (int)W - 1 - X0), rmax = min(15, (int)H - 1 - Y0);
 
     const int col = lane & 15, rb = lane >> 4;
@@ -531,6 +534,7 @@ raster_fwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict
             const int ti = k * kFwd16Threads + tid;
             if (ti >= n) continue;
             const int64_t g = flatten_ids[b0 + ti];
+            if (R2S_DBG_BAD(g >= 0 && g < n_splats, R2S_DBG_RECORD_ID)) continue;
             const float4 p = splats[2 * g];
             const float4 q = splats[2 * g + 1];
             int c_lo, c_hi, r_lo, r_hi;
@@ -631,7 +635,9 @@ raster_fwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict
     for (int p = tid; p < 256; p += kFwd16Threads) {
         const int r = p >> 4, c = p & 15;
         const float v = (s_acc[0][p] + s_acc[1][p]) + (s_acc[2][p] + s_acc[3][p]);
-        if (c <= cmax && r <= rmax) out[(int64_t)(Y0 + r) * W + X0 + c] = v;
+        if (c <= cmax && r <= rmax &&
+            !R2S_DBG_BAD(Y0 + r < (int)H && X0 + c < (int)W, R2S_DBG_PIXEL))
+            out[(int64_t)(Y0 + r) * W + X0 + c] = v;
     }
 }
 
@@ -663,7 +669,8 @@ template <bool WITH_ABS>
 __global__ void __launch_bounds__(kBwd16Threads)
 raster_bwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict__ offsets,
                     const int32_t* __restrict__ flatten_ids, int64_t n_keys, int64_t n_isects,
-                    const float* __restrict__ v_image, uint32_t W, uint32_t H, uint32_t ntx,
+                    int64_t n_splats, const float* __restrict__ v_image, uint32_t W, uint32_t H,
+                    uint32_t ntx,
                     uint32_t nty, const uint16_t* __restrict__ cull_in,
                     float* __restrict__ stats) {
     // upstream gradient of the tile, row-major and (16 floats further, so
@@ -686,6 +693,7 @@ raster_bwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict
     const int start = offsets[key];
     const int end = key + 1 < n_keys ? offsets[key + 1] : (int)n_isects;
     if (start >= end) return;
+    if (R2S_DBG_BAD(start >= 0 && end <= n_isects, R2S_DBG_TILE_RANGE)) return;  // CTA-uniform
     const int cmax = min(15, (int)W - 1 - X0), rmax = min(15, (int)H - 1 - Y0);
     {
         const float* vc = v_image + cam * (int64_t)H * W;
@@ -711,7 +719,10 @@ raster_bwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict
             float4 p = make_float4(0.f, 0.f, 0.f, 0.f), q = p;
             int rows = 0x0f;  // empty: first row 15 > last row 0
             bucket[k] = 256;
-            if (i < end) {
+            if (i < end && R2S_DBG_BAD(flatten_ids[i] >= 0 && flatten_ids[i] < n_splats,
+                                        R2S_DBG_RECORD_ID)) {
+                // checked build: an id outside the records stays unstaged
+            } else if (i < end) {
                 g = flatten_ids[i];
                 p = splats[2 * (int64_t)g];
                 q = splats[2 * (int64_t)g + 1];
@@ -890,13 +901,13 @@ int check_tiles(int64_t C, uint32_t W, uint32_t H, uint32_t T, uint32_t ntx, uin
 }
 
 int launch_raster_fwd16(const float4* splats, const int32_t* offsets, const int32_t* flatten_ids,
-                        int64_t C, int64_t n_isects, uint32_t W, uint32_t H, uint32_t ntx,
-                        uint32_t nty, float* image, cudaStream_t stream,
+                        int64_t C, int64_t N, int64_t n_isects, uint32_t W, uint32_t H,
+                        uint32_t ntx, uint32_t nty, float* image, cudaStream_t stream,
                         uint16_t* cull_out = nullptr) {
     const dim3 grid(ntx, nty, (unsigned)C);
     raster_fwd16_kernel<<<grid, kFwd16Threads, 0, stream>>>(
-        splats, offsets, flatten_ids, C * (int64_t)ntx * nty, n_isects, W, H, ntx, nty, image,
-        cull_out);
+        splats, offsets, flatten_ids, C * (int64_t)ntx * nty, n_isects, C * N, W, H, ntx, nty,
+        image, cull_out);
     return check_launch("rasterize_to_pixels_fwd");
 }
 
@@ -909,12 +920,12 @@ int launch_raster_bwd16(const float4* splats, const int32_t* offsets, const int3
     const dim3 grid(ntx, nty, (unsigned)C);
     if (with_abs)
         raster_bwd16_kernel<true><<<grid, kBwd16Threads, 0, stream>>>(
-            splats, offsets, flatten_ids, C * (int64_t)ntx * nty, n_isects, v_image, W, H, ntx,
-            nty, cull_in, stats);
+            splats, offsets, flatten_ids, C * (int64_t)ntx * nty, n_isects, C * N, v_image, W, H,
+            ntx, nty, cull_in, stats);
     else
         raster_bwd16_kernel<false><<<grid, kBwd16Threads, 0, stream>>>(
-            splats, offsets, flatten_ids, C * (int64_t)ntx * nty, n_isects, v_image, W, H, ntx,
-            nty, cull_in, stats);
+            splats, offsets, flatten_ids, C * (int64_t)ntx * nty, n_isects, C * N, v_image, W, H,
+            ntx, nty, cull_in, stats);
     return check_launch("rasterize_to_pixels_bwd");
 }
 
@@ -980,8 +991,8 @@ extern "C" int r2s_rasterize_to_pixels_fwd(int dtype, const void* means2d, const
         pack_splats_kernel<<<grid_for(C * N), kThreads, 0, stream>>>(
             (const float*)means2d, (const float*)conics, (const float*)opacities,
             (const float*)mus, C * N, (float4*)splat_scratch);
-        return launch_raster_fwd16((const float4*)splat_scratch, offsets, flatten_ids, C, n_isects,
-                                   W, H, ntx, nty, (float*)image, stream);
+        return launch_raster_fwd16((const float4*)splat_scratch, offsets, flatten_ids, C, N,
+                                   n_isects, W, H, ntx, nty, (float*)image, stream);
     }
     return R2S_DTYPE_DISPATCH(dtype, "rasterize_to_pixels_fwd", [&] {
         RasterSrc<scalar_t> src{nullptr, (const scalar_t*)means2d, (const scalar_t*)conics,
@@ -1060,8 +1071,8 @@ extern "C" int r2s_raster_splats_fwd_f32(const float* splats, const int32_t* off
     }
     if (int rc = check_tiles(C, W, H, T, ntx, nty)) return rc;
     if (T == 16)
-        return launch_raster_fwd16((const float4*)splats, offsets, flatten_ids, C, n_isects, W, H,
-                                   ntx, nty, image, stream, cull_ranges);
+        return launch_raster_fwd16((const float4*)splats, offsets, flatten_ids, C, N, n_isects, W,
+                                   H, ntx, nty, image, stream, cull_ranges);
     RasterSrc<float> src{(const float4*)splats, nullptr, nullptr, nullptr, nullptr};
     return launch_raster_fwd<float, true>(src, offsets, flatten_ids, C, n_isects, W, H, T, ntx,
                                           nty, image, stream);
@@ -1217,3 +1228,7 @@ extern "C" int r2s_rasterize_to_pixels_bwd_noalloc_f32(
                                        splats, stats, v_means2d_abs, v_means2d, v_conics,
                                        v_opacities, v_mus, stream);
 }
+
+namespace r2s {
+R2S_DBG_DEFINE_READER(debug_flags_raster)
+}  // namespace r2s

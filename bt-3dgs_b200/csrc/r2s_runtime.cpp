@@ -33,7 +33,42 @@ int check_launch(const char* what) {
 
 }  // namespace r2s
 
-extern "C" const char* r2s_version(void) { return "r2s-b200 0.1.0 (sm_100a)"; }
+namespace r2s {
+// flag words of the checked build, one per translation unit (r2s_debug.cuh)
+int debug_flags_raster(unsigned* flags, int clear);
+int debug_flags_voxel(unsigned* flags, int clear);
+int debug_flags_binning(unsigned* flags, int clear);
+}  // namespace r2s
+
+extern "C" const char* r2s_version(void) {
+#ifdef R2S_DEBUG
+    return "r2s-b200 0.1.0 (sm_100a, bounds-checked build)";
+#else
+    return "r2s-b200 0.1.0 (sm_100a)";
+#endif
+}
+
+extern "C" int r2s_debug_build(void) {
+#ifdef R2S_DEBUG
+    return 1;
+#else
+    return 0;
+#endif
+}
+
+extern "C" int r2s_debug_flags(unsigned* flags, int clear) {
+    if (flags == nullptr) return r2s::fail(R2S_ERR_ARG, "debug_flags: flags is null");
+    *flags = 0;
+    int (*readers[])(unsigned*, int) = {r2s::debug_flags_raster, r2s::debug_flags_voxel,
+                                        r2s::debug_flags_binning};
+    for (auto read : readers) {
+        const int e = read(flags, clear);
+        if (e != 0)
+            return r2s::fail(R2S_ERR_CUDA, "debug_flags: reading the flag words failed (%s)",
+                             cudaGetErrorString((cudaError_t)e));
+    }
+    return R2S_OK;
+}
 
 extern "C" size_t r2s_last_error(char* buf, size_t len) {
     const std::string& m = r2s::g_last_error;

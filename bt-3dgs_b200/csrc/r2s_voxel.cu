@@ -27,6 +27,7 @@
 
 #include "r2s_common.cuh"
 #include "r2s_cull.cuh"
+#include "r2s_debug.cuh"
 
 namespace r2s {
 
@@ -514,8 +515,8 @@ constexpr int kVRowsThreads = 128;
 __global__ void __launch_bounds__(kVRowsThreads)
 voxel_rows8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict__ offsets,
                    const int32_t* __restrict__ flatten_ids, int64_t n_keys, int64_t n_isects,
-                   uint32_t dim2, uint32_t dim1, uint32_t dim0, uint32_t nt2, uint32_t nt1,
-                   uint32_t layer_begin, uint2* __restrict__ rows) {
+                   int64_t n_splats, uint32_t dim2, uint32_t dim1, uint32_t dim0, uint32_t nt2,
+                   uint32_t nt1, uint32_t layer_begin, uint2* __restrict__ rows) {
     const uint32_t bz = blockIdx.z + layer_begin;
     const int64_t key = ((int64_t)blockIdx.z * nt1 + blockIdx.y) * nt2 + blockIdx.x;
     const int X0 = blockIdx.x * 8, Y0 = blockIdx.y * 8, Z0 = bz * 8;
@@ -524,8 +525,10 @@ voxel_rows8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict
     const int zmax = min(7, (int)dim0 - 1 - Z0);
     const int start = offsets[key];
     const int end = key + 1 < n_keys ? offsets[key + 1] : (int)n_isects;
+    if (R2S_DBG_BAD(start >= 0 && start <= end && end <= n_isects, R2S_DBG_TILE_RANGE)) return;
     for (int i = start + threadIdx.x; i < end; i += kVRowsThreads) {
         const int64_t g = flatten_ids[i];
+        if (R2S_DBG_BAD(g >= 0 && g < n_splats, R2S_DBG_RECORD_ID)) continue;
         const VRecord r = load_vrecord(vsplats, g);
         int xl, xh, yl, yh, zl, zh;
         cull_range_v(r.m[0], r.e[0], (float)X0, xmax, xl, xh);
@@ -547,8 +550,9 @@ constexpr int kVFwd8Batch = 128;
 __global__ void __launch_bounds__(kVFwd8Threads)
 voxel_fwd8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict__ offsets,
                   const int32_t* __restrict__ flatten_ids, const uint2* __restrict__ rows,
-                  int64_t n_keys, int64_t n_isects, uint32_t dim2, uint32_t dim1, uint32_t dim0,
-                  uint32_t nt2, uint32_t nt1, uint32_t layer_begin, float* __restrict__ vol) {
+                  int64_t n_keys, int64_t n_isects, int64_t n_splats, uint32_t dim2,
+                  uint32_t dim1, uint32_t dim0, uint32_t nt2, uint32_t nt1, uint32_t layer_begin,
+                  float* __restrict__ vol) {
     __shared__ float4 s_a[kVFwd8Batch];  // mx, my, mz, A
     __shared__ float4 s_b[kVFwd8Batch];  // B, Cq, D, E
     __shared__ float4 s_c[kVFwd8Batch];  // F, w, s threshold, warp mask (bits)
@@ -567,6 +571,8 @@ voxel_fwd8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict_
     const float pz0 = (float)(Z0 + lz) + 0.5f, pz1 = (float)(Z0 + lz) + 1.5f;
     const int start = offsets[key];
     const int end = key + 1 < n_keys ? offsets[key + 1] : (int)n_isects;
+    if (R2S_DBG_BAD(start >= 0 && start <= end && end <= n_isects, R2S_DBG_TILE_RANGE))
+        return;  // uniform over the CTA
     float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};  // [z][x]
 
     for (int b0 = start; b0 < end; b0 += kVFwd8Batch) {
@@ -574,6 +580,10 @@ voxel_fwd8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict_
         __syncthreads();
         for (int j = tid; j < n; j += kVFwd8Threads) {
             const int64_t g = flatten_ids[b0 + j];
+            if (R2S_DBG_BAD(g >= 0 && g < n_splats, R2S_DBG_RECORD_ID)) {
+                s_c[j] = make_float4(0.f, 0.f, 0.f, __uint_as_float(0u));  // no warp evaluates it
+                continue;
+            }
             const VRecord r = load_vrecord(vsplats, g);
             int xl, xh, yl, yh, zl, zh;
             cull_range_v(r.m[0], r.e[0], (float)X0, xmax, xl, xh);
@@ -633,6 +643,11 @@ voxel_fwd8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict_
 #pragma unroll
     for (int zz = 0; zz < 2; ++zz) {
         if (lz + zz > zmax) continue;
+        if (R2S_DBG_BAD(Z0 + lz + zz - zoff <
+                                min((int64_t)(layer_begin + gridDim.z) * 8, (int64_t)dim0) - zoff &&
+                            Y0 + ly < (int)dim1 && X0 + lx < (int)dim2,
+                        R2S_DBG_PIXEL))
+            continue;
         float* row = vol + ((Z0 + lz + zz - zoff) * (int64_t)dim1 + (Y0 + ly)) * dim2 + X0 + lx;
         if (lx + 3 <= xmax && (dim2 & 3) == 0) {
             *reinterpret_cast<float4*>(row) =
@@ -660,9 +675,9 @@ constexpr int kVBwd8Batch = 1024;   // records staged and sorted per batch
 __global__ void __launch_bounds__(kVBwd8Threads)
 voxel_bwd8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict__ offsets,
                   const int32_t* __restrict__ flatten_ids, const uint2* __restrict__ rows,
-                  int64_t n_keys, int64_t n_isects, const float* __restrict__ v_vol,
-                  uint32_t dim2, uint32_t dim1, uint32_t dim0, uint32_t nt2, uint32_t nt1,
-                  uint32_t layer_begin, float* __restrict__ stats) {
+                  int64_t n_keys, int64_t n_isects, int64_t n_splats,
+                  const float* __restrict__ v_vol, uint32_t dim2, uint32_t dim1, uint32_t dim0,
+                  uint32_t nt2, uint32_t nt1, uint32_t layer_begin, float* __restrict__ stats) {
     __shared__ __align__(16) float s_v[512];
     __shared__ uint2 s_tab[kVBwd8Batch];     // per-slice rows (byte k: first | last << 4)
     __shared__ int32_t s_g[kVBwd8Batch];
@@ -681,12 +696,16 @@ voxel_bwd8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict_
     const int start = offsets[key];
     const int end = key + 1 < n_keys ? offsets[key + 1] : (int)n_isects;
     if (start >= end) return;
+    if (R2S_DBG_BAD(start >= 0 && end <= n_isects, R2S_DBG_TILE_RANGE)) return;  // CTA-uniform
     const int64_t zoff = (int64_t)layer_begin * 8;
     for (int p = tid; p < 512; p += kVBwd8Threads) {
         const int z = p >> 6, y = (p >> 3) & 7, x = p & 7;
-        s_v[p] = (x <= xmax && y <= ymax && z <= zmax)
-                     ? v_vol[((Z0 + z - zoff) * (int64_t)dim1 + (Y0 + y)) * dim2 + X0 + x]
-                     : 0.f;
+        bool in = x <= xmax && y <= ymax && z <= zmax;
+        if (in && R2S_DBG_BAD(Z0 + z - zoff < min((int64_t)(layer_begin + gridDim.z) * 8,
+                                                   (int64_t)dim0) - zoff,
+                              R2S_DBG_PIXEL))
+            in = false;
+        s_v[p] = in ? v_vol[((Z0 + z - zoff) * (int64_t)dim1 + (Y0 + y)) * dim2 + X0 + x] : 0.f;
     }
     const float X0f = (float)X0, Y0f = (float)Y0, Z0f = (float)Z0;
 
@@ -702,7 +721,10 @@ voxel_bwd8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict_
             int32_t g = 0;
             uint32_t tlo = 0x0f0f0f0fu, thi = 0x0f0f0f0fu;
             int ezl = 8, ezh = -1;
-            if (i < end) {
+            if (i < end && R2S_DBG_BAD(flatten_ids[i] >= 0 && flatten_ids[i] < n_splats,
+                                        R2S_DBG_RECORD_ID)) {
+                // checked build: an id outside the records stays unstaged
+            } else if (i < end) {
                 g = flatten_ids[i];
                 if (rows != nullptr) {
                     const uint2 tab = rows[i];
@@ -998,7 +1020,7 @@ extern "C" int r2s_voxel_rows_f32(const float* vsplats, const int32_t* offsets,
     const dim3 grid(nt2, nt1, layer_end - layer_begin);
     voxel_rows8_kernel<<<grid, kVRowsThreads, 0, stream>>>(
         (const float4*)vsplats, offsets, flatten_ids,
-        (int64_t)(layer_end - layer_begin) * nt1 * nt2, n_isects, dim2, dim1, dim0, nt2, nt1,
+        (int64_t)(layer_end - layer_begin) * nt1 * nt2, n_isects, N, dim2, dim1, dim0, nt2, nt1,
         layer_begin, reinterpret_cast<uint2*>(rows));
     return check_launch("voxel_rows");
 }
@@ -1024,8 +1046,8 @@ extern "C" int r2s_voxel_splats_fwd_f32(const float* vsplats, const int32_t* off
         const dim3 grid(nt2, nt1, layer_end - layer_begin);
         voxel_fwd8_kernel<<<grid, kVFwd8Threads, 0, stream>>>(
             (const float4*)vsplats, offsets, flatten_ids, reinterpret_cast<const uint2*>(rows),
-            (int64_t)(layer_end - layer_begin) * nt1 * nt2, n_isects, dim2, dim1, dim0, nt2, nt1,
-            layer_begin, volume);
+            (int64_t)(layer_end - layer_begin) * nt1 * nt2, n_isects, N, dim2, dim1, dim0, nt2,
+            nt1, layer_begin, volume);
         return check_launch("voxel_splats_fwd");
     }
     VoxSrc<float> src{(const float4*)vsplats, nullptr, nullptr, nullptr};
@@ -1050,8 +1072,8 @@ extern "C" int r2s_voxel_splats_bwd_f32(const float* vsplats, const int32_t* off
             const dim3 grid(nt2, nt1, layer_end - layer_begin);
             voxel_bwd8_kernel<<<grid, kVBwd8Threads, 0, stream>>>(
                 (const float4*)vsplats, offsets, flatten_ids, reinterpret_cast<const uint2*>(rows),
-                (int64_t)(layer_end - layer_begin) * nt1 * nt2, n_isects, v_volume, dim2, dim1,
-                dim0, nt2, nt1, layer_begin, stats);
+                (int64_t)(layer_end - layer_begin) * nt1 * nt2, n_isects, N, v_volume, dim2,
+                dim1, dim0, nt2, nt1, layer_begin, stats);
         }
         return check_launch("voxel_splats_bwd");
     }
@@ -1060,3 +1082,7 @@ extern "C" int r2s_voxel_splats_bwd_f32(const float* vsplats, const int32_t* off
                                             dim1, dim0, T, nt2, nt1, layer_begin, layer_end, stats,
                                             stream);
 }
+
+namespace r2s {
+R2S_DBG_DEFINE_READER(debug_flags_voxel)
+}  // namespace r2s

@@ -57,6 +57,8 @@ _SIGNATURES = {
     "r2s_last_error": ([ctypes.c_char_p, ctypes.c_size_t], ctypes.c_size_t),
     "r2s_split_children_f32": (
         [_p, _p, _p, _p, _p, _i64, _f64, _f64, _f64, _i32, _p, _p, _p, _p, _p], _i32),
+    "r2s_debug_build": ([], _i32),
+    "r2s_debug_flags": ([ctypes.POINTER(ctypes.c_uint32), _i32], _i32),
     "r2s_calib_ffma_f32": ([_p, _i64, _i32, _p], _i32),
     "r2s_calib_ex2_f32": ([_p, _i64, _i32, _p], _i32),
     "r2s_parameter_transform_fwd": ([_i32, _p, _p, _f64, _f64, _p, _p, _i64, _p], _i32),

@@ -146,6 +146,20 @@ R2S_API const char* r2s_version(void);
  * truncated to len-1 bytes); returns the full message length. */
 R2S_API size_t r2s_last_error(char* buf, size_t len);
 
+/* Bounds-checked build (libr2s_debug.so: every source built with R2S_DEBUG;
+ * no counterpart in the reference, whose contributor guide asks for a CUDA
+ * sanitizer run instead, CONTRIBUTING.md:33-35).  In that build the
+ * rasterizer, voxelizer and binning kernels test every tile record range
+ * (within [0, n_isects)), record id (below C*N or N), pixel/voxel index and
+ * binning output slot before using it; a failed test sets a bit in
+ * *flags (1 tile range, 2 record id, 4 pixel/voxel, 8 binning slot) and
+ * skips the access.  r2s_debug_build() is 1 in that build, 0 in the release
+ * library, whose r2s_debug_flags() always reports 0.  r2s_debug_flags reads
+ * (and with clear != 0 resets) the flags of all kernels; flags is a host
+ * pointer and the call waits for the device. */
+R2S_API int r2s_debug_build(void);
+R2S_API int r2s_debug_flags(unsigned* flags, int clear);
+
 /* Pipe calibration (measurement support; no counterpart in the reference).
  * `blocks` CTAs of 256 threads each run 8 independent chains of `iters`
  * FFMAs (2 FLOP each) or of `iters` FMUL + ex2.approx steps, and write one
