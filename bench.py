@@ -897,9 +897,9 @@ def pipe_peaks(dev):
 
 # DRAM traffic of one raster_bwd16_kernel launch per view: the ncu capture of
 # `bench.py --views 8` in profiles/raster_bwd16_cfg2_8views.md,
-# dram__bytes_read.sum + dram__bytes_write.sum = 530.674 MB + 105.416 MB for 8
+# dram__bytes_read.sum + dram__bytes_write.sum = 530.805 MB + 106.821 MB for 8
 # views (traffic grows with the views).
-BWD16_DRAM_BYTES_PER_VIEW = (530.674176e6 + 105.415936e6) / 8
+BWD16_DRAM_BYTES_PER_VIEW = (530.805248e6 + 106.821376e6) / 8
 # FP32 work per evaluated pixel of raster_bwd16_kernel<true> (absolute
 # gradients on), counted from its inner loop: 7 FFMA (the exponent: 2; the row
 # moment R1; the two conic products a dx + b dy, b dx + c dy; the two absolute
