@@ -172,8 +172,10 @@ class HostPipeline:
     result back, every step inside the timed region.  The copies run on a copy
     stream: the next step's inputs upload while this step computes (a
     double-buffered input pipeline) and the outputs download behind the next
-    step.  Subclasses set ``self.host`` (pinned host inputs) and implement
-    ``step(*device_inputs)`` returning the device tensors to download."""
+    step into two alternating sets of pinned host buffers, allocated once, as
+    a training loop keeps them.  Subclasses set ``self.host`` (pinned host
+    inputs) and implement ``step(*device_inputs)`` returning the device
+    tensors to download."""
 
     def _upload(self):
         with torch.cuda.stream(self.copy_stream):
@@ -185,6 +187,22 @@ class HostPipeline:
     def reset_pipeline(self):
         self.copy_stream = torch.cuda.Stream(device=self.dev)
         self.prefetched = None
+        # host output buffers survive a reset (allocated in the warm-up steps)
+        self.out_sets = getattr(self, "out_sets", None)
+        self.out_events = [None, None]
+        self.out_turn = 0
+
+    def _host_outputs(self, results):
+        """The pinned host buffers of this step (the set the step before last
+        used: its download has completed once its event has)."""
+        if self.out_sets is None:
+            self.out_sets = [[torch.empty(r.shape, dtype=r.dtype, pin_memory=True)
+                              for r in results] for _ in range(2)]
+        k = self.out_turn
+        self.out_turn ^= 1
+        if self.out_events[k] is not None:
+            self.out_events[k].synchronize()
+        return k, self.out_sets[k]
 
     def step_e2e(self, prefetch_next=True):
         if getattr(self, "copy_stream", None) is None:
@@ -201,10 +219,14 @@ class HostPipeline:
         done = torch.cuda.Event()
         done.record(compute)
         self.copy_stream.wait_event(done)
+        k, outs = self._host_outputs(results)
         with torch.cuda.stream(self.copy_stream):
-            outs = [r.to("cpu", non_blocking=True) for r in results]
-            for r in results:
+            for o, r in zip(outs, results):
+                o.copy_(r, non_blocking=True)
                 r.record_stream(self.copy_stream)
+            ev = torch.cuda.Event()
+            ev.record(self.copy_stream)
+        self.out_events[k] = ev
         return outs
 
     def bytes_e2e(self):
