@@ -388,14 +388,16 @@ class OursVoxel(HostPipeline):
                                                    wl.RADIUS_CLIP)
             T.mark("volume mapping")
             offs, fids, _ = W.fused_bin(rects, l1 - l0, N, nt * nt, nt, 1, segment_base=l0)
-            T.mark("3D binning (incl. host read of the record count)")
-            rows = W.fused_voxel_rows(vs, offs, fids, N, G, G, G, wl.VOL_TILE, nt, nt, nt, l0, l1)
+            order = W.fused_brick_order(offs, fids.numel())
+            T.mark("3D binning (incl. host read of the record count) + brick order")
+            rows = W.fused_voxel_rows(vs, offs, fids, N, G, G, G, wl.VOL_TILE, nt, nt, nt, l0, l1,
+                                      order=order)
             T.mark("row table")
             W.fused_voxel_fwd(vs, offs, fids, N, G, G, G, wl.VOL_TILE, nt, nt, nt, l0, l1,
-                              rows=rows)
+                              rows=rows, order=order)
             T.mark("voxel forward")
             stats = W.fused_voxel_bwd(vs, offs, fids, self.v_vol, N, G, G, G, wl.VOL_TILE, nt, nt,
-                                      nt, l0, l1, rows=rows)
+                                      nt, l0, l1, rows=rows, order=order)
             T.mark("voxel backward")
             outs = [torch.empty_like(t) for t in (m, q, s, o)]
             W.fused_explicit_backward(m, q, s, o, wl.SCALE_MIN, wl.SCALE_MAX, None, None, 0, 0,
@@ -1237,10 +1239,10 @@ def main():
     # our kernels per timed step: projection = prepare, project_splats, binning
     # (count, column scan, scan, place), raster forward, raster backward,
     # explicit backward; voxel = prepare, map, binning (count, column scan,
-    # scan, place), row table, voxel forward, voxel backward, explicit
-    # backward (the zero-view projection pass launches nothing)
+    # scan, place), brick order, row table, voxel forward, voxel backward,
+    # explicit backward (the zero-view projection pass launches nothing)
     gpu_launches = args.steps * 9
-    vox_launches = args.steps * 10
+    vox_launches = args.steps * 11
     if rank != 0:
         return
     line = {

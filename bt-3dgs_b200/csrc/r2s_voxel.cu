@@ -506,6 +506,55 @@ __device__ __forceinline__ void table_slices(uint32_t tlo, uint32_t thi, int& ez
     }
 }
 
+// Launch order of the brick CTAs.  The per-brick kernels below map their
+// linear block index through `order` (when given) to a brick key, so that
+// the GPU, which starts blocks in linear order, begins with the bricks that
+// hold the most records: the classic longest-first schedule, which keeps a
+// long brick from starting last and idling the other SMs at the end of a
+// launch whose bricks fill about one wave (a z-slab of a multi-GPU split).
+__device__ __forceinline__ int64_t brick_of_block(const int32_t* __restrict__ order,
+                                                  uint32_t nt2, uint32_t nt1, int& bx, int& by,
+                                                  int& bzl) {
+    const int64_t lin = ((int64_t)blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+    const int64_t key = order != nullptr ? (int64_t)order[lin] : lin;
+    bx = (int)(key % nt2);
+    by = (int)((key / nt2) % nt1);
+    bzl = (int)(key / ((int64_t)nt2 * nt1));
+    return key;
+}
+
+constexpr int kOrderThreads = 1024;
+
+// order[] = brick keys grouped by floor(log2(records)) from the largest
+// group down (an approximate longest-first order; empty bricks last).  One
+// CTA: a histogram of the 33 groups, their descending prefix, a scatter.
+__global__ void __launch_bounds__(kOrderThreads)
+brick_order_kernel(const int32_t* __restrict__ offsets, int64_t n_keys, int64_t n_isects,
+                   int32_t* __restrict__ order) {
+    __shared__ int s_cnt[33];
+    __shared__ int s_cur[33];
+    const int tid = threadIdx.x;
+    if (tid < 33) s_cnt[tid] = 0;
+    __syncthreads();
+    auto group = [&](int64_t k) {
+        const int64_t end = k + 1 < n_keys ? (int64_t)offsets[k + 1] : n_isects;
+        const int64_t c = end - (int64_t)offsets[k];
+        return c > 0 ? 32 - __clz((unsigned)min(c, (int64_t)INT32_MAX)) : 0;  // 0..31
+    };
+    for (int64_t k = tid; k < n_keys; k += kOrderThreads) atomicAdd(&s_cnt[group(k)], 1);
+    __syncthreads();
+    if (tid == 0) {
+        int run = 0;
+        for (int b = 32; b >= 0; --b) {
+            s_cur[b] = run;
+            run += s_cnt[b];
+        }
+    }
+    __syncthreads();
+    for (int64_t k = tid; k < n_keys; k += kOrderThreads)
+        order[atomicAdd(&s_cur[group(k)], 1)] = (int32_t)k;
+}
+
 // Row table of every (record, brick) pair of the brick lists: rows[i] =
 // brick_rows of record i against its brick (per-slice first | last row,
 // 0x0f for none).  One CTA per brick; computed once per binning and read by
@@ -516,10 +565,12 @@ __global__ void __launch_bounds__(kVRowsThreads)
 voxel_rows8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict__ offsets,
                    const int32_t* __restrict__ flatten_ids, int64_t n_keys, int64_t n_isects,
                    int64_t n_splats, uint32_t dim2, uint32_t dim1, uint32_t dim0, uint32_t nt2,
-                   uint32_t nt1, uint32_t layer_begin, uint2* __restrict__ rows) {
-    const uint32_t bz = blockIdx.z + layer_begin;
-    const int64_t key = ((int64_t)blockIdx.z * nt1 + blockIdx.y) * nt2 + blockIdx.x;
-    const int X0 = blockIdx.x * 8, Y0 = blockIdx.y * 8, Z0 = bz * 8;
+                   uint32_t nt1, uint32_t layer_begin, const int32_t* __restrict__ order,
+                   uint2* __restrict__ rows) {
+    int bxi, byi, bzl;
+    const int64_t key = brick_of_block(order, nt2, nt1, bxi, byi, bzl);
+    const uint32_t bz = bzl + layer_begin;
+    const int X0 = bxi * 8, Y0 = byi * 8, Z0 = bz * 8;
     const int xmax = min(7, (int)dim2 - 1 - X0);
     const int ymax = min(7, (int)dim1 - 1 - Y0);
     const int zmax = min(7, (int)dim0 - 1 - Z0);
@@ -552,15 +603,16 @@ voxel_fwd8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict_
                   const int32_t* __restrict__ flatten_ids, const uint2* __restrict__ rows,
                   int64_t n_keys, int64_t n_isects, int64_t n_splats, uint32_t dim2,
                   uint32_t dim1, uint32_t dim0, uint32_t nt2, uint32_t nt1, uint32_t layer_begin,
-                  float* __restrict__ vol) {
+                  const int32_t* __restrict__ order, float* __restrict__ vol) {
     __shared__ float4 s_a[kVFwd8Batch];  // mx, my, mz, A
     __shared__ float4 s_b[kVFwd8Batch];  // B, Cq, D, E
     __shared__ float4 s_c[kVFwd8Batch];  // F, w, s threshold, warp mask (bits)
 
     const int tid = threadIdx.x, warp = tid >> 5;
-    const uint32_t bz = blockIdx.z + layer_begin;
-    const int64_t key = ((int64_t)blockIdx.z * nt1 + blockIdx.y) * nt2 + blockIdx.x;
-    const int X0 = blockIdx.x * 8, Y0 = blockIdx.y * 8, Z0 = bz * 8;
+    int bxi, byi, bzl;
+    const int64_t key = brick_of_block(order, nt2, nt1, bxi, byi, bzl);
+    const uint32_t bz = bzl + layer_begin;
+    const int X0 = bxi * 8, Y0 = byi * 8, Z0 = bz * 8;
     const int xmax = min(7, (int)dim2 - 1 - X0);
     const int ymax = min(7, (int)dim1 - 1 - Y0);
     const int zmax = min(7, (int)dim0 - 1 - Z0);
@@ -677,7 +729,8 @@ voxel_bwd8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict_
                   const int32_t* __restrict__ flatten_ids, const uint2* __restrict__ rows,
                   int64_t n_keys, int64_t n_isects, int64_t n_splats,
                   const float* __restrict__ v_vol, uint32_t dim2, uint32_t dim1, uint32_t dim0,
-                  uint32_t nt2, uint32_t nt1, uint32_t layer_begin, float* __restrict__ stats) {
+                  uint32_t nt2, uint32_t nt1, uint32_t layer_begin,
+                  const int32_t* __restrict__ order, float* __restrict__ stats) {
     __shared__ __align__(16) float s_v[512];
     __shared__ uint2 s_tab[kVBwd8Batch];     // per-slice rows (byte k: first | last << 4)
     __shared__ int32_t s_g[kVBwd8Batch];
@@ -687,9 +740,10 @@ voxel_bwd8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict_
     __shared__ int s_next;                   // next group to take
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const uint32_t bz = blockIdx.z + layer_begin;
-    const int64_t key = ((int64_t)blockIdx.z * nt1 + blockIdx.y) * nt2 + blockIdx.x;
-    const int X0 = blockIdx.x * 8, Y0 = blockIdx.y * 8, Z0 = bz * 8;
+    int bxi, byi, bzl;
+    const int64_t key = brick_of_block(order, nt2, nt1, bxi, byi, bzl);
+    const uint32_t bz = bzl + layer_begin;
+    const int X0 = bxi * 8, Y0 = byi * 8, Z0 = bz * 8;
     const int xmax = min(7, (int)dim2 - 1 - X0);
     const int ymax = min(7, (int)dim1 - 1 - Y0);
     const int zmax = min(7, (int)dim0 - 1 - Z0);
@@ -1010,7 +1064,8 @@ extern "C" int r2s_voxel_rows_f32(const float* vsplats, const int32_t* offsets,
                                   const int32_t* flatten_ids, int64_t N, int64_t n_isects,
                                   uint32_t dim2, uint32_t dim1, uint32_t dim0, uint32_t T,
                                   uint32_t nt2, uint32_t nt1, uint32_t nt0, uint32_t layer_begin,
-                                  uint32_t layer_end, uint32_t* rows, r2s_stream_t stream) {
+                                  uint32_t layer_end, const int32_t* brick_order, uint32_t* rows,
+                                  r2s_stream_t stream) {
     R2S_REQUIRE(N >= 0 && n_isects >= 0, "voxel_rows: negative size");
     R2S_REQUIRE(T == 8, "voxel_rows: the row table is built for 8-voxel bricks");
     R2S_REQUIRE(layer_begin <= layer_end && layer_end <= nt0, "voxel_rows: bad layer range");
@@ -1021,7 +1076,7 @@ extern "C" int r2s_voxel_rows_f32(const float* vsplats, const int32_t* offsets,
     voxel_rows8_kernel<<<grid, kVRowsThreads, 0, stream>>>(
         (const float4*)vsplats, offsets, flatten_ids,
         (int64_t)(layer_end - layer_begin) * nt1 * nt2, n_isects, N, dim2, dim1, dim0, nt2, nt1,
-        layer_begin, reinterpret_cast<uint2*>(rows));
+        layer_begin, brick_order, reinterpret_cast<uint2*>(rows));
     return check_launch("voxel_rows");
 }
 
@@ -1030,7 +1085,8 @@ extern "C" int r2s_voxel_splats_fwd_f32(const float* vsplats, const int32_t* off
                                         int64_t N, int64_t n_isects,
                                         uint32_t dim2, uint32_t dim1, uint32_t dim0, uint32_t T,
                                         uint32_t nt2, uint32_t nt1, uint32_t nt0,
-                                        uint32_t layer_begin, uint32_t layer_end, float* volume,
+                                        uint32_t layer_begin, uint32_t layer_end,
+                                        const int32_t* brick_order, float* volume,
                                         r2s_stream_t stream) {
     R2S_REQUIRE(N >= 0 && n_isects >= 0, "voxel_splats_fwd: negative size");
     R2S_REQUIRE(layer_begin <= layer_end && layer_end <= nt0, "voxel_splats_fwd: bad layer range");
@@ -1047,7 +1103,7 @@ extern "C" int r2s_voxel_splats_fwd_f32(const float* vsplats, const int32_t* off
         voxel_fwd8_kernel<<<grid, kVFwd8Threads, 0, stream>>>(
             (const float4*)vsplats, offsets, flatten_ids, reinterpret_cast<const uint2*>(rows),
             (int64_t)(layer_end - layer_begin) * nt1 * nt2, n_isects, N, dim2, dim1, dim0, nt2,
-            nt1, layer_begin, volume);
+            nt1, layer_begin, brick_order, volume);
         return check_launch("voxel_splats_fwd");
     }
     VoxSrc<float> src{(const float4*)vsplats, nullptr, nullptr, nullptr};
@@ -1061,7 +1117,8 @@ extern "C" int r2s_voxel_splats_bwd_f32(const float* vsplats, const int32_t* off
                                         int64_t N, int64_t n_isects, uint32_t dim2, uint32_t dim1,
                                         uint32_t dim0, uint32_t T, uint32_t nt2, uint32_t nt1,
                                         uint32_t nt0, uint32_t layer_begin, uint32_t layer_end,
-                                        float* stats, r2s_stream_t stream) {
+                                        const int32_t* brick_order, float* stats,
+                                        r2s_stream_t stream) {
     R2S_REQUIRE(N >= 0 && n_isects >= 0, "voxel_splats_bwd: negative size");
     R2S_REQUIRE(layer_begin <= layer_end && layer_end <= nt0, "voxel_splats_bwd: bad layer range");
     if (int rc = check_bricks(T, nt2, nt1, nt0)) return rc;
@@ -1073,7 +1130,7 @@ extern "C" int r2s_voxel_splats_bwd_f32(const float* vsplats, const int32_t* off
             voxel_bwd8_kernel<<<grid, kVBwd8Threads, 0, stream>>>(
                 (const float4*)vsplats, offsets, flatten_ids, reinterpret_cast<const uint2*>(rows),
                 (int64_t)(layer_end - layer_begin) * nt1 * nt2, n_isects, N, v_volume, dim2,
-                dim1, dim0, nt2, nt1, layer_begin, stats);
+                dim1, dim0, nt2, nt1, layer_begin, brick_order, stats);
         }
         return check_launch("voxel_splats_bwd");
     }
@@ -1081,6 +1138,15 @@ extern "C" int r2s_voxel_splats_bwd_f32(const float* vsplats, const int32_t* off
     return launch_voxel_bwd<float, true, 0>(src, offsets, flatten_ids, v_volume, N, n_isects, dim2,
                                             dim1, dim0, T, nt2, nt1, layer_begin, layer_end, stats,
                                             stream);
+}
+
+extern "C" int r2s_brick_order(const int32_t* offsets, int64_t n_keys, int64_t n_isects,
+                               int32_t* order, r2s_stream_t stream) {
+    R2S_REQUIRE(n_keys >= 0 && n_isects >= 0, "brick_order: negative size");
+    if (n_keys == 0) return R2S_OK;
+    R2S_REQUIRE(n_keys <= INT32_MAX, "brick_order: too many bricks");
+    brick_order_kernel<<<1, kOrderThreads, 0, stream>>>(offsets, n_keys, n_isects, order);
+    return check_launch("brick_order");
 }
 
 namespace r2s {

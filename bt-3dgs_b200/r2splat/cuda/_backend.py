@@ -109,14 +109,15 @@ _SIGNATURES = {
         [_p, _p, _p, _p, _p, _i64, _u32, _u32, _u32, _u32, _u32, _u32, _u32, _f64, _f64, _p, _p,
          _p, _p, _p, _p, _p], _i32),
     "r2s_voxel_rows_f32": (
-        [_p, _p, _p, _i64, _i64, _u32, _u32, _u32, _u32, _u32, _u32, _u32, _u32, _u32, _p, _p],
-        _i32),
+        [_p, _p, _p, _i64, _i64, _u32, _u32, _u32, _u32, _u32, _u32, _u32, _u32, _u32, _p, _p,
+         _p], _i32),
+    "r2s_brick_order": ([_p, _i64, _i64, _p, _p], _i32),
     "r2s_voxel_splats_fwd_f32": (
         [_p, _p, _p, _p, _i64, _i64, _u32, _u32, _u32, _u32, _u32, _u32, _u32, _u32, _u32, _p,
-         _p], _i32),
+         _p, _p], _i32),
     "r2s_voxel_splats_bwd_f32": (
         [_p, _p, _p, _p, _p, _i64, _i64, _u32, _u32, _u32, _u32, _u32, _u32, _u32, _u32, _u32,
-         _p, _p], _i32),
+         _p, _p, _p], _i32),
     "r2s_explicit_backward_f32": (
         [_p, _p, _p, _p, _f64, _f64, _p, _p, _i64, _i64, _u32, _u32, _f64, _p, _p, _p, _p, _p,
          _u32, _u32, _u32, _f64, _p, _i32, _p, _p, _p, _p, _p], _i32),

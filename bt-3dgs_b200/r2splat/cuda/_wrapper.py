@@ -748,8 +748,18 @@ def fused_map(means, covars, opacities, ranges, centers, dim2, dim1, dim0, tile,
     return means3d, conics, radii, vsplats, rects, counts
 
 
+def fused_brick_order(offsets, n_isects):
+    """Longest-first launch order [n_keys] (int32) of the bricks of a 3D
+    binning (``r2s_brick_order``)."""
+    dev = offsets.device
+    order = torch.empty((offsets.numel(),), dtype=torch.int32, device=dev)
+    _call("r2s_brick_order", _ptr(offsets), offsets.numel(), int(n_isects), _ptr(order),
+          _stream(dev))
+    return order
+
+
 def fused_voxel_rows(vsplats, offsets, flatten_ids, N, dim2, dim1, dim0, tile, nt2, nt1, nt0,
-                     layer_begin=0, layer_end=None):
+                     layer_begin=0, layer_end=None, order=None):
     """Row table [n_isects, 2] (int32 bit patterns) of a 3D binning with
     8-voxel bricks, or None for other brick sizes."""
     if tile != 8:
@@ -760,12 +770,12 @@ def fused_voxel_rows(vsplats, offsets, flatten_ids, N, dim2, dim1, dim0, tile, n
     rows = torch.empty((flatten_ids.numel(), 2), dtype=torch.int32, device=dev)
     _call("r2s_voxel_rows_f32", _ptr(vsplats), _ptr(offsets), _ptr(flatten_ids), N,
           flatten_ids.numel(), dim2, dim1, dim0, tile, nt2, nt1, nt0, layer_begin, layer_end,
-          _ptr(rows), _stream(dev))
+          _ptr(order), _ptr(rows), _stream(dev))
     return rows
 
 
 def fused_voxel_fwd(vsplats, offsets, flatten_ids, N, dim2, dim1, dim0, tile, nt2, nt1, nt0,
-                    layer_begin=0, layer_end=None, out=None, rows=None):
+                    layer_begin=0, layer_end=None, out=None, rows=None, order=None):
     dev = vsplats.device
     if layer_end is None:
         layer_end = nt0
@@ -775,19 +785,19 @@ def fused_voxel_fwd(vsplats, offsets, flatten_ids, N, dim2, dim1, dim0, tile, nt
         out = torch.empty((max(z1 - z0, 0), dim1, dim2), dtype=torch.float32, device=dev)
     _call("r2s_voxel_splats_fwd_f32", _ptr(vsplats), _ptr(offsets), _ptr(flatten_ids), _ptr(rows),
           N, flatten_ids.numel(), dim2, dim1, dim0, tile, nt2, nt1, nt0, layer_begin, layer_end,
-          _ptr(out), _stream(dev))
+          _ptr(order), _ptr(out), _stream(dev))
     return out
 
 
 def fused_voxel_bwd(vsplats, offsets, flatten_ids, v_volume, N, dim2, dim1, dim0, tile, nt2, nt1,
-                    nt0, layer_begin=0, layer_end=None, rows=None):
+                    nt0, layer_begin=0, layer_end=None, rows=None, order=None):
     dev = vsplats.device
     if layer_end is None:
         layer_end = nt0
     stats = torch.empty((N, 12), dtype=torch.float32, device=dev)
     _call("r2s_voxel_splats_bwd_f32", _ptr(vsplats), _ptr(offsets), _ptr(flatten_ids), _ptr(rows),
           _ptr(v_volume), N, flatten_ids.numel(), dim2, dim1, dim0, tile, nt2, nt1, nt0,
-          layer_begin, layer_end, _ptr(stats), _stream(dev))
+          layer_begin, layer_end, _ptr(order), _ptr(stats), _stream(dev))
     return stats
 
 

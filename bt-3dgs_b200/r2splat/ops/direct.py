@@ -107,6 +107,8 @@ class VoxelForwardBuffers:
     # only, indexing this slab's flatten_ids, and output their voxel rows
     layer_begin: int = 0
     layer_end: Optional[int] = None
+    # float32: longest-first launch order of the bricks (r2s_brick_order)
+    order: Optional[torch.Tensor] = None
 
 
 def _fast(*tensors: torch.Tensor) -> bool:
@@ -340,15 +342,16 @@ def _voxelize_forward(
             offsets, flatten_ids, _ = W.fused_bin(rects, l1 - l0, N, nt1 * nt2, nt2, 1,
                                                   segment_base=l0)
             tile_offsets = offsets.view(l1 - l0, nt1, nt2)
+            order = W.fused_brick_order(offsets, flatten_ids.numel())
             rows = W.fused_voxel_rows(vsplats, tile_offsets, flatten_ids, N, dim2, dim1, dim0,
-                                      tile_size, nt2, nt1, nt0, l0, l1)
+                                      tile_size, nt2, nt1, nt0, l0, l1, order=order)
             output = W.fused_voxel_fwd(vsplats, tile_offsets, flatten_ids, N, dim2, dim1, dim0,
-                                       tile_size, nt2, nt1, nt0, l0, l1, rows=rows)
+                                       tile_size, nt2, nt1, nt0, l0, l1, rows=rows, order=order)
         return VoxelForwardBuffers(
             output=output, means3d=means3d, radii=radii, tile_offsets=tile_offsets,
             flatten_ids=flatten_ids, ranges=ranges_c, centers=centers_c, dim2=dim2, dim1=dim1,
             dim0=dim0, tile_size=tile_size, eps3d=float(eps3d), vsplats=vsplats, conics=conics,
-            opacity=opac, rows=rows, layer_begin=l0, layer_end=l1)
+            opacity=opac, rows=rows, layer_begin=l0, layer_end=l1, order=order)
 
     if z_layers is not None and (l0, l1) != (0, nt0):
         raise RuntimeError("z_layers (a z-slab of the grid) needs float32 inputs")

@@ -250,7 +250,7 @@ def _explicit_backward_fused(state, means, quats, raw_scales, raw_opacities,
                 vb.vsplats, vb.tile_offsets, vb.flatten_ids, vox.output.grad.contiguous(), N,
                 vb.dim2, vb.dim1, vb.dim0, vb.tile_size, vb.tile_offsets.size(2),
                 vb.tile_offsets.size(1), nt0, vb.layer_begin,
-                nt0 if vb.layer_end is None else vb.layer_end, rows=vb.rows)
+                nt0 if vb.layer_end is None else vb.layer_end, rows=vb.rows, order=vb.order)
 
         params = (means, quats, raw_scales, raw_opacities)
         accumulate = all(_inplace_grad_ok(p) for p in params)

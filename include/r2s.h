@@ -452,7 +452,16 @@ R2S_API int r2s_voxel_rows_f32(const float* vsplats, const int32_t* tile_offsets
                              const int32_t* flatten_ids, int64_t N, int64_t n_isects,
                              uint32_t dim2, uint32_t dim1, uint32_t dim0, uint32_t tile_size,
                              uint32_t nt2, uint32_t nt1, uint32_t nt0, uint32_t layer_begin,
-                             uint32_t layer_end, uint32_t* rows, r2s_stream_t stream);
+                             uint32_t layer_end, const int32_t* brick_order, uint32_t* rows,
+                             r2s_stream_t stream);
+/* Launch order of the bricks of a 3D binning (this build's scheduling; the
+ * reference launches bricks in key order): order [n_keys] = the brick keys
+ * (0 .. n_keys-1 of the binning's tile_offsets) grouped by floor(log2 of
+ * their record count), largest group first, empty bricks last -- an
+ * approximate longest-first order.  The three per-brick entry points take it
+ * as `brick_order` (NULL: key order); results do not depend on it. */
+R2S_API int r2s_brick_order(const int32_t* tile_offsets, int64_t n_keys, int64_t n_isects,
+                            int32_t* order, r2s_stream_t stream);
 /* Voxelize bricks [z_begin/8 .. ) from voxel splat records; `volume` points
  * at voxel row z_begin of a [dim0,dim1,dim2] grid (z-slab output).  `rows`:
  * the row table of the same binning, or NULL. */
@@ -460,8 +469,8 @@ R2S_API int r2s_voxel_splats_fwd_f32(const float* vsplats, const int32_t* tile_o
                              const int32_t* flatten_ids, const uint32_t* rows, int64_t N,
                              int64_t n_isects, uint32_t dim2, uint32_t dim1, uint32_t dim0,
                              uint32_t tile_size, uint32_t nt2, uint32_t nt1, uint32_t nt0,
-                             uint32_t layer_begin, uint32_t layer_end, float* volume,
-                             r2s_stream_t stream);
+                             uint32_t layer_begin, uint32_t layer_end,
+                             const int32_t* brick_order, float* volume, r2s_stream_t stream);
 /* Voxel backward statistics [N, 12] = (S0, Sx, Sy, Sz, Sxx, Sxy, Sxz, Syy,
  * Syz, Szz, 0, 0), accumulated over bricks; zeroes `stats` first.  `rows`:
  * the row table of the same binning, or NULL. */
@@ -470,8 +479,8 @@ R2S_API int r2s_voxel_splats_bwd_f32(const float* vsplats, const int32_t* tile_o
                              const float* v_volume, int64_t N,
                              int64_t n_isects, uint32_t dim2, uint32_t dim1, uint32_t dim0,
                              uint32_t tile_size, uint32_t nt2, uint32_t nt1, uint32_t nt0,
-                             uint32_t layer_begin, uint32_t layer_end, float* stats,
-                             r2s_stream_t stream);
+                             uint32_t layer_begin, uint32_t layer_end,
+                             const int32_t* brick_order, float* stats, r2s_stream_t stream);
 
 /* Whole explicit backward per Gaussian (explicit.py:233-385): converts the
  * raster statistics of every view to the reference's per-view gradients

@@ -45,3 +45,46 @@ def test_row_table_matches_box_culling(dims, layers):
     b = rows.view(torch.uint8).reshape(-1, 8).long()
     lo, hi = b & 15, b >> 4
     assert bool(((lo <= hi) & (hi <= 7) | (b == 0x0F)).all())
+
+
+@pytest.mark.parametrize("dims,layers", [((48, 48, 48), None), ((40, 40, 64), (3, 7))])
+def test_brick_order_is_a_longest_first_permutation(dims, layers):
+    """r2s_brick_order lists every brick once, in non-increasing
+    floor(log2(records)) groups; the row table, forward and backward launched
+    in that order give the key-order results (the forward bit for bit)."""
+    import r2s_workloads as wl
+    from r2splat.cuda import _wrapper as W
+
+    dim2, dim1, dim0 = dims
+    m, q, s, o = (t.cuda() for t in wl.make_gaussians(wl.CONFIGS[1], n=20000, seed=5))
+    cov, _, op = W.fused_prepare(q, s, o, wl.SCALE_MIN, wl.SCALE_MAX)
+    rng, ctr = (t.cuda() for t in wl.unit_cube_box())
+    nt2, nt1, nt0 = (dim2 + 7) // 8, (dim1 + 7) // 8, (dim0 + 7) // 8
+    _, _, _, vs, rects, _ = W.fused_map(m, cov, op, rng, ctr, dim2, dim1, dim0, 8, nt2, nt1, nt0,
+                                        wl.EPS3D, wl.RADIUS_CLIP)
+    l0, l1 = layers if layers else (0, nt0)
+    N = m.size(0)
+    offs, fids, _ = W.fused_bin(rects, l1 - l0, N, nt1 * nt2, nt2, 1, segment_base=l0)
+    order = W.fused_brick_order(offs, fids.numel())
+    n_keys = offs.numel()
+    assert torch.equal(order.sort().values.long(), torch.arange(n_keys, device="cuda"))
+    counts = torch.diff(torch.cat([offs.long(), torch.tensor([fids.numel()], device="cuda")]))
+    groups = torch.where(counts > 0, torch.floor(torch.log2(counts.clamp_min(1).double())) + 1,
+                         torch.zeros_like(counts, dtype=torch.float64))
+    g_ord = groups[order.long()]
+    assert bool((g_ord[:-1] >= g_ord[1:]).all()), "order is not longest-first by group"
+    args = (vs, offs, fids, N, dim2, dim1, dim0, 8, nt2, nt1, nt0, l0, l1)
+    rows_k = W.fused_voxel_rows(*args)
+    rows_o = W.fused_voxel_rows(*args, order=order)
+    assert torch.equal(rows_k, rows_o)
+    v_k = W.fused_voxel_fwd(*args, rows=rows_k)
+    v_o = W.fused_voxel_fwd(*args, rows=rows_o, order=order)
+    assert torch.equal(v_k, v_o) and v_k.abs().max() > 0
+    g = torch.Generator(device="cuda").manual_seed(3)
+    v_vol = torch.randn(v_k.shape, generator=g, device="cuda")
+    st_k = W.fused_voxel_bwd(vs, offs, fids, v_vol, N, dim2, dim1, dim0, 8, nt2, nt1, nt0, l0, l1,
+                             rows=rows_k)
+    st_o = W.fused_voxel_bwd(vs, offs, fids, v_vol, N, dim2, dim1, dim0, 8, nt2, nt1, nt0, l0, l1,
+                             rows=rows_o, order=order)
+    rel = ((st_o.double() - st_k.double()).norm() / st_k.double().norm()).item()
+    assert rel < 1e-6, rel
