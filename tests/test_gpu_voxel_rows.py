@@ -69,8 +69,8 @@ def test_brick_order_is_a_longest_first_permutation(dims, layers):
     n_keys = offs.numel()
     assert torch.equal(order.sort().values.long(), torch.arange(n_keys, device="cuda"))
     counts = torch.diff(torch.cat([offs.long(), torch.tensor([fids.numel()], device="cuda")]))
-    groups = torch.where(counts > 0, torch.floor(torch.log2(counts.clamp_min(1).double())) + 1,
-                         torch.zeros_like(counts, dtype=torch.float64))
+    # bit length of the count (floor(log2 c) + 1, 0 for empty bricks), exactly
+    groups = torch.frexp(counts.double()).exponent.long() * (counts > 0)
     g_ord = groups[order.long()]
     assert bool((g_ord[:-1] >= g_ord[1:]).all()), "order is not longest-first by group"
     args = (vs, offs, fids, N, dim2, dim1, dim0, 8, nt2, nt1, nt0, l0, l1)
