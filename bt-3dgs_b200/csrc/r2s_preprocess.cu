@@ -931,7 +931,7 @@ __global__ void explicit_bwd_kernel(
     const float4* __restrict__ rstats, float2* __restrict__ v_means2d,
     float2* __restrict__ v_means2d_abs, const float* __restrict__ ranges,
     const float* __restrict__ centers, uint32_t dim2, uint32_t dim1, uint32_t dim0, float eps3d,
-    const float4* __restrict__ vstats, int accumulate, float* __restrict__ out_means,
+    const double* __restrict__ vstats, int accumulate, float* __restrict__ out_means,
     float* __restrict__ out_quats, float* __restrict__ out_scales,
     float* __restrict__ out_opac, DensifyArgs dens) {
     const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -1006,8 +1006,12 @@ __global__ void explicit_bwd_kernel(
             dens.max_radii[g] = fmaxf(dens.max_radii[g], d_rmax);
     }
     if (vstats != nullptr) {
-        const float4 t0 = vstats[g * 3], t1 = vstats[g * 3 + 1], t2 = vstats[g * 3 + 2];
-        // (S0, Sx, Sy, Sz | Sxx, Sxy, Sxz, Syy | Syz, Szz, -, -)
+        // float64 sums (S0, Sx, Sy, Sz | Sxx, Sxy, Sxz, Syy | Syz, Szz, -, -), each
+        // rounded once to float
+        const double* vs = vstats + g * 12;
+        const float4 t0 = make_float4((float)vs[0], (float)vs[1], (float)vs[2], (float)vs[3]);
+        const float4 t1 = make_float4((float)vs[4], (float)vs[5], (float)vs[6], (float)vs[7]);
+        const float4 t2 = make_float4((float)vs[8], (float)vs[9], 0.f, 0.f);
         VolMap<float> o;
         vol_map(means + g * 3, cov3, ranges, centers, dim2, dim1, dim0, eps3d, o);
         float P[6];
@@ -1240,7 +1244,7 @@ int explicit_backward_launch(
     double smin, double smax, const float* viewmats, const float* Ks, int64_t C, int64_t N,
     uint32_t width, uint32_t height, double eps2d, const float* raster_stats, float* v_means2d,
     float* v_means2d_abs, const float* ranges, const float* centers, uint32_t dim2,
-    uint32_t dim1, uint32_t dim0, double eps3d, const float* vox_stats, int accumulate,
+    uint32_t dim1, uint32_t dim0, double eps3d, const double* vox_stats, int accumulate,
     float* v_means, float* v_quats, float* v_raw_scales, float* v_raw_opacities,
     const r2s_densify_args* densify, r2s_stream_t stream) {
     R2S_REQUIRE(C >= 0 && N >= 0, "explicit_backward: negative size");
@@ -1266,7 +1270,7 @@ int explicit_backward_launch(
         means, quats, raw_scales, raw_opacities, (float)smin, (float)smax, viewmats, Ks, C, N,
         width, height, (float)eps2d, (const float4*)raster_stats, (float2*)v_means2d,
         (float2*)v_means2d_abs, ranges, centers, dim2, dim1, dim0, (float)eps3d,
-        (const float4*)vox_stats, accumulate, v_means, v_quats, v_raw_scales, v_raw_opacities,
+        vox_stats, accumulate, v_means, v_quats, v_raw_scales, v_raw_opacities,
         dens);
     return check_launch("explicit_backward");
 }
@@ -1277,7 +1281,7 @@ extern "C" int r2s_explicit_backward_f32(
     double smin, double smax, const float* viewmats, const float* Ks, int64_t C, int64_t N,
     uint32_t width, uint32_t height, double eps2d, const float* raster_stats, float* v_means2d,
     float* v_means2d_abs, const float* ranges, const float* centers, uint32_t dim2,
-    uint32_t dim1, uint32_t dim0, double eps3d, const float* vox_stats, int accumulate,
+    uint32_t dim1, uint32_t dim0, double eps3d, const double* vox_stats, int accumulate,
     float* v_means, float* v_quats, float* v_raw_scales, float* v_raw_opacities,
     r2s_stream_t stream) {
     return explicit_backward_launch(means, quats, raw_scales, raw_opacities, smin, smax, viewmats,
@@ -1292,7 +1296,7 @@ extern "C" int r2s_explicit_backward_densify_f32(
     double smin, double smax, const float* viewmats, const float* Ks, int64_t C, int64_t N,
     uint32_t width, uint32_t height, double eps2d, const float* raster_stats, float* v_means2d,
     float* v_means2d_abs, const float* ranges, const float* centers, uint32_t dim2,
-    uint32_t dim1, uint32_t dim0, double eps3d, const float* vox_stats, int accumulate,
+    uint32_t dim1, uint32_t dim0, double eps3d, const double* vox_stats, int accumulate,
     float* v_means, float* v_quats, float* v_raw_scales, float* v_raw_opacities,
     const r2s_densify_args* densify, r2s_stream_t stream) {
     R2S_REQUIRE(densify != nullptr, "explicit_backward_densify: null densify arguments");

@@ -40,6 +40,7 @@
 #include "r2s_common.cuh"
 #include "r2s_cull.cuh"
 #include "r2s_debug.cuh"
+#include "r2s_refexpr.cuh"
 
 namespace r2s {
 
@@ -466,6 +467,38 @@ __device__ __forceinline__ float s_threshold(float wmu) {
     return a >= 1.0f ? log2f(a) : -1.0f;  // negative: nothing passes
 }
 
+// Exact cut-off decisions in the backward.  The backward evaluates the
+// shifted exponent z = s_thr - s (s_thr added in the chain's last FMA) and
+// keeps a pixel when z >= 0; the reference's test (sigma from its own
+// expression tree, __expf, alpha = (w mu) vis >= 1e-5: ref_keep2d) agrees
+// except for pixels whose s lies within the sum of both evaluations' rounding
+// errors of s_thr.  Bound, in log2 units with u = 2^-24 and
+// M = log2(e) (|a| dx^2 / 2 + |b dx dy| + |c| dy^2 / 2) the magnitude of the
+// quadratic's terms:
+//   z: three rounded coefficients, five roundings of partial sums (the last
+//     one of a value near 0 at the cut-off)                        <= 8 u M + u s
+//   reference sigma: six roundings                                      <= 6 u M
+//   reference __expf(x), x ~ -s ln2: at most 2 + floor(1.173 |x|) ulp (the
+//     CUDA intrinsic's documented bound), then alpha = w mu * vis (one ulp)
+//                                                                    <= (9 + 2.4 s) u
+//   threshold: |w mu| * 1e5 rounded, log2f (fast math, <= 2^-20 absolute),
+//     1e-5f against 1/1e5                                                <= 24 u
+// i.e. |z - z_ref| <= u (14 M + 3.4 s_thr + 33).  The band is |z| <= delta
+// with twice that, delta = u (32 M + 8 s_thr + 100).  M is bounded over the
+// pixels that can lie near the cut-off: |dx| <= Dx, |dy| <= Dy, the smaller of
+// the record's culling extents (the ellipse at the cut-off, widened by
+// margins for rounding) and the largest offsets of the tile's pixel centres
+// from the mean; a pixel outside the extents is dropped by both tests.  A
+// pixel in the band is re-decided by ref_keep2d; every other pixel is decided
+// alike by both tests.
+__device__ __forceinline__ float cutoff_band(float a, float b, float c, float s_thr, float Dx,
+                                             float Dy) {
+    const float M = kLog2e * (0.5f * fabsf(a) * Dx * Dx + fabsf(b) * Dx * Dy +
+                              0.5f * fabsf(c) * Dy * Dy);
+    const float d = (32.0f * M + 8.0f * fabsf(s_thr) + 100.0f) * 0x1p-24f;
+    return d < 1e30f ? d : CUDART_INF_F;  // NaN: every pixel in the band
+}
+
 // Culling ranges of one (record, tile) pair after tile_cull, 4 bits each:
 // c_lo | c_hi << 4 | r_lo << 8 | r_hi << 12 (an empty range stays empty).
 __device__ __forceinline__ uint16_t pack_cull(int c_lo, int c_hi, int r_lo, int r_hi) {
@@ -685,6 +718,9 @@ raster_bwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict
     __shared__ uint16_t s_perm[kBwd16Batch];
     __shared__ int32_t s_cnt[257];
     __shared__ int32_t s_wsum[kBwd16Threads / 32];
+    __shared__ uint16_t s_fix[kBwd16Batch];  // records with a pixel in the cut-off band
+    __shared__ int s_nfix;
+    __shared__ float s_fx[kBwd16Threads / 32][8];
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int64_t cam = blockIdx.z;
@@ -707,7 +743,7 @@ raster_bwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict
     for (int base = start; base < end; base += kBwd16Batch) {
         // stage the batch; bucket 256 holds records that reach no pixel
         s_cnt[tid] = 0;
-        if (tid == 0) s_cnt[256] = 0;
+        if (tid == 0) s_cnt[256] = 0, s_nfix = 0;
         __syncthreads();
         constexpr int kPer = kBwd16Batch / kBwd16Threads;
         int bucket[kPer], rank[kPer];
@@ -736,6 +772,13 @@ raster_bwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict
                               r_lo, r_hi);
                 }
                 if (c_lo <= c_hi && r_lo <= r_hi) {
+                    // cut-off band of the record: a pixel near the cut-off lies
+                    // inside the record's culling extents (q.z, q.w) and the tile
+                    const float Dx = fminf(q.z, fmaxf(fabsf((X0f + 0.5f) - p.x),
+                                                      fabsf((X0f + 15.5f) - p.x)));
+                    const float Dy = fminf(q.w, fmaxf(fabsf((Y0f + 0.5f) - p.y),
+                                                      fabsf((Y0f + 15.5f) - p.y)));
+                    const float band = cutoff_band(p.z, p.w, q.x, s_threshold(q.y), Dx, Dy);
                     if (c_hi - c_lo < r_hi - r_lo) {
                         // fewer columns than rows: walk the columns, with the
                         // record transposed (x <-> y, a <-> c) and flagged in
@@ -747,6 +790,7 @@ raster_bwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict
                         r_hi = c_hi;
                         g = (int32_t)((uint32_t)g | 0x80000000u);
                     }
+                    q.z = band;
                     bucket[k] = r_lo * 16 + r_hi;
                     rows = r_lo | (r_hi << 4);
                 }
@@ -791,10 +835,15 @@ raster_bwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict
             const float* const vb = tr ? s_vT : s_v;
             const float4 p = s_p[idx], q = s_q[idx];
 
-            // negated coefficients: the packed chain yields -s exactly (see the
-            // forward kernel for the cut-off test on the bits of -s)
+            // negated coefficients; the packed chain yields z = s_thr - s (the
+            // threshold enters the last FMA through the row term): a pixel is
+            // kept when z >= 0 and lies in the cut-off band when |z| <= q.z
+            // (tested once per record on the smallest |z| of the walk).  The
+            // sums run over 2^z = 2^s_thr e^-sigma and are scaled back by
+            // 2^-s_thr once per record.
             const float A = -0.5f * kLog2e * p.z, B = -kLog2e * p.w, Cc = -0.5f * kLog2e * q.x;
-            const int thr_n = (int)(__float_as_uint(s_threshold(q.y)) ^ 0x80000000u);
+            const float s_thr = s_threshold(q.y);
+            float z_min = CUDART_INF_F;
             const float2 A2 = make_float2(A, A);
             const float2 a2 = make_float2(p.z, p.z), b2 = make_float2(p.w, p.w);
             float2 dx[8], col[8];
@@ -807,7 +856,7 @@ raster_bwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict
             for (int r = row0; r <= row1; ++r) {
                 const bool rin = r >= r_lo && r <= r_hi;
                 const float dy = (Vo + ((float)r + 0.5f)) - p.y;
-                const float by = B * dy, cyy = Cc * dy * dy;
+                const float by = B * dy, cyy = fmaf(Cc * dy, dy, s_thr);
                 const float2 by2 = make_float2(by, by), cyy2 = make_float2(cyy, cyy);
                 const float bdy = p.w * dy, cdy = q.x * dy;
                 const float2 bdy2 = make_float2(bdy, bdy), cdy2 = make_float2(cdy, cdy);
@@ -821,10 +870,11 @@ raster_bwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict
                         const int j = 2 * j4 + h;
                         const float2 v2 = h ? make_float2(v4.z, v4.w) : make_float2(v4.x, v4.y);
                         const float2 t = ffma2(A2, dx[j], by2);
-                        const float2 sn = ffma2(dx[j], t, cyy2);  // -s
-                        float e0 = exp2f(sn.x), e1 = exp2f(sn.y);
-                        e0 = (rin && __float_as_int(sn.x) <= thr_n) ? e0 : 0.f;
-                        e1 = (rin && __float_as_int(sn.y) <= thr_n) ? e1 : 0.f;
+                        const float2 z = ffma2(dx[j], t, cyy2);  // s_thr - s
+                        float e0 = exp2f(z.x), e1 = exp2f(z.y);
+                        z_min = fminf(z_min, fminf(fabsf(z.x), fabsf(z.y)));
+                        e0 = (rin && z.x >= 0.f) ? e0 : 0.f;
+                        e1 = (rin && z.y >= 0.f) ? e1 : 0.f;
                         const float2 ve = fmul2(v2, make_float2(e0, e1));
                         col[j] = fadd2(col[j], ve);
                         r0 = fadd2(r0, ve);
@@ -845,6 +895,7 @@ raster_bwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict
                 Sxy = fmaf(dy, R1, Sxy);
             }
             if (!live) continue;
+            if (!(z_min > q.z)) s_fix[atomicAdd(&s_nfix, 1)] = (uint16_t)idx;  // also NaN
             float S0 = 0.f, Sx = 0.f, Sxx = 0.f;
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
@@ -853,6 +904,10 @@ raster_bwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict
                 Sx += cx.x + cx.y;
                 Sxx = fmaf(cx.x, dx[j].x, Sxx);
                 Sxx = fmaf(cx.y, dx[j].y, Sxx);
+            }
+            {  // 2^-s_thr: the sums back to e^-sigma
+                const float k = exp2f(-s_thr);
+                S0 *= k, Sx *= k, Sy *= k, Sxx *= k, Sxy *= k, Syy *= k, Ax *= k, Ay *= k;
             }
             if (tr) {  // back to image axes
                 float t = Sx;
@@ -868,6 +923,71 @@ raster_bwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict
                 red_add_v4(st + 4, Sxy, Syy, Ax, Ay);
             else
                 red_add_v2(st + 4, Sxy, Syy);
+        }
+        __syncthreads();
+        // records with a pixel in the cut-off band: every pixel of the walk
+        // re-decided by the reference's own test, one pixel per thread; where
+        // the decisions differ, the pixel's moments are added or taken back
+        const int n_fix = s_nfix;
+        for (int f = 0; f < n_fix; ++f) {
+            const int idx = s_fix[f];
+            const int32_t gi = s_g[idx];
+            const bool tr = gi < 0;
+            const float4 p = s_p[idx], q = s_q[idx];
+            const int r_lo = s_rows[idx] & 15, r_hi = s_rows[idx] >> 4;
+            const int rw = tid >> 4, cw = tid & 15;  // walked row and column
+            // the main loop's fast decision, operation for operation
+            const float Uo = tr ? Y0f : X0f, Vo = tr ? X0f : Y0f;
+            const float A = -0.5f * kLog2e * p.z, B = -kLog2e * p.w, Cc = -0.5f * kLog2e * q.x;
+            const float s_thr = s_threshold(q.y);
+            const float dx = (Uo + ((float)cw + 0.5f)) - p.x;
+            const float dy = (Vo + ((float)rw + 0.5f)) - p.y;
+            const float by = B * dy, cyy = fmaf(Cc * dy, dy, s_thr);
+            const float z = fmaf(dx, fmaf(A, dx, by), cyy);
+            const bool fast = rw >= r_lo && rw <= r_hi && z >= 0.f;
+            // the reference's decision, in image axes
+            const int i = tr ? cw : rw, j = tr ? rw : cw;
+            const bool inside = i <= rmax && j <= cmax;
+            const float mx = tr ? p.y : p.x, my = tr ? p.x : p.y;
+            const float ca = tr ? q.x : p.z, cc = tr ? p.z : q.x;
+            const bool exact = inside && ref_keep2d(ca, p.w, cc, q.y, (X0f + ((float)j + 0.5f)) - mx,
+                                                    (Y0f + ((float)i + 0.5f)) - my);
+            const bool diff = inside && fast != exact;
+            float m[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            if (diff) {
+                const float sgn = exact ? 1.0f : -1.0f;
+                const float ve = (tr ? s_vT : s_v)[rw * 16 + cw] * (exp2f(z) * exp2f(-s_thr));
+                m[0] = sgn * ve;
+                m[1] = sgn * ve * dx;
+                m[2] = sgn * ve * dy;
+                m[3] = sgn * ve * dx * dx;
+                m[4] = sgn * ve * dx * dy;
+                m[5] = sgn * ve * dy * dy;
+                m[6] = sgn * fabsf(ve) * fabsf(fmaf(p.z, dx, p.w * dy));
+                m[7] = sgn * fabsf(ve) * fabsf(fmaf(p.w, dx, q.x * dy));
+                if (tr) {  // back to image axes
+                    float t = m[1];
+                    m[1] = m[2], m[2] = t;
+                    t = m[3];
+                    m[3] = m[5], m[5] = t;
+                    t = m[6];
+                    m[6] = m[7], m[7] = t;
+                }
+            }
+            if (!__syncthreads_or(diff)) continue;  // CTA-uniform
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const float v = warp_sum(m[k]);
+                if (lane == 0) s_fx[warp][k] = v;
+            }
+            __syncthreads();
+            // stats layout: S0, Sx, Sy, Sxx, Sxy, Syy (, Ax, Ay)
+            if (tid < (WITH_ABS ? 8 : 6)) {
+                float v = 0.f;
+#pragma unroll
+                for (int w = 0; w < kBwd16Threads / 32; ++w) v += s_fx[w][tid];
+                atomicAdd(stats + (gi & 0x7fffffff) * (int64_t)8 + tid, v);
+            }
         }
         __syncthreads();
     }

@@ -14,7 +14,8 @@
 // the compiler contracts it differently; the variants below fix the order of
 // every rounding with explicit intrinsics, so that a test can find the one
 // that reproduces the reference's values bit for bit
-// (tests/test_gpu_refexpr.py).
+// (tests/test_gpu_refexpr.py).  The raster backward decides the pixels
+// within rounding of the cut-off with ref_keep2d (r2s_raster.cu).
 #pragma once
 
 #include <cuda_runtime.h>
@@ -74,6 +75,18 @@ __device__ __forceinline__ float ref_alpha2d(int variant, float a, float b, floa
     const float sigma = ref_sigma2d(variant, a, b, c, dx, dy);
     const float alpha = wmu * __expf(-sigma);
     return (sigma < 0.f || fabsf(alpha) < 1e-5f) ? 0.f : alpha;
+}
+
+// The reference's keep/drop decision for a (Gaussian, pixel) pair, bit for
+// bit: variant 2, the one tests/test_gpu_refexpr.py finds exact for both the
+// reference's forward and its backward.  wmu = opacity * mu (one rounded
+// product, as the reference's `opac * mu * vis` forms it); dx, dy the pixel
+// centre minus the mean.  A NaN alpha is kept, like the reference's test.
+__device__ __forceinline__ bool ref_keep2d(float a, float b, float c, float wmu, float dx,
+                                           float dy) {
+    const float sigma = ref_sigma2d_v2(a, b, c, dx, dy);
+    const float alpha = wmu * __expf(-sigma);
+    return !(sigma < 0.f || fabsf(alpha) < 1e-5f);
 }
 
 }  // namespace r2s

@@ -297,13 +297,25 @@ __device__ __forceinline__ void vstats_red(S* dst, const S v[10]) {
         for (int k = 0; k < 10; ++k) atomicAdd(dst + k, v[k]);
     }
 }
+// float moments into the float64 per-Gaussian sums of the fused path: the
+// sum over a Gaussian's bricks is then exact to ~1e-16 whatever order the
+// atomics land in, so repeated or differently sharded runs agree
+__device__ __forceinline__ void vstats_red(double* dst, const float v[10]) {
+#pragma unroll
+    for (int k = 0; k < 10; ++k) atomicAdd(dst + k, (double)v[k]);
+}
+
+// per-Gaussian statistics of the voxel backward: float64 for the fused
+// path (splat records), the input type for the reference-layout wrappers
+template <typename S, bool SPLATS>
+using VStat = typename std::conditional<SPLATS, double, S>::type;
 
 template <typename S, bool SPLATS, int EXPMODE>
 __global__ void voxel_bwd_kernel(VoxSrc<S> src, const int32_t* __restrict__ offsets,
                                  const int32_t* __restrict__ flatten_ids, int64_t n_keys,
                                  int64_t n_isects, const S* __restrict__ v_vol, uint32_t dim2,
                                  uint32_t dim1, uint32_t dim0, int T, uint32_t nt2, uint32_t nt1,
-                                 uint32_t layer_begin, S* __restrict__ stats) {
+                                 uint32_t layer_begin, VStat<S, SPLATS>* __restrict__ stats) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int nthr = blockDim.x;
     const int TT = T * T, TTT = T * T * T;
@@ -730,7 +742,7 @@ voxel_bwd8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict_
                   int64_t n_keys, int64_t n_isects, int64_t n_splats,
                   const float* __restrict__ v_vol, uint32_t dim2, uint32_t dim1, uint32_t dim0,
                   uint32_t nt2, uint32_t nt1, uint32_t layer_begin,
-                  const int32_t* __restrict__ order, float* __restrict__ stats) {
+                  const int32_t* __restrict__ order, double* __restrict__ stats) {
     __shared__ __align__(16) float s_v[512];
     __shared__ uint2 s_tab[kVBwd8Batch];     // per-slice rows (byte k: first | last << 4)
     __shared__ int32_t s_g[kVBwd8Batch];
@@ -904,10 +916,8 @@ voxel_bwd8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict_
                 Sxx = fmaf(cx.x, dx[j].x, Sxx);
                 Sxx = fmaf(cx.y, dx[j].y, Sxx);
             }
-            float* st = stats + g * 12;
-            red_add_v4(st, S0, Sx, Sy, Sz);
-            red_add_v4(st + 4, Sxx, Sxy, Sxz, Syy);
-            red_add_v2(st + 8, Syz, Szz);
+            const float m[10] = {S0, Sx, Sy, Sz, Sxx, Sxy, Sxz, Syy, Syz, Szz};
+            vstats_red(stats + g * 12, m);
                 };
         int grp = warp;
         while (grp < n_groups) {
@@ -976,8 +986,8 @@ template <typename S, bool SPLATS, int EXPMODE>
 int launch_voxel_bwd(const VoxSrc<S>& src, const int32_t* offsets, const int32_t* flatten_ids,
                      const S* v_vol, int64_t N, int64_t n_isects, uint32_t dim2, uint32_t dim1,
                      uint32_t dim0, uint32_t T, uint32_t nt2, uint32_t nt1, uint32_t layer_begin,
-                     uint32_t layer_end, S* stats, cudaStream_t stream) {
-    cudaMemsetAsync(stats, 0, (size_t)N * 12 * sizeof(S), stream);
+                     uint32_t layer_end, VStat<S, SPLATS>* stats, cudaStream_t stream) {
+    cudaMemsetAsync(stats, 0, (size_t)N * 12 * sizeof(VStat<S, SPLATS>), stream);
     if (n_isects == 0) return check_launch("voxelize_to_voxels_bwd");
     const int nthr = 256;
     const size_t smem = al16v((size_t)T * T * T * sizeof(S)) + 10 * al16v((size_t)nthr * sizeof(S)) +
@@ -1117,14 +1127,14 @@ extern "C" int r2s_voxel_splats_bwd_f32(const float* vsplats, const int32_t* off
                                         int64_t N, int64_t n_isects, uint32_t dim2, uint32_t dim1,
                                         uint32_t dim0, uint32_t T, uint32_t nt2, uint32_t nt1,
                                         uint32_t nt0, uint32_t layer_begin, uint32_t layer_end,
-                                        const int32_t* brick_order, float* stats,
+                                        const int32_t* brick_order, double* stats,
                                         r2s_stream_t stream) {
     R2S_REQUIRE(N >= 0 && n_isects >= 0, "voxel_splats_bwd: negative size");
     R2S_REQUIRE(layer_begin <= layer_end && layer_end <= nt0, "voxel_splats_bwd: bad layer range");
     if (int rc = check_bricks(T, nt2, nt1, nt0)) return rc;
     if (N == 0) return R2S_OK;
     if (T == 8) {
-        cudaMemsetAsync(stats, 0, (size_t)N * 12 * sizeof(float), stream);
+        cudaMemsetAsync(stats, 0, (size_t)N * 12 * sizeof(double), stream);
         if (n_isects > 0 && layer_end > layer_begin) {
             const dim3 grid(nt2, nt1, layer_end - layer_begin);
             voxel_bwd8_kernel<<<grid, kVBwd8Threads, 0, stream>>>(

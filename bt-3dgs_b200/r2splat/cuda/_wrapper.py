@@ -791,10 +791,12 @@ def fused_voxel_fwd(vsplats, offsets, flatten_ids, N, dim2, dim1, dim0, tile, nt
 
 def fused_voxel_bwd(vsplats, offsets, flatten_ids, v_volume, N, dim2, dim1, dim0, tile, nt2, nt1,
                     nt0, layer_begin=0, layer_end=None, rows=None, order=None):
+    """Voxel backward statistics [N, 12], float64 per-Gaussian sums
+    (r2s_voxel_splats_bwd_f32), the input of fused_explicit_backward."""
     dev = vsplats.device
     if layer_end is None:
         layer_end = nt0
-    stats = torch.empty((N, 12), dtype=torch.float32, device=dev)
+    stats = torch.empty((N, 12), dtype=torch.float64, device=dev)
     _call("r2s_voxel_splats_bwd_f32", _ptr(vsplats), _ptr(offsets), _ptr(flatten_ids), _ptr(rows),
           _ptr(v_volume), N, flatten_ids.numel(), dim2, dim1, dim0, tile, nt2, nt1, nt0,
           layer_begin, layer_end, _ptr(order), _ptr(stats), _stream(dev))
@@ -807,7 +809,10 @@ def fused_explicit_backward(means, quats, raw_scales, raw_opacities, scale_min, 
                             densify=None):
     """``densify``: None, or (radii [C,N,2] int32, scale_x, scale_y, extent,
     absgrad, grad2d [N], count [N], max_radii [N] or None) for the fused
-    densification statistics."""
+    densification statistics.  ``vox_stats``: the float64 output of
+    fused_voxel_bwd, or None."""
+    _require(vox_stats is None or vox_stats.dtype == torch.float64,
+             "vox_stats must be the float64 statistics of fused_voxel_bwd")
     dev = means.device
     C = 0 if viewmats is None else viewmats.size(0)
     N = means.size(0)

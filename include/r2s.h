@@ -471,16 +471,19 @@ R2S_API int r2s_voxel_splats_fwd_f32(const float* vsplats, const int32_t* tile_o
                              uint32_t tile_size, uint32_t nt2, uint32_t nt1, uint32_t nt0,
                              uint32_t layer_begin, uint32_t layer_end,
                              const int32_t* brick_order, float* volume, r2s_stream_t stream);
-/* Voxel backward statistics [N, 12] = (S0, Sx, Sy, Sz, Sxx, Sxy, Sxz, Syy,
- * Syz, Szz, 0, 0), accumulated over bricks; zeroes `stats` first.  `rows`:
- * the row table of the same binning, or NULL. */
+/* Voxel backward statistics [N, 12] float64 = (S0, Sx, Sy, Sz, Sxx, Sxy, Sxz,
+ * Syy, Syz, Szz, 0, 0): each brick's float moments added into float64
+ * per-Gaussian sums, so that the result does not depend on the order of the
+ * additions (runs, brick orders and z-slab splits agree to ~1e-16);
+ * zeroes `stats` first.  `rows`: the row table of the same binning, or
+ * NULL. */
 R2S_API int r2s_voxel_splats_bwd_f32(const float* vsplats, const int32_t* tile_offsets,
                              const int32_t* flatten_ids, const uint32_t* rows,
                              const float* v_volume, int64_t N,
                              int64_t n_isects, uint32_t dim2, uint32_t dim1, uint32_t dim0,
                              uint32_t tile_size, uint32_t nt2, uint32_t nt1, uint32_t nt0,
                              uint32_t layer_begin, uint32_t layer_end,
-                             const int32_t* brick_order, float* stats, r2s_stream_t stream);
+                             const int32_t* brick_order, double* stats, r2s_stream_t stream);
 
 /* Whole explicit backward per Gaussian (explicit.py:233-385): converts the
  * raster statistics of every view to the reference's per-view gradients
@@ -490,14 +493,15 @@ R2S_API int r2s_voxel_splats_bwd_f32(const float* vsplats, const int32_t* tile_o
  * parameter_transform_bwd and the softplus chain for opacities.  Outputs
  * v_means [N,3], v_quats [N,4], v_raw_scales [N,3], v_raw_opacities [N];
  * with accumulate != 0 they are added to the existing contents.
- * raster_stats / vox_stats may be NULL (that path had no upstream gradient). */
+ * raster_stats / vox_stats may be NULL (that path had no upstream gradient);
+ * vox_stats is the float64 output of r2s_voxel_splats_bwd_f32. */
 R2S_API int r2s_explicit_backward_f32(
     const float* means, const float* quats, const float* raw_scales,
     const float* raw_opacities, double scale_min, double scale_max, const float* viewmats,
     const float* Ks, int64_t C, int64_t N, uint32_t width, uint32_t height, double eps2d,
     const float* raster_stats, float* v_means2d, float* v_means2d_abs, const float* ranges,
     const float* centers, uint32_t dim2, uint32_t dim1, uint32_t dim0, double eps3d,
-    const float* vox_stats, int accumulate, float* v_means, float* v_quats,
+    const double* vox_stats, int accumulate, float* v_means, float* v_quats,
     float* v_raw_scales, float* v_raw_opacities, r2s_stream_t stream);
 
 /* Densification statistics of BinaryTreeStrategy._update_state
@@ -529,7 +533,7 @@ R2S_API int r2s_explicit_backward_densify_f32(
     const float* Ks, int64_t C, int64_t N, uint32_t width, uint32_t height, double eps2d,
     const float* raster_stats, float* v_means2d, float* v_means2d_abs, const float* ranges,
     const float* centers, uint32_t dim2, uint32_t dim1, uint32_t dim0, double eps3d,
-    const float* vox_stats, int accumulate, float* v_means, float* v_quats,
+    const double* vox_stats, int accumulate, float* v_means, float* v_quats,
     float* v_raw_scales, float* v_raw_opacities, const r2s_densify_args* densify,
     r2s_stream_t stream);
 

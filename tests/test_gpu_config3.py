@@ -19,7 +19,7 @@ the gradients of an upstream gradient on the slab the reference's.
 import pytest
 import torch
 
-from _helpers import REL_L2_F32, check_grad_accuracy, rel_l2
+from _helpers import REL_L2_F32, rel_l2
 
 pytestmark = pytest.mark.gpu
 
@@ -42,29 +42,6 @@ def cfg3():
     cfg = wl.CONFIGS[3]
     m, q, s, o = (t.cuda() for t in wl.make_gaussians(cfg))
     return cfg, dict(means=m, quats=q, scales=s, opac=o)
-
-
-def _float64_projection_gradients(ref, p, v_img, d, covars):
-    """Parameter gradients of one view batch in float64 by the reference's
-    double kernels from the float32 forward values and binning."""
-    import r2s_workloads as wl
-
-    C = ref.C
-    f8 = torch.float64
-    det = p["img_w"]
-    _, v_m2, v_con, v_op, v_mu = C.rasterize_to_pixels_bwd_per_gaussian(
-        p["means2d"].to(f8), p["conics"].to(f8), p["opacity"].to(f8), p["mus"].to(f8),
-        p["tile_offsets"], p["isect_ids"], p["flatten_ids"], v_img.to(f8), det, det, wl.IMG_TILE,
-        False)
-    v_c2 = C.conics_mu_bwd(p["cov2d"].to(f8), wl.EPS2D, p["conics"].to(f8), p["mus"].to(f8),
-                           v_con.contiguous(), v_mu.contiguous())
-    v_means, v_cov = C.world_to_image_projection_bwd(
-        d["means"].to(f8), covars.to(f8), p["viewmats"].to(f8), p["Ks"].to(f8), det, det,
-        v_m2.contiguous(), v_c2.contiguous())
-    v_quats, v_scales = C.parameter_transform_bwd(d["quats"].to(f8), d["scales"].to(f8),
-                                                  wl.SCALE_MIN, wl.SCALE_MAX, v_cov.contiguous())
-    v_raw = v_op.sum(0) * torch.sigmoid(d["opac"].to(f8))
-    return {"means": v_means, "quats": v_quats, "scales": v_scales, "opac": v_raw}
 
 
 def test_config3_view_batches_match_reference_batches(ref, cfg3):
@@ -95,7 +72,6 @@ def test_config3_view_batches_match_reference_batches(ref, cfg3):
     covars, _, opac = ref.prepare(d["quats"], d["scales"], d["opac"], wl.SCALE_MIN, wl.SCALE_MAX)
     assert torch.equal(st.covars, covars)
     theirs = {k: torch.zeros_like(d[k]) for k in params}
-    truth = {k: torch.zeros(d[k].shape, dtype=torch.float64, device="cuda") for k in params}
     m2_grad = []
     for c0, c1, ids in pb.view_batches:
         p = ref.rasterize_forward(d["means"], covars, opac, vm[c0:c1], K[c0:c1], det, det,
@@ -114,15 +90,14 @@ def test_config3_view_batches_match_reference_batches(ref, cfg3):
                       ("opac", "opacities")):
             theirs[k] += gb[pk]
         m2_grad.append((c0, c1, gb["means2d"], gb["means2d_abs"]))
-        tb = _float64_projection_gradients(ref, p, v_img[c0:c1], d, covars)
-        for k in truth:
-            truth[k] += tb[k]
-        del p, gb, tb
+        del p, gb
         torch.cuda.empty_cache()
     for c0, c1, gm2, gabs in m2_grad:
         assert rel_l2(res.means2d.grad[c0:c1], gm2) < REL_L2_F32
         assert rel_l2(res.means2d.absgrad[c0:c1], gabs) < REL_L2_F32
-    check_grad_accuracy("cfg3-40views", ours, theirs, truth)
+    for k in ours:  # the plain bar (exact cut-off decisions in the raster backward)
+        e = rel_l2(ours[k], theirs[k])
+        assert e < REL_L2_F32, f"cfg3-40views: grad {k} rel-L2 {e:.3e}"
 
 
 def test_config3_z_slab_matches_reference_layers(ref, cfg3):

@@ -13,7 +13,7 @@ import os
 import pytest
 import torch
 
-from _helpers import REL_L2_F32, check_grad_accuracy, rel_l2
+from _helpers import REL_L2_F32, rel_l2
 
 pytestmark = pytest.mark.gpu
 
@@ -231,21 +231,22 @@ def test_fused_op_layer_matches_reference_pipeline(ref, case):
     E.explicit_backward(state, params["means"], params["quats"], params["scales"], params["opac"])
     theirs = ref.explicit_backward(p, v_img, v, v_vol, d["means"], d["quats"], d["scales"], d["opac"],
                                    covars, opac, wl.SCALE_MIN, wl.SCALE_MAX, absgrad=True)
-    pairs = (("means", "means"), ("quats", "quats"), ("scales", "scales"), ("opac", "opacities"))
-    if name in NOISE_LIMITED:
-        truth = _float64_gradients(ref, d, p, v_img, v, v_vol, covars)
-        check_grad_accuracy(name, {k: params[k].grad for k, _ in pairs},
-                            {k: theirs[pk] for k, pk in pairs}, truth)
-    else:
-        for key, pk in pairs:
-            e = rel_l2(params[key].grad, theirs[pk])
-            assert e < REL_L2_F32, f"{name}: grad {key} rel-L2 {e:.3e}"
+    # every case at the plain bar: the raster backward decides the pixels at
+    # the cut-off exactly like the reference (ref_keep2d) and the voxel
+    # statistics are float64 sums
+    for key, pk in (("means", "means"), ("quats", "quats"), ("scales", "scales"),
+                    ("opac", "opacities")):
+        e = rel_l2(params[key].grad, theirs[pk])
+        assert e < REL_L2_F32, f"{name}: grad {key} rel-L2 {e:.3e}"
     assert rel_l2(res.means2d.grad, theirs["means2d"]) < REL_L2_F32
     assert rel_l2(res.means2d.absgrad, theirs["means2d_abs"]) < REL_L2_F32
 
 
-# cases whose parameter gradients are limited by float32 summation noise
-NOISE_LIMITED = {"cfg2-4views", "cfg2-75views"}
+# cases where a z-slab's gradient alone is dominated by the voxel cut-off
+# decisions (pixels within rounding of |alpha| = 1e-6, decided by each build
+# its own way): the slab is compared with the reference there only through
+# the full-grid test above
+VOXEL_DECISION_LIMITED = {"cfg2-4views", "cfg2-75views"}
 
 
 def _float64_gradients(ref, d, p, v_img, v, v_vol, covars):
@@ -354,13 +355,12 @@ def test_explicit_voxelize_z_slab_matches_full_grid_and_reference(ref, case):
     a rank's z-slab -- voxelizes exactly the rows of those brick layers of the
     full grid (bit-identical: same records, same order per brick), and its
     backward of a slab gradient equals the backward of the full grid with
-    that gradient placed in a zero volume (the same per-brick moments; only
-    the order of the per-Gaussian float additions differs, so the float bar
-    applies).  The full-grid
-    backward is compared with the reference at the plain bar here for configs
-    0 and 1 and by test_fused_voxel_gradients_alone_match_reference at config
-    2, where the slab's smaller gradient is dominated by cut-off decisions
-    (see tests/_helpers.py)."""
+    that gradient placed in a zero volume (the same per-brick moments added
+    into float64 per-Gaussian sums, so the order of the additions does not
+    show: 1e-6).  The slab backward is compared with the reference at the
+    plain bar here for configs 0 and 1, and the full grid by
+    test_fused_voxel_gradients_alone_match_reference at config 2, where the
+    slab's smaller gradient is dominated by the voxel cut-off decisions."""
     name, d = case
     import r2s_shard as shard
     import r2s_workloads as wl
@@ -393,8 +393,8 @@ def test_explicit_voxelize_z_slab_matches_full_grid_and_reference(ref, case):
     assert torch.equal(vols[1], vols[0][z0:z1]), f"{name}: slab rows differ from the full grid"
     for key in grads[0]:
         e = rel_l2(grads[1][key], grads[0][key])
-        assert e < REL_L2_F32, f"{name}: slab grad {key} vs full-grid grad rel-L2 {e:.3e}"
-    if name not in NOISE_LIMITED:
+        assert e < 1e-6, f"{name}: slab grad {key} vs full-grid grad rel-L2 {e:.3e}"
+    if name not in VOXEL_DECISION_LIMITED:
         covars, max_s, opac = ref.prepare(d["quats"], d["scales"], d["opac"], wl.SCALE_MIN,
                                           wl.SCALE_MAX)
         v = ref.voxelize_forward(d["means"], covars, max_s, opac, d["ranges"], d["centers"], G, G,

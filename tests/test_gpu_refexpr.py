@@ -18,7 +18,7 @@ import subprocess
 import pytest
 import torch
 
-from _helpers import ROOT
+from _helpers import REL_L2_F32, ROOT, rel_l2
 
 pytestmark = pytest.mark.gpu
 
@@ -112,3 +112,61 @@ def test_reference_cut_off_expression_is_reproduced(probe):
     exact = [v for v, r in report.items() if r["value_mismatch"] == 0
              and r["bwd_decision_mismatch"] == 0]
     assert exact, f"no variant reproduces the reference: {report}"
+
+
+def test_raster_backward_decides_the_cut_off_like_the_reference():
+    """The pixels nearest the cut-off, one per image: this build's raster
+    backward (the 16x16 kernel: fast test, cut-off band, re-decision with
+    ref_keep2d) keeps exactly the pixels the reference's backward keeps.
+    Each Gaussian is replicated over K images, each with a one-hot upstream
+    gradient at one of its K pixels nearest the cut-off (by a float64
+    sigma); v_mu = opacity * vis at that pixel when it is kept, 0 when it is
+    dropped -- a decision per image, read from both builds."""
+    from oracle.ref_harness import ReferencePipeline
+    from r2splat.cuda import _wrapper as Wr
+
+    ref = ReferencePipeline()
+    C0, W, K = 4096, 64, 4
+    m, conics, wmu = _inputs(C0, W, seed=1)
+    dev = "cuda"
+    # mu != 1: the reference's alpha rounds (opacity * mu) * vis
+    g = torch.Generator().manual_seed(2)
+    mus = torch.empty(C0).uniform_(0.3, 1.0, generator=g)
+    op = (wmu / mus).clamp(max=1.0)
+    rep = lambda t: t.repeat_interleave(K, 0).contiguous().to(dev)  # noqa: E731
+    C = C0 * K
+    m2 = rep(m).reshape(C, 1, 2)
+    con = rep(conics).reshape(C, 1, 3)
+    opac = rep(op).reshape(C, 1)
+    mu = rep(mus).reshape(C, 1)
+    radii = torch.full((C, 1, 2), 4 * W, dtype=torch.int32, device=dev)
+    nt = W // 16
+    _, ids, fids = ref.C.isect_tiles(m2, radii, 16, nt, nt)
+    offs = ref.C.isect_offset_encode(ids, C, nt, nt)
+    # K pixels nearest the cut-off of each Gaussian, by a float64 sigma
+    f8 = torch.float64
+    ys, xs = torch.meshgrid(torch.arange(W, dtype=f8) + 0.5, torch.arange(W, dtype=f8) + 0.5,
+                            indexing="ij")
+    dx = xs[None] - m[:, 0, None, None].to(f8)
+    dy = ys[None] - m[:, 1, None, None].to(f8)
+    a, b, c = (conics[:, k, None, None].to(f8) for k in range(3))
+    sig = 0.5 * (a * dx * dx + c * dy * dy) + b * dx * dy
+    w8 = (op.to(f8) * mus.to(f8))[:, None, None]
+    gap = (sig - torch.log(w8 * 1e5)).abs().reshape(C0, -1)
+    near = gap.topk(K, dim=1, largest=False).indices.reshape(C)  # [C0 * K]
+    v_img = torch.zeros((C, W * W), device=dev)
+    v_img[torch.arange(C, device=dev), near.to(dev)] = 1.0
+    v_img = v_img.reshape(C, W, W)
+    args = (m2, con, opac, mu, offs, ids, fids, v_img, W, W, 16, False)
+    theirs = ref.C.rasterize_to_pixels_bwd_per_gaussian(*args)
+    mine = Wr.rasterize_to_pixels_bwd_per_gaussian(*args)
+    ref_keep = theirs[4].reshape(C) != 0
+    our_keep = mine[4].reshape(C) != 0
+    kept = int(ref_keep.sum())
+    assert 0 < kept < C, kept  # both decisions occur among the tested pixels
+    assert torch.equal(our_keep, ref_keep), (
+        f"{int((our_keep != ref_keep).sum())} of {C} cut-off decisions differ")
+    # the kept values: opacity * vis from each build's own exponential (this
+    # build's pre-scaled exp2, the reference's __expf)
+    e = rel_l2(mine[4].reshape(C)[ref_keep], theirs[4].reshape(C)[ref_keep])
+    assert e < REL_L2_F32, e
