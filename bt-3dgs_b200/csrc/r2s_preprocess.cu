@@ -13,6 +13,7 @@
 #include <math_constants.h>
 
 #include "r2s_common.cuh"
+#include "r2s_cutoff.cuh"
 #include "r2s_tiles.cuh"
 
 namespace r2s {
@@ -899,7 +900,8 @@ __global__ void map_vsplats_kernel(const float* __restrict__ means,
     out[0] = make_float4(o.m[0], o.m[1], o.m[2], P[0]);
     out[1] = make_float4(P[1], P[2], P[3], P[4]);
     out[2] = make_float4(P[5], w, e[0], e[1]);
-    out[3] = make_float4(e[2], 0.f, 0.f, 0.f);
+    // the voxel backward's cut-off band (r2s_cutoff.cuh)
+    out[3] = make_float4(e[2], cutoff_band_v(P, s_threshold_v(w), e[0], e[1], e[2]), 0.f, 0.f);
     int32_t count;
     rects[g] = tile_rect_3d(o.m[0], o.m[1], o.m[2], static_cast<float>(r[0]),
                             static_cast<float>(r[1]), static_cast<float>(r[2]), tile, nt2, nt1,

@@ -40,6 +40,7 @@
 #include "r2s_common.cuh"
 #include "r2s_cull.cuh"
 #include "r2s_debug.cuh"
+#include "r2s_cutoff.cuh"
 #include "r2s_refexpr.cuh"
 
 namespace r2s {
@@ -450,9 +451,10 @@ __global__ void raster_unpack_kernel(const S* __restrict__ stats, const S* __res
 // 0 <= s <= s_thr, s_thr = log2(|w mu| * 1e5); for non-negative floats the
 // IEEE bit patterns are ordered like the values and every negative s (sign
 // bit set) compares above s_thr as an unsigned integer, so one integer
-// compare decides the pair.  Pairs within rounding of the alpha cut-off may
-// be decided differently from the reference's float test; each such pair
-// moves a pixel by at most ~1e-5.  The 16x16 kernels evaluate -s with negated
+// compare decides the pair.  In the forward, pairs within rounding of the
+// alpha cut-off may be decided differently from the reference's float test
+// (each such pair moves a pixel by at most ~1e-5); the 16x16 backward
+// re-decides them exactly (r2s_cutoff.cuh).  The 16x16 forward evaluates -s with negated
 // coefficients (exact: negation commutes with rounding) and compare the bits
 // of -s as signed integers with INT_MIN + bits(s_thr); the one value decided
 // differently from "0 <= s <= s_thr" is s = -0.0, which needs a conic that is
@@ -460,43 +462,6 @@ __global__ void raster_unpack_kernel(const S* __restrict__ stats, const S* __res
 
 __device__ __forceinline__ bool s_valid(float s, uint32_t thr_bits) {
     return __float_as_uint(s) <= thr_bits;
-}
-
-__device__ __forceinline__ float s_threshold(float wmu) {
-    const float a = fabsf(wmu) * 1e5f;
-    return a >= 1.0f ? log2f(a) : -1.0f;  // negative: nothing passes
-}
-
-// Exact cut-off decisions in the backward.  The backward evaluates the
-// shifted exponent z = s_thr - s (s_thr added in the chain's last FMA) and
-// keeps a pixel when z >= 0; the reference's test (sigma from its own
-// expression tree, __expf, alpha = (w mu) vis >= 1e-5: ref_keep2d) agrees
-// except for pixels whose s lies within the sum of both evaluations' rounding
-// errors of s_thr.  Bound, in log2 units with u = 2^-24 and
-// M = log2(e) (|a| dx^2 / 2 + |b dx dy| + |c| dy^2 / 2) the magnitude of the
-// quadratic's terms:
-//   z: three rounded coefficients, five roundings of partial sums (the last
-//     one of a value near 0 at the cut-off)                        <= 8 u M + u s
-//   reference sigma: six roundings                                      <= 6 u M
-//   reference __expf(x), x ~ -s ln2: at most 2 + floor(1.173 |x|) ulp (the
-//     CUDA intrinsic's documented bound), then alpha = w mu * vis (one ulp)
-//                                                                    <= (9 + 2.4 s) u
-//   threshold: |w mu| * 1e5 rounded, log2f (fast math, <= 2^-20 absolute),
-//     1e-5f against 1/1e5                                                <= 24 u
-// i.e. |z - z_ref| <= u (14 M + 3.4 s_thr + 33).  The band is |z| <= delta
-// with twice that, delta = u (32 M + 8 s_thr + 100).  M is bounded over the
-// pixels that can lie near the cut-off: |dx| <= Dx, |dy| <= Dy, the smaller of
-// the record's culling extents (the ellipse at the cut-off, widened by
-// margins for rounding) and the largest offsets of the tile's pixel centres
-// from the mean; a pixel outside the extents is dropped by both tests.  A
-// pixel in the band is re-decided by ref_keep2d; every other pixel is decided
-// alike by both tests.
-__device__ __forceinline__ float cutoff_band(float a, float b, float c, float s_thr, float Dx,
-                                             float Dy) {
-    const float M = kLog2e * (0.5f * fabsf(a) * Dx * Dx + fabsf(b) * Dx * Dy +
-                              0.5f * fabsf(c) * Dy * Dy);
-    const float d = (32.0f * M + 8.0f * fabsf(s_thr) + 100.0f) * 0x1p-24f;
-    return d < 1e30f ? d : CUDART_INF_F;  // NaN: every pixel in the band
 }
 
 // Culling ranges of one (record, tile) pair after tile_cull, 4 bits each:
@@ -950,8 +915,12 @@ raster_bwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict
             const bool inside = i <= rmax && j <= cmax;
             const float mx = tr ? p.y : p.x, my = tr ? p.x : p.y;
             const float ca = tr ? q.x : p.z, cc = tr ? p.z : q.x;
-            const bool exact = inside && ref_keep2d(ca, p.w, cc, q.y, (X0f + ((float)j + 0.5f)) - mx,
-                                                    (Y0f + ((float)i + 0.5f)) - my);
+            // outside the band the sign of z is the reference's decision
+            const bool exact =
+                inside && (fabsf(z) > q.z ? z >= 0.f
+                                          : ref_keep2d(ca, p.w, cc, q.y,
+                                                       (X0f + ((float)j + 0.5f)) - mx,
+                                                       (Y0f + ((float)i + 0.5f)) - my));
             const bool diff = inside && fast != exact;
             float m[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
             if (diff) {

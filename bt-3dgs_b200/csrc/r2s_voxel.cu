@@ -28,6 +28,8 @@
 #include "r2s_common.cuh"
 #include "r2s_cull.cuh"
 #include "r2s_debug.cuh"
+#include "r2s_cutoff.cuh"
+#include "r2s_refexpr.cuh"
 
 namespace r2s {
 
@@ -445,10 +447,12 @@ __global__ void voxel_bwd_kernel(VoxSrc<S> src, const int32_t* __restrict__ offs
 // Validity test as in the 16x16 rasterizer: with s = sigma*log2(e) the
 // reference's test (sigma >= 0 and |w exp(-sigma)| >= 1e-6) is
 // 0 <= s <= log2(|w| 1e6), decided by one unsigned compare of the bits of s.
-// Pairs within rounding of the cut-off may be decided differently from the
-// reference's float test; each such pair moves a voxel by at most ~1e-6.
+// In the forward, pairs within rounding of the cut-off may be decided
+// differently from the reference's float test (each such pair moves a voxel
+// by at most ~1e-6); the 8x8x8 backward re-decides them exactly
+// (r2s_cutoff.cuh).
 
-// The kernels evaluate -s (negated coefficients, exact) and compare its bits as
+// The forward evaluates -s (negated coefficients, exact) and compare its bits as
 // signed integers with INT_MIN + bits(s_thr); s = -0.0 (a conic that is not
 // positive definite, voxel centre on the mean) counts as s < 0.
 __device__ __forceinline__ bool sn_valid_v(float sn, int thr_n) {
@@ -459,17 +463,13 @@ __device__ __forceinline__ int thr_neg_v(float thr) {
     return (int)(__float_as_uint(thr) ^ 0x80000000u);
 }
 
-__device__ __forceinline__ float s_threshold_v(float w) {
-    const float a = fabsf(w) * 1e6f;
-    return a >= 1.0f ? log2f(a) : -1.0f;  // records with a < 1 have an empty box
-}
-
 struct VRecord {
     float m[3];
     // negated pre-scaled conic: -sigma log2(e) = dx (A dx + B dy + Cq dz) + dy (D dy + E dz) + F dz^2
     float A, B, Cq, D, E, F;
     float w;
     float e[3];
+    float band;  // cut-off band of the voxel backward (cutoff_band_v)
 };
 
 __device__ __forceinline__ VRecord load_vrecord(const float4* __restrict__ vsplats, int64_t g) {
@@ -489,6 +489,7 @@ __device__ __forceinline__ VRecord load_vrecord(const float4* __restrict__ vspla
     r.e[0] = c.z;
     r.e[1] = c.w;
     r.e[2] = d.x;
+    r.band = d.y;
     return r;
 }
 
@@ -736,7 +737,7 @@ constexpr int kVBwd8Batch = 1024;   // records staged and sorted per batch
 // in that slice, and the 8 voxels of each row in packed pairs.  Per-column
 // sums Col_x = sum v e over rows give S0, Sx, Sxx; per-row sums R0 = sum_x v e
 // and R1 = sum_x v e dx give the y/z moments, so every moment is a direct sum.
-__global__ void __launch_bounds__(kVBwd8Threads)
+__global__ void __launch_bounds__(kVBwd8Threads, 3)
 voxel_bwd8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict__ offsets,
                   const int32_t* __restrict__ flatten_ids, const uint2* __restrict__ rows,
                   int64_t n_keys, int64_t n_isects, int64_t n_splats,
@@ -750,6 +751,8 @@ voxel_bwd8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict_
     __shared__ uint16_t s_perm[kVBwd8Batch];
     __shared__ int32_t s_cnt[65];            // bucket 64: records that reach no voxel
     __shared__ int s_next;                   // next group to take
+    __shared__ uint16_t s_fix[kVBwd8Batch];  // records with a voxel in the cut-off band
+    __shared__ int s_nfix;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     int bxi, byi, bzl;
@@ -777,6 +780,7 @@ voxel_bwd8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict_
 
     for (int base = start; base < end; base += kVBwd8Batch) {
         if (tid < 65) s_cnt[tid] = 0;
+        if (tid == 0) s_nfix = 0;
         __syncthreads();
         constexpr int kPer = kVBwd8Batch / kVBwd8Threads;
         int bucket[kPer], rank[kPer];
@@ -855,7 +859,11 @@ voxel_bwd8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict_
             const uint2 tab = s_tab[idx];
             const VRecord r = load_vrecord(vsplats, g);
 
-            const int thr_n = thr_neg_v(s_threshold_v(r.w));
+            // z = s_thr - s from the chain (s_thr enters through the slice
+            // term): kept when z >= 0, in the cut-off band when |z| <= band;
+            // the sums run over 2^z and are scaled by 2^-s_thr per record
+            const float s_thr = s_threshold_v(r.w);
+            float z_min = CUDART_INF_F;
             const float2 A2 = make_float2(r.A, r.A);
             float2 dx[4], col[4];
 #pragma unroll
@@ -871,7 +879,7 @@ voxel_bwd8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict_
                 const int y1 = __reduce_max_sync(0xffffffffu, yhi);
                 if (y0 > y1) continue;  // warp-uniform: no row of this slice
                 const float dz = (Z0f + ((float)z + 0.5f)) - r.m[2];
-                const float cdz = r.Cq * dz, edz = r.E * dz, fzz = r.F * dz * dz;
+                const float cdz = r.Cq * dz, edz = r.E * dz, fzz = fmaf(r.F * dz, dz, s_thr);
                 for (int y = y0; y <= y1; ++y) {
                     const bool rin = y >= ylo && y <= yhi;
                     const float dy = (Y0f + ((float)y + 0.5f)) - r.m[1];
@@ -887,10 +895,11 @@ voxel_bwd8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict_
                                           : j == 1 ? make_float2(va.z, va.w)
                                           : j == 2 ? make_float2(vb.x, vb.y)
                                                    : make_float2(vb.z, vb.w);
-                        const float2 sn = ffma2(dx[j], ffma2(A2, dx[j], by2), rest2);  // -s
-                        float e0 = exp2f(sn.x), e1 = exp2f(sn.y);
-                        e0 = (rin && sn_valid_v(sn.x, thr_n)) ? e0 : 0.f;
-                        e1 = (rin && sn_valid_v(sn.y, thr_n)) ? e1 : 0.f;
+                        const float2 z2 = ffma2(dx[j], ffma2(A2, dx[j], by2), rest2);  // s_thr - s
+                        float e0 = exp2f(z2.x), e1 = exp2f(z2.y);
+                        z_min = fminf(z_min, fminf(fabsf(z2.x), fabsf(z2.y)));
+                        e0 = (rin && z2.x >= 0.f) ? e0 : 0.f;
+                        e1 = (rin && z2.y >= 0.f) ? e1 : 0.f;
                         const float2 ve = fmul2(v2, make_float2(e0, e1));
                         col[j] = fadd2(col[j], ve);
                         r0 = fadd2(r0, ve);
@@ -907,6 +916,7 @@ voxel_bwd8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict_
                 }
             }
             if (!live) return;
+            if (!(z_min > r.band)) s_fix[atomicAdd(&s_nfix, 1)] = (uint16_t)idx;  // also NaN
             float S0 = 0.f, Sx = 0.f, Sxx = 0.f;
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
@@ -916,7 +926,9 @@ voxel_bwd8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict_
                 Sxx = fmaf(cx.x, dx[j].x, Sxx);
                 Sxx = fmaf(cx.y, dx[j].y, Sxx);
             }
-            const float m[10] = {S0, Sx, Sy, Sz, Sxx, Sxy, Sxz, Syy, Syz, Szz};
+            const float k = exp2f(-s_thr);  // 2^-s_thr: the sums back to e^-sigma
+            const float m[10] = {S0 * k,  Sx * k,  Sy * k,  Sz * k,  Sxx * k,
+                                 Sxy * k, Sxz * k, Syy * k, Syz * k, Szz * k};
             vstats_red(stats + g * 12, m);
                 };
         int grp = warp;
@@ -926,6 +938,51 @@ voxel_bwd8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict_
             int nxt = 0;
             if (lane == 0) nxt = atomicAdd(&s_next, 1);
             grp = __shfl_sync(0xffffffffu, nxt, 0);
+        }
+        __syncthreads();
+        // records with a voxel in the cut-off band: every voxel of the brick
+        // re-decided by the reference's own test, two voxels per thread;
+        // where the decisions differ (a few voxels in a million records), the
+        // voxel's moments are added to or taken back from the record's
+        // float64 sums
+        const int n_fix = s_nfix;
+        for (int f = 0; f < n_fix; ++f) {
+            const int idx = s_fix[f];
+            const int64_t g = s_g[idx];
+            const uint2 tab = s_tab[idx];
+            const float4 a = vsplats[4 * g], b = vsplats[4 * g + 1], c = vsplats[4 * g + 2];
+            const float kc[6] = {a.w, b.x, b.y, b.z, b.w, c.x};  // raw conic (raw_conic)
+            // the pre-scaled coefficients of load_vrecord, operation for operation
+            const float A = -0.5f * kLog2eV * a.w, B = -kLog2eV * b.x, Cq = -kLog2eV * b.y;
+            const float D = -0.5f * kLog2eV * b.z, E = -kLog2eV * b.w, F = -0.5f * kLog2eV * c.x;
+            const float s_thr = s_threshold_v(c.y);
+            const float band = vsplats[4 * g + 3].y;
+#pragma unroll 1
+            for (int vox = tid; vox < 512; vox += kVBwd8Threads) {
+                const int z = vox >> 6, y = (vox >> 3) & 7, x = vox & 7;
+                if (x > xmax || y > ymax || z > zmax) continue;
+                // the main loop's fast decision, operation for operation; a
+                // voxel outside the row table is dropped by both tests
+                const uint32_t byte = ((z < 4 ? tab.x : tab.y) >> (8 * (z & 3))) & 0xffu;
+                if (y < (int)(byte & 15u) || y > (int)(byte >> 4)) continue;
+                const float dx = (X0f + ((float)x + 0.5f)) - a.x;
+                const float dy = (Y0f + ((float)y + 0.5f)) - a.y;
+                const float dz = (Z0f + ((float)z + 0.5f)) - a.z;
+                const float cdz = Cq * dz, edz = E * dz, fzz = fmaf(F * dz, dz, s_thr);
+                const float by = fmaf(B, dy, cdz);
+                const float rest = fmaf(dy, fmaf(D, dy, edz), fzz);
+                const float zz = fmaf(dx, fmaf(A, dx, by), rest);
+                const bool fast = zz >= 0.f;
+                // outside the band the sign of z is the reference's decision
+                const bool exact =
+                    fabsf(zz) > band ? zz >= 0.f : ref_keep3d(kc, c.y, dx, dy, dz);
+                if (fast == exact) continue;
+                const float ve = (exact ? 1.0f : -1.0f) * s_v[vox] * (exp2f(zz) * exp2f(-s_thr));
+                const float vx = ve * dx, vy = ve * dy, vz = ve * dz;
+                const float mv[10] = {ve, vx, vy, vz, vx * dx, vx * dy, vx * dz, vy * dy, vy * dz,
+                                      vz * dz};
+                vstats_red(stats + g * 12, mv);
+            }
         }
         __syncthreads();
     }

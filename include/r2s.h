@@ -434,7 +434,10 @@ R2S_API int r2s_raster_splats_bwd_f32(const float* splats, const int32_t* tile_o
 /* Volume mapping + voxel splat records + brick rectangles
  * (direct.py:289-314: world_to_volume_mapping_fwd and the first pass of
  * isect_tiles_3d).  Writes means3d [N,3], conics [N,6], radii [N,3],
- * vsplats [N,16] (x, y, z, c00, c01, c02, c11, c12, c22, w, ex, ey, ez, 0..),
+ * vsplats [N,16] (x, y, z, c00, c01, c02, c11, c12, c22, w, ex, ey, ez, band, 0,
+ * 0): the conic, opacity, culling half-extents and the voxel backward's
+ * cut-off band (the log2-unit distance from the cut-off inside which its fast
+ * test is re-checked against the reference's),
  * rects3 [N] (16 B), tiles_per_gauss [N] (nullable). */
 R2S_API int r2s_map_vsplats_f32(const float* means, const float* covars, const float* opacities,
                         const float* ranges, const float* centers, int64_t N, uint32_t dim2,

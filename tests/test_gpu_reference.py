@@ -242,13 +242,6 @@ def test_fused_op_layer_matches_reference_pipeline(ref, case):
     assert rel_l2(res.means2d.absgrad, theirs["means2d_abs"]) < REL_L2_F32
 
 
-# cases where a z-slab's gradient alone is dominated by the voxel cut-off
-# decisions (pixels within rounding of |alpha| = 1e-6, decided by each build
-# its own way): the slab is compared with the reference there only through
-# the full-grid test above
-VOXEL_DECISION_LIMITED = {"cfg2-4views", "cfg2-75views"}
-
-
 def _float64_gradients(ref, d, p, v_img, v, v_vol, covars):
     """Parameter gradients evaluated in float64 by the reference's own double
     kernels from the float32 forward values and the float32 binning (the
@@ -357,10 +350,8 @@ def test_explicit_voxelize_z_slab_matches_full_grid_and_reference(ref, case):
     backward of a slab gradient equals the backward of the full grid with
     that gradient placed in a zero volume (the same per-brick moments added
     into float64 per-Gaussian sums, so the order of the additions does not
-    show: 1e-6).  The slab backward is compared with the reference at the
-    plain bar here for configs 0 and 1, and the full grid by
-    test_fused_voxel_gradients_alone_match_reference at config 2, where the
-    slab's smaller gradient is dominated by the voxel cut-off decisions."""
+    show: 1e-6), and the reference's at the plain bar (the voxel backward
+    decides the cut-off exactly like the reference)."""
     name, d = case
     import r2s_shard as shard
     import r2s_workloads as wl
@@ -394,17 +385,16 @@ def test_explicit_voxelize_z_slab_matches_full_grid_and_reference(ref, case):
     for key in grads[0]:
         e = rel_l2(grads[1][key], grads[0][key])
         assert e < 1e-6, f"{name}: slab grad {key} vs full-grid grad rel-L2 {e:.3e}"
-    if name not in VOXEL_DECISION_LIMITED:
-        covars, max_s, opac = ref.prepare(d["quats"], d["scales"], d["opac"], wl.SCALE_MIN,
-                                          wl.SCALE_MAX)
-        v = ref.voxelize_forward(d["means"], covars, max_s, opac, d["ranges"], d["centers"], G, G,
-                                 G, wl.VOL_TILE, wl.EPS3D, wl.RADIUS_CLIP)
-        theirs = ref.explicit_backward(None, None, v, v_full, d["means"], d["quats"], d["scales"],
-                                       d["opac"], covars, opac, wl.SCALE_MIN, wl.SCALE_MAX)
-        for key, pk in (("means", "means"), ("quats", "quats"), ("scales", "scales"),
-                        ("opac", "opacities")):
-            e = rel_l2(grads[1][key], theirs[pk])
-            assert e < REL_L2_F32, f"{name}: slab grad {key} rel-L2 {e:.3e}"
+    covars, max_s, opac = ref.prepare(d["quats"], d["scales"], d["opac"], wl.SCALE_MIN,
+                                      wl.SCALE_MAX)
+    v = ref.voxelize_forward(d["means"], covars, max_s, opac, d["ranges"], d["centers"], G, G,
+                             G, wl.VOL_TILE, wl.EPS3D, wl.RADIUS_CLIP)
+    theirs = ref.explicit_backward(None, None, v, v_full, d["means"], d["quats"], d["scales"],
+                                   d["opac"], covars, opac, wl.SCALE_MIN, wl.SCALE_MAX)
+    for key, pk in (("means", "means"), ("quats", "quats"), ("scales", "scales"),
+                    ("opac", "opacities")):
+        e = rel_l2(grads[1][key], theirs[pk])
+        assert e < REL_L2_F32, f"{name}: slab grad {key} rel-L2 {e:.3e}"
     with pytest.raises(ValueError):
         st = E.prepare_explicit_gaussians(d["quats"], d["scales"], d["opac"],
                                           scale_min=wl.SCALE_MIN, scale_max=wl.SCALE_MAX)

@@ -247,11 +247,10 @@ def test_training_step_gradients_match_reference():
         assert abs(a - b) <= 1e-5 * max(1e-3, abs(b)), (k, a, b)
     assert rel_l2(res.image.grad, image.grad) < 1e-5
     # parameter gradients: the 1e-5 bar, or within 2e-5 and no less accurate
-    # than the reference against a float64 evaluation.  Here the loss's volume
-    # term runs through the voxel cut-off (|alpha| = 1e-6), which each build
-    # decides its own way at pixels within rounding of it: measured, the
-    # quaternion gradients of both builds lie 1.9e-5 from the float64
-    # evaluation and 1.0e-5 from each other.
+    # than the reference against a float64 evaluation.  The quaternion
+    # gradient of this loss is ill-conditioned: measured, the reference's own
+    # float32 result lies 1.9e-5 from the float64 evaluation of the same
+    # inputs, this build's as far, and the two 1.0e-5 from each other.
     from _helpers import check_grad_accuracy
     from test_gpu_reference import _float64_gradients
 
