@@ -294,14 +294,22 @@ class OursProjection(HostPipeline):
                                                           wl.IMG_TILE, nt, nt, wl.EPS2D,
                                                           wl.RADIUS_CLIP)
             T.mark("project")
-            offs, ids, _ = W.fused_bin(rects, C, N, nt * nt, nt, 0)
-            T.mark("binning (incl. host read of the record count)")
-            cull = torch.empty(ids.shape, dtype=torch.int16, device=self.dev)
-            W.fused_raster_fwd(splats, offs, ids, C, N, det, det, wl.IMG_TILE, nt, nt, cull=cull)
-            T.mark("raster forward")
-            stats = W.fused_raster_bwd(splats, offs, ids, self.v_img, C, N, det, det,
-                                       wl.IMG_TILE, nt, nt, True, cull=cull)
-            T.mark("raster backward")
+            # the op layer's view batches (one batch unless the records pass
+            # the int32 tile offsets, as at config 3)
+            stats = torch.empty((C * N, 8), dtype=torch.float32, device=self.dev)
+            for c0, c1 in W.plan_view_batches(rects, C, N):
+                offs, ids, _ = W.fused_bin(rects[c0 * N * 8:c1 * N * 8], c1 - c0, N, nt * nt, nt,
+                                           0)
+                T.mark("binning (incl. host read of the record count)")
+                cull = torch.empty(ids.shape, dtype=torch.int16, device=self.dev)
+                W.fused_raster_fwd(splats[c0:c1], offs, ids, c1 - c0, N, det, det, wl.IMG_TILE,
+                                   nt, nt, cull=cull)
+                T.mark("raster forward")
+                W.fused_raster_bwd(splats[c0:c1], offs, ids, self.v_img[c0:c1], c1 - c0, N, det,
+                                   det, wl.IMG_TILE, nt, nt, True, out=stats[c0 * N:c1 * N],
+                                   cull=cull)
+                T.mark("raster backward")
+                del offs, ids, cull
             outs = [torch.empty_like(t) for t in (m, q, s, o)]
             v2 = torch.empty((C, N, 2), device=self.dev)
             v2a = torch.empty((C, N, 2), device=self.dev)
@@ -438,7 +446,8 @@ class PhaseTimer:
         torch.cuda.synchronize()
         out = {}
         for (_, a), (name, b) in zip(self.events, self.events[1:]):
-            out[name] = round(a.elapsed_time(b), 4)
+            out[name] = out.get(name, 0.0) + a.elapsed_time(b)  # a phase repeated per batch sums
+        out = {k: round(v, 4) for k, v in out.items()}
         return {"ms": out, "total_ms": round(sum(out.values()), 4)}
 
 
@@ -921,14 +930,15 @@ def pipe_peaks(dev):
 
 # DRAM traffic of one raster_bwd16_kernel launch per view: the ncu capture of
 # `bench.py --views 8` in profiles/raster_bwd16_cfg2_8views.md,
-# dram__bytes_read.sum + dram__bytes_write.sum = 530.805 MB + 106.821 MB for 8
+# dram__bytes_read.sum + dram__bytes_write.sum = 530.231 MB + 105.894 MB for 8
 # views (traffic grows with the views).
-BWD16_DRAM_BYTES_PER_VIEW = (530.805248e6 + 106.821376e6) / 8
+BWD16_DRAM_BYTES_PER_VIEW = (530.231296e6 + 105.893632e6) / 8
 # FP32 work per evaluated pixel of raster_bwd16_kernel<true> (absolute
 # gradients on), counted from its inner loop: 7 FFMA (the exponent: 2; the row
 # moment R1; the two conic products a dx + b dy, b dx + c dy; the two absolute
 # sums), 1 FMUL (v e) and 2 FADD (the column and row sums): 10 FP32-pipe
-# instructions, 17 FLOP, and 1 MUFU ex2.
+# instructions, 17 FLOP, and 1 MUFU ex2.  The keep test (z >= 0) and the
+# cut-off band's running min of |z| run on the ALU pipe and are not counted.
 BWD16_FLOP_PER_PAIR = 17
 BWD16_FP32_INST_PER_PAIR = 10
 
