@@ -929,7 +929,7 @@ def pipe_peaks(dev):
 
 
 # DRAM traffic of one raster_bwd16_kernel launch per view: the ncu capture of
-# `bench.py --views 8` in profiles/raster_bwd16_cfg2_8views.md,
+# `bench.py --views 8` (one kernel, one launch, --set full),
 # dram__bytes_read.sum + dram__bytes_write.sum = 530.231 MB + 105.894 MB for 8
 # views (traffic grows with the views).
 BWD16_DRAM_BYTES_PER_VIEW = (530.231296e6 + 105.893632e6) / 8
