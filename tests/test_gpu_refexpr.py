@@ -162,6 +162,9 @@ def test_raster_backward_decides_the_cut_off_like_the_reference():
     mine = Wr.rasterize_to_pixels_bwd_per_gaussian(*args)
     ref_keep = theirs[4].reshape(C) != 0
     our_keep = mine[4].reshape(C) != 0
+    # the reference's pixel backward mode decides alike
+    pix = ref.C.rasterize_to_pixels_bwd(m2, con, opac, mu, offs, fids, v_img, W, W, 16, False)
+    assert torch.equal(pix[4].reshape(C) != 0, ref_keep)
     kept = int(ref_keep.sum())
     assert 0 < kept < C, kept  # both decisions occur among the tested pixels
     assert torch.equal(our_keep, ref_keep), (
@@ -211,7 +214,8 @@ def test_reference_voxel_cut_off_expression_is_reproduced(probe):
     its cell; each variant is evaluated on the same voxels, and the
     backward's decision (csrc/VoxelizeToVoxelsBwd.cu:395-402) is read from
     v_opacity of a one-hot upstream gradient at each cell's voxel nearest the
-    cut-off.  Requires a variant that matches both exactly."""
+    cut-off.  Requires a variant that matches both exactly; the reference's
+    pixel backward mode decides like its primitive mode."""
     from oracle.ref_harness import ReferencePipeline
 
     probe.probe_alpha3d.restype = ctypes.c_int
@@ -265,6 +269,9 @@ def test_reference_voxel_cut_off_expression_is_reproduced(probe):
     grads = ref.C.voxelize_to_voxels_bwd_per_gaussian(m3, con, op, offs, ids, fids, v_vol, G, G,
                                                       G, 8)
     ref_keep = grads[2].reshape(C) != 0  # v_opacity = vis at the one voxel, 0 if dropped
+    # the reference's pixel backward mode decides alike
+    pix = ref.C.voxelize_to_voxels_bwd(m3, con, op, offs, fids, v_vol, G, G, G, 8)
+    assert torch.equal(pix[2].reshape(C) != 0, ref_keep)
     for v in VARIANTS3D:
         ours_keep = outs[v][torch.arange(C, device=dev), near] != 0
         report[v]["bwd_decision_mismatch"] = int((ours_keep != ref_keep).sum())
