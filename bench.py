@@ -1246,13 +1246,14 @@ def main():
     e2e_value = cfg.n_gaussians * job_views / (e2e_ms * 1e-3)
     vox_value = cfg.grid ** 3 / (vms * 1e-3) / 1e6
     barrier(world)
-    # our kernels per timed step: projection = prepare, project_splats, binning
-    # (count, column scan, scan, place), raster forward, raster backward,
-    # explicit backward; voxel = prepare, map, binning (count, column scan,
-    # scan, place), brick order, row table, voxel forward, voxel backward,
-    # explicit backward (the zero-view projection pass launches nothing)
-    gpu_launches = args.steps * 9
-    vox_launches = args.steps * 11
+    # our kernels per timed step: projection = prepare (covariances, then the
+    # softplus opacities), project_splats, binning (count, column scan, scan,
+    # place), raster forward, raster backward, explicit backward; voxel =
+    # prepare (two), map, binning (count, column scan, scan, place), brick
+    # order, row table, voxel forward, voxel backward, explicit backward (the
+    # zero-view projection pass launches nothing)
+    gpu_launches = args.steps * 10
+    vox_launches = args.steps * 12
     if rank != 0:
         return
     line = {
