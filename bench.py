@@ -833,7 +833,12 @@ def run_train_bench(args, cfg, dev, world, rank, local, flush):
                                 "kind": "reference",
                                 "sample": "the reference's CUDA build and PyTorch code on GPU 0"}
     else:
-        line["gpu_launches"] = args.steps * 21
+        # per step: prepare (2), project_splats, binning (4), raster forward;
+        # TV sub-volume: map, 3D binning (4), brick order, row table, voxel
+        # forward; losses: projection loss and its gradient, TV and its
+        # gradient; backward: raster, voxel, explicit backward with the
+        # densification statistics; Adam; plus the split's children kernel
+        line["gpu_launches"] = args.steps * 24 + len(splits)
     print(json.dumps(line))
 
 
