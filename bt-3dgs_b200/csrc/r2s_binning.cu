@@ -549,8 +549,10 @@ int bin_place_impl(const void* rects, int64_t S, int64_t N, int64_t T, uint32_t 
     R2S_REQUIRE(ws_bytes >= p.bytes, "binning: workspace too small");
     const WsView w = carve(const_cast<void*>(ws), p);
     // staged placement when the per-(warp, tile) counters leave room for a
-    // staging buffer of at least 4096 records in ~104 KB (two 16-warp CTAs per SM)
-    constexpr int kStagedSmem = 104 * 1024;
+    // staging buffer of at least 4096 records in 112 KB: two 16-warp CTAs per SM
+    // (2 x (112 + 1) KB of the SM's 228 KB); 2304 tiles per segment (768^2
+    // detectors) leave 6656 records
+    constexpr int kStagedSmem = 112 * 1024;
     const int64_t fixed = (int64_t)kStagedWarps * ((T + 1) / 2) * 4 + (int64_t)3 * T * 4;
     const int64_t cap = ((kStagedSmem - fixed) / 2) & ~int64_t(7);
     if (cap >= 4096 && p.chunk <= 65536) {
