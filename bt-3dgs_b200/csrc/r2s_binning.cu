@@ -549,12 +549,14 @@ int bin_place_impl(const void* rects, int64_t S, int64_t N, int64_t T, uint32_t 
     R2S_REQUIRE(ws_bytes >= p.bytes, "binning: workspace too small");
     const WsView w = carve(const_cast<void*>(ws), p);
     // staged placement when the per-(warp, tile) counters leave room for a
-    // staging buffer of at least 4096 records in 112 KB: two 16-warp CTAs per SM
-    // (2 x (112 + 1) KB of the SM's 228 KB); 2304 tiles per segment (768^2
-    // detectors) leave 6656 records
-    constexpr int kStagedSmem = 112 * 1024;
+    // staging buffer of at least 4096 records: in 112 KB, two 16-warp CTAs per
+    // SM (2 x (112 + 1) KB of the SM's 228 KB; 2304 tiles per segment, a 768^2
+    // detector, leave 6656 records), else in 224 KB, one CTA per SM (4096
+    // bricks per layer, a 512^3 grid, leave 24576)
+    constexpr int64_t kStagedSmemTwo = 112 * 1024, kStagedSmemOne = 224 * 1024;
     const int64_t fixed = (int64_t)kStagedWarps * ((T + 1) / 2) * 4 + (int64_t)3 * T * 4;
-    const int64_t cap = ((kStagedSmem - fixed) / 2) & ~int64_t(7);
+    const int64_t budget = fixed + 4096 * 2 <= kStagedSmemTwo ? kStagedSmemTwo : kStagedSmemOne;
+    const int64_t cap = ((budget - fixed) / 2) & ~int64_t(7);
     if (cap >= 4096 && p.chunk <= 65536) {
         const size_t smem = (size_t)(fixed + cap * 2);
         const unsigned blocks = (unsigned)(S * p.n_chunks);
