@@ -297,7 +297,8 @@ class OursProjection(HostPipeline):
             # the op layer's view batches (one batch unless the records pass
             # the int32 tile offsets, as at config 3)
             stats = torch.empty((C * N, 8), dtype=torch.float32, device=self.dev)
-            for c0, c1 in W.plan_view_batches(rects, C, N):
+            batches = W.plan_view_batches(rects, C, N)
+            for c0, c1 in batches:
                 offs, ids, _ = W.fused_bin(rects[c0 * N * 8:c1 * N * 8], c1 - c0, N, nt * nt, nt,
                                            0)
                 T.mark("binning (incl. host read of the record count)")
@@ -320,7 +321,9 @@ class OursProjection(HostPipeline):
             if self.world > 1:
                 self.allreduce(outs)
             T.mark("gradient all-reduce")
-        return T.result()
+        res = T.result()
+        res["view_batches"] = len(batches)
+        return res
 
 
 class OursVoxel(HostPipeline):
@@ -1228,6 +1231,7 @@ def main():
         peaks = pipe_peaks(dev)
         roof = (dominant_kernel_roofline(proj, hbm_peak, peak_kind, peaks)
                 if rank == 0 else None)
+        proj.phases()  # the first call sizes the allocator's blocks for these calls
         proj_phases = proj.phases()
         h2d, d2h = proj.bytes_e2e()
         del proj
@@ -1235,6 +1239,7 @@ def main():
         vox = OursVoxel(cfg, world, rank, dev, wl.make_gaussians(cfg))
         vms = time_steps(vox.step, args.steps, args.warmup, world, flush)
         v_e2e_ms = time_e2e(vox, args.steps, max(1, args.warmup // 2), world, flush)
+        vox.phases()
         vox_phases = vox.phases()
         vh2d, vd2h = vox.bytes_e2e()
     del vox
@@ -1253,11 +1258,12 @@ def main():
     barrier(world)
     # our kernels per timed step: projection = prepare (covariances, then the
     # softplus opacities), project_splats, binning (count, column scan, scan,
-    # place), raster forward, raster backward, explicit backward; voxel =
+    # place), raster forward, raster backward, explicit backward (binning to
+    # raster backward once per view batch); voxel =
     # prepare (two), map, binning (count, column scan, scan, place), brick
     # order, row table, voxel forward, voxel backward, explicit backward (the
     # zero-view projection pass launches nothing)
-    gpu_launches = args.steps * 10
+    gpu_launches = args.steps * (4 + 6 * proj_phases["view_batches"])
     vox_launches = args.steps * 12
     if rank != 0:
         return
