@@ -608,20 +608,30 @@ voxel_rows8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict
     }
 }
 
-constexpr int kVFwd8Threads = 64;  // 2 warps; a warp owns four z-slices, a thread 4x2 voxels (x, z)
-constexpr int kVFwd8Batch = 128;
+// A group of 2 warps covers a brick's 512 voxels (a warp owns four z-slices,
+// a thread 4x2 voxels (x, z)).  A CTA holds GROUPS groups; they take the
+// staged records of each batch in turn (record t of the batch to group
+// t mod GROUPS) and add their partial sums in group order at the end.  One
+// group per CTA is the fastest on launches of many waves (the full grid);
+// launches of fewer bricks (a z-slab of a multi-GPU split: one or a few waves)
+// finish sooner with four, since with one group an SM runs a handful of
+// heavy bricks at low occupancy once the light ones are done.
+constexpr int kVFwd8Batch = 128;  // records staged per group and batch
+constexpr int kVFwd8GroupedBricks = 16384;  // fewer bricks per launch: four groups
 
-__global__ void __launch_bounds__(kVFwd8Threads)
+template <int GROUPS>
+__global__ void __launch_bounds__(64 * GROUPS)
 voxel_fwd8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict__ offsets,
                   const int32_t* __restrict__ flatten_ids, const uint2* __restrict__ rows,
                   int64_t n_keys, int64_t n_isects, int64_t n_splats, uint32_t dim2,
                   uint32_t dim1, uint32_t dim0, uint32_t nt2, uint32_t nt1, uint32_t layer_begin,
                   const int32_t* __restrict__ order, float* __restrict__ vol) {
-    __shared__ float4 s_a[kVFwd8Batch];  // mx, my, mz, A
-    __shared__ float4 s_b[kVFwd8Batch];  // B, Cq, D, E
-    __shared__ float4 s_c[kVFwd8Batch];  // F, w, s threshold, warp mask (bits)
+    constexpr int kThreads = 64 * GROUPS, kBatch = kVFwd8Batch * GROUPS;
+    __shared__ float4 s_a[kBatch];  // mx, my, mz, A
+    __shared__ float4 s_b[kBatch];  // B, Cq, D, E
+    __shared__ float4 s_c[kBatch];  // F, w, s threshold, warp mask (bits)
 
-    const int tid = threadIdx.x, warp = tid >> 5;
+    const int tid = threadIdx.x, grp = tid >> 6, gt = tid & 63, warp = gt >> 5;
     int bxi, byi, bzl;
     const int64_t key = brick_of_block(order, nt2, nt1, bxi, byi, bzl);
     const uint32_t bz = bzl + layer_begin;
@@ -629,7 +639,7 @@ voxel_fwd8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict_
     const int xmax = min(7, (int)dim2 - 1 - X0);
     const int ymax = min(7, (int)dim1 - 1 - Y0);
     const int zmax = min(7, (int)dim0 - 1 - Z0);
-    const int lx = (tid & 1) * 4, ly = (tid >> 1) & 7, lz = (tid >> 4) * 2;
+    const int lx = (gt & 1) * 4, ly = (gt >> 1) & 7, lz = (gt >> 4) * 2;
     const float2 px01 = make_float2((float)(X0 + lx) + 0.5f, (float)(X0 + lx) + 1.5f);
     const float2 px23 = make_float2((float)(X0 + lx) + 2.5f, (float)(X0 + lx) + 3.5f);
     const float py = (float)(Y0 + ly) + 0.5f;
@@ -640,10 +650,10 @@ voxel_fwd8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict_
         return;  // uniform over the CTA
     float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};  // [z][x]
 
-    for (int b0 = start; b0 < end; b0 += kVFwd8Batch) {
-        const int n = min(kVFwd8Batch, end - b0);
+    for (int b0 = start; b0 < end; b0 += kBatch) {
+        const int n = min(kBatch, end - b0);
         __syncthreads();
-        for (int j = tid; j < n; j += kVFwd8Threads) {
+        for (int j = tid; j < n; j += kThreads) {
             const int64_t g = flatten_ids[b0 + j];
             if (R2S_DBG_BAD(g >= 0 && g < n_splats, R2S_DBG_RECORD_ID)) {
                 s_c[j] = make_float4(0.f, 0.f, 0.f, __uint_as_float(0u));  // no warp evaluates it
@@ -675,7 +685,7 @@ voxel_fwd8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict_
                                  __uint_as_float(msk));
         }
         __syncthreads();
-        for (int t = 0; t < n; ++t) {
+        for (int t = grp; t < n; t += GROUPS) {
             const float4 c = s_c[t];
             if (!((__float_as_uint(c.w) >> warp) & 1u)) continue;  // warp-uniform
             const float4 a = s_a[t], b = s_b[t];
@@ -702,6 +712,21 @@ voxel_fwd8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict_
                 if (sn_valid_v(s23.y, thr_n)) acc[zz][3] = fmaf(c.y, e3, acc[zz][3]);
             }
         }
+    }
+    if constexpr (GROUPS > 1) {  // the groups' sums, added in group order by group 0
+        __syncthreads();  // the last batch's records are no longer read
+        float* const s_part = reinterpret_cast<float*>(s_a);  // [group - 1][8][64]
+        static_assert((GROUPS - 1) * 8 * 64 <= kBatch * 4, "partial sums fit in s_a");
+        if (grp > 0) {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) s_part[((grp - 1) * 8 + k) * 64 + gt] = acc[k >> 2][k & 3];
+        }
+        __syncthreads();
+        if (grp > 0) return;
+#pragma unroll
+        for (int g = 1; g < GROUPS; ++g)
+#pragma unroll
+            for (int k = 0; k < 8; ++k) acc[k >> 2][k & 3] += s_part[((g - 1) * 8 + k) * 64 + gt];
     }
     if (ly > ymax) return;
     const int64_t zoff = (int64_t)layer_begin * 8;
@@ -1167,10 +1192,15 @@ extern "C" int r2s_voxel_splats_fwd_f32(const float* vsplats, const int32_t* off
     }
     if (T == 8) {
         const dim3 grid(nt2, nt1, layer_end - layer_begin);
-        voxel_fwd8_kernel<<<grid, kVFwd8Threads, 0, stream>>>(
-            (const float4*)vsplats, offsets, flatten_ids, reinterpret_cast<const uint2*>(rows),
-            (int64_t)(layer_end - layer_begin) * nt1 * nt2, n_isects, N, dim2, dim1, dim0, nt2,
-            nt1, layer_begin, brick_order, volume);
+        const int64_t n_keys = (int64_t)(layer_end - layer_begin) * nt1 * nt2;
+        if (n_keys < kVFwd8GroupedBricks)
+            voxel_fwd8_kernel<4><<<grid, 64 * 4, 0, stream>>>(
+                (const float4*)vsplats, offsets, flatten_ids, reinterpret_cast<const uint2*>(rows),
+                n_keys, n_isects, N, dim2, dim1, dim0, nt2, nt1, layer_begin, brick_order, volume);
+        else
+            voxel_fwd8_kernel<1><<<grid, 64, 0, stream>>>(
+                (const float4*)vsplats, offsets, flatten_ids, reinterpret_cast<const uint2*>(rows),
+                n_keys, n_isects, N, dim2, dim1, dim0, nt2, nt1, layer_begin, brick_order, volume);
         return check_launch("voxel_splats_fwd");
     }
     VoxSrc<float> src{(const float4*)vsplats, nullptr, nullptr, nullptr};

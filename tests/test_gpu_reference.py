@@ -345,8 +345,11 @@ def test_fused_voxel_gradients_alone_match_reference(ref, case):
 
 def test_explicit_voxelize_z_slab_matches_full_grid_and_reference(ref, case):
     """explicit_voxelize(..., z_layers=(l0, l1)) -- this build's extension for
-    a rank's z-slab -- voxelizes exactly the rows of those brick layers of the
-    full grid (bit-identical: same records, same order per brick), and its
+    a rank's z-slab -- voxelizes the rows of those brick layers of the full
+    grid (same records in the same order per brick: bit-identical when both
+    launches use the same number of record groups per brick, else equal to
+    float rounding, 1e-6, as launches of fewer than 16,384 bricks split each
+    brick's records over four groups), and its
     backward of a slab gradient equals the backward of the full grid with
     that gradient placed in a zero volume (the same per-brick moments added
     into float64 per-Gaussian sums, so the order of the additions does not
@@ -381,7 +384,8 @@ def test_explicit_voxelize_z_slab_matches_full_grid_and_reference(ref, case):
         E.explicit_backward(st, params["means"], params["quats"], params["scales"], params["opac"])
         grads.append({k: params[k].grad for k in params})
     assert vols[1].shape == (z1 - z0, G, G)
-    assert torch.equal(vols[1], vols[0][z0:z1]), f"{name}: slab rows differ from the full grid"
+    e = rel_l2(vols[1], vols[0][z0:z1])
+    assert e < 1e-6, f"{name}: slab rows vs the full grid rel-L2 {e:.3e}"
     for key in grads[0]:
         e = rel_l2(grads[1][key], grads[0][key])
         assert e < 1e-6, f"{name}: slab grad {key} vs full-grid grad rel-L2 {e:.3e}"
