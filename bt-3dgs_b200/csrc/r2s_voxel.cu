@@ -612,12 +612,14 @@ voxel_rows8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict
 // a thread 4x2 voxels (x, z)).  A CTA holds GROUPS groups; they take the
 // staged records of each batch in turn (record t of the batch to group
 // t mod GROUPS) and add their partial sums in group order at the end.  One
-// group per CTA is the fastest on launches of many waves (the full grid);
-// launches of fewer bricks (a z-slab of a multi-GPU split: one or a few waves)
-// finish sooner with four, since with one group an SM runs a handful of
-// heavy bricks at low occupancy once the light ones are done.
+// group per CTA is the fastest on launches of many records (the full config-2
+// grid: 20M records, 2.44 ms against 2.80 ms with four groups); launches of
+// fewer records per SM (a z-slab of a multi-GPU split, a small grid) finish
+// sooner with four (2-4M records: 0.43-0.54 ms against 0.63-0.69 ms), since
+// with one group an SM runs a handful of heavy bricks at low occupancy once
+// the light ones are done.  The two cross near 6M records on 148 SMs.
 constexpr int kVFwd8Batch = 128;  // records staged per group and batch
-constexpr int kVFwd8GroupedBricks = 16384;  // fewer bricks per launch: four groups
+constexpr int64_t kVFwd8GroupedRecordsPerSM = 32768;  // fewer per launch: four groups
 
 template <int GROUPS>
 __global__ void __launch_bounds__(64 * GROUPS)
@@ -1193,7 +1195,10 @@ extern "C" int r2s_voxel_splats_fwd_f32(const float* vsplats, const int32_t* off
     if (T == 8) {
         const dim3 grid(nt2, nt1, layer_end - layer_begin);
         const int64_t n_keys = (int64_t)(layer_end - layer_begin) * nt1 * nt2;
-        if (n_keys < kVFwd8GroupedBricks)
+        int dev = 0, sms = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (n_isects < kVFwd8GroupedRecordsPerSM * std::max(sms, 1))
             voxel_fwd8_kernel<4><<<grid, 64 * 4, 0, stream>>>(
                 (const float4*)vsplats, offsets, flatten_ids, reinterpret_cast<const uint2*>(rows),
                 n_keys, n_isects, N, dim2, dim1, dim0, nt2, nt1, layer_begin, brick_order, volume);

@@ -348,7 +348,7 @@ def test_explicit_voxelize_z_slab_matches_full_grid_and_reference(ref, case):
     a rank's z-slab -- voxelizes the rows of those brick layers of the full
     grid (same records in the same order per brick: bit-identical when both
     launches use the same number of record groups per brick, else equal to
-    float rounding, 1e-6, as launches of fewer than 16,384 bricks split each
+    float rounding, 1e-6, as launches of few records per SM split each
     brick's records over four groups), and its
     backward of a slab gradient equals the backward of the full grid with
     that gradient placed in a zero volume (the same per-brick moments added
