@@ -339,8 +339,9 @@ class OursVoxel(HostPipeline):
         vm1, K1 = wl.make_cameras(VOXEL_STEP_VIEWS, VOXEL_STEP_DETECTOR)
         self.vm1, self.K1 = vm1.to(dev), K1.to(dev)
         if world > 1:
-            # z-slabs balanced by records per brick layer (every rank computes
-            # the same ranges from the same mapping)
+            # z-slabs balanced by the cost of each brick layer, its records
+            # plus a per-brick share (every rank computes the same ranges from
+            # the same mapping)
             from r2splat.cuda import _wrapper as W
 
             with torch.no_grad():
@@ -348,7 +349,8 @@ class OursVoxel(HostPipeline):
                 cov, _, op = W.fused_prepare(q, s, o, wl.SCALE_MIN, wl.SCALE_MAX)
                 rects = W.fused_map(m, cov, op, self.rng, self.ctr, G, G, G, wl.VOL_TILE,
                                     self.nt, self.nt, self.nt, wl.EPS3D, wl.RADIUS_CLIP)[4]
-            self.layers = shard.balanced_layer_ranges(shard.layer_weights(rects, self.nt),
+            self.layers = shard.balanced_layer_ranges(shard.layer_costs(rects, self.nt,
+                                                                        self.nt * self.nt),
                                                       world)[rank]
         else:
             self.layers = None

@@ -99,6 +99,22 @@ def layer_weights(rects3: torch.Tensor, n_layers: int) -> List[float]:
     return torch.cumsum(diff, 0)[:n_layers].tolist()
 
 
+# Time of a brick layer beyond its records, in records: its 3D binning, row
+# table and brick launches cost about as much per brick as 94 records do in
+# the voxel forward and backward (a fit of t = a + b records + c layers to the
+# eight z-slabs of config 2 on 8 B200s: b = 0.31 ms per million records,
+# c = 0.030 ms per layer of 1,024 bricks).
+BRICK_COST_RECORDS = 94.0
+
+
+def layer_costs(rects3: torch.Tensor, n_layers: int, bricks_per_layer: int) -> List[float]:
+    """Weights of the z-slab split: records per brick layer plus the layer's
+    own cost (BRICK_COST_RECORDS per brick), so that ranks of many sparse
+    layers are not given as many records as ranks of a few dense ones."""
+    extra = BRICK_COST_RECORDS * bricks_per_layer
+    return [x + extra for x in layer_weights(rects3, n_layers)]
+
+
 def slab_rows(l0: int, l1: int, tile: int, dim0: int) -> Tuple[int, int]:
     """Voxel rows [z0, z1) of brick layers [l0, l1) in a grid of depth dim0."""
     z0 = l0 * tile

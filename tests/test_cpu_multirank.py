@@ -240,6 +240,8 @@ def test_layer_weights_from_packed_rects():
             (pack(3, 3), pack(0, 1), pack(0, 4), 0)]   # empty in x
     rects = torch.tensor(rows, dtype=torch.int64).to(torch.int32).contiguous().view(torch.uint8)
     assert shard.layer_weights(rects, 4) == [6.0, 6.0, 7.0, 1.0]
+    extra = shard.BRICK_COST_RECORDS * 9
+    assert shard.layer_costs(rects, 4, 9) == [6.0 + extra, 6.0 + extra, 7.0 + extra, 1.0 + extra]
 
 
 @pytest.mark.parametrize("split", [(4, 4), (3, 5), (1, 2, 5)])
