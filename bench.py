@@ -161,7 +161,8 @@ def max_over_ranks(world, value: float) -> float:
 def job_config(cfg, views: int) -> dict:
     """The workload keys both arms print (same dict for the same job)."""
     return {"workload": cfg.name, "n_gaussians": cfg.n_gaussians, "views": views,
-            "detector": cfg.detector, "grid": cfg.grid, "l2": "256MiB flush between steps"}
+            "detector": cfg.detector, "grid": cfg.grid,
+            "l2": "256MiB flush between steps, outside the timed events"}
 
 
 # ---------------------------------------------------------------------------
@@ -286,6 +287,7 @@ class OursProjection(HostPipeline):
         m, q, s, o = self.params
         C, N, det = self.views, m.size(0), self.det
         nt = (det + wl.IMG_TILE - 1) // wl.IMG_TILE
+        stats = torch.empty((C * N, 8), dtype=torch.float32, device=self.dev)
         T = PhaseTimer()
         with torch.no_grad():
             cov, ms, op = W.fused_prepare(q, s, o, wl.SCALE_MIN, wl.SCALE_MAX)
@@ -294,13 +296,14 @@ class OursProjection(HostPipeline):
                                                           wl.IMG_TILE, nt, nt, wl.EPS2D,
                                                           wl.RADIUS_CLIP)
             T.mark("project")
-            # the op layer's view batches (one batch unless the records pass
-            # the int32 tile offsets, as at config 3)
-            stats = torch.empty((C * N, 8), dtype=torch.float32, device=self.dev)
-            batches = W.plan_view_batches(rects, C, N)
-            for c0, c1 in batches:
-                offs, ids, _ = W.fused_bin(rects[c0 * N * 8:c1 * N * 8], c1 - c0, N, nt * nt, nt,
-                                           0)
+            # the op layer's binning: all views at once, or contiguous view
+            # batches when the records pass the int32 tile offsets (config 3)
+            binned = W.fused_bin(rects, C, N, nt * nt, nt, 0, limit=W.MAX_RECORDS_PER_BATCH)
+            batches = ([(0, C, binned)] if binned is not None else
+                       [(c0, c1, None) for c0, c1 in W.plan_view_batches(rects, C, N)])
+            for c0, c1, pre in batches:
+                offs, ids, _ = pre if pre is not None else W.fused_bin(
+                    rects[c0 * N * 8:c1 * N * 8], c1 - c0, N, nt * nt, nt, 0)
                 T.mark("binning (incl. host read of the record count)")
                 cull = torch.empty(ids.shape, dtype=torch.int16, device=self.dev)
                 W.fused_raster_fwd(splats[c0:c1], offs, ids, c1 - c0, N, det, det, wl.IMG_TILE,
@@ -310,7 +313,7 @@ class OursProjection(HostPipeline):
                                    det, wl.IMG_TILE, nt, nt, True, out=stats[c0 * N:c1 * N],
                                    cull=cull)
                 T.mark("raster backward")
-                del offs, ids, cull
+                del offs, ids, cull, pre
             outs = [torch.empty_like(t) for t in (m, q, s, o)]
             v2 = torch.empty((C, N, 2), device=self.dev)
             v2a = torch.empty((C, N, 2), device=self.dev)
@@ -827,7 +830,7 @@ def run_train_bench(args, cfg, dev, world, rank, local, flush):
                             f"steps (longest axis, revised opacity); timed steps "
                             f"{timed_first}-{trainer.step_no - 1} include split(s) at {splits}",
                    "gaussians_per_timed_step": timed_sizes,
-                   "l2": "256MiB flush between steps"},
+                   "l2": "256MiB flush between steps, outside the timed events"},
         "clocks": clk.summary(),
     }
     if ref:
@@ -851,22 +854,25 @@ def run_train_bench(args, cfg, dev, world, rank, local, flush):
 # timing helpers
 # ---------------------------------------------------------------------------
 def time_steps(fn, steps, warmup, world, flush):
+    """Device time per step: each of the K steps between its own pair of
+    CUDA events on the compute stream, the 256 MiB L2 flush before each step
+    outside the pair, the K steps bracketed by a barrier and a synchronize."""
     for _ in range(warmup):
         flush.zero_()
         fn()
     torch.cuda.synchronize()
     barrier(world)
     torch.cuda.synchronize()
-    a = torch.cuda.Event(enable_timing=True)
-    b = torch.cuda.Event(enable_timing=True)
-    a.record()
-    for _ in range(steps):
+    pairs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+             for _ in range(steps)]
+    for a, b in pairs:
         flush.zero_()  # inputs and L2: 256 MiB write between steps
+        a.record()
         fn()
-    b.record()
+        b.record()
     torch.cuda.synchronize()
     barrier(world)
-    ms = a.elapsed_time(b) / steps
+    ms = sum(a.elapsed_time(b) for a, b in pairs) / steps
     return max_over_ranks(world, ms)
 
 
@@ -1261,11 +1267,14 @@ def main():
     # our kernels per timed step: projection = prepare (covariances, then the
     # softplus opacities), project_splats, binning (count, column scan, scan,
     # place), raster forward, raster backward, explicit backward (binning to
-    # raster backward once per view batch); voxel =
+    # raster backward once per view batch; with several batches, the first
+    # binning's count, column scan and scan also run once for all views, as
+    # the op layer first tries one binning); voxel =
     # prepare (two), map, binning (count, column scan, scan, place), brick
     # order, row table, voxel forward, voxel backward, explicit backward (the
     # zero-view projection pass launches nothing)
-    gpu_launches = args.steps * (4 + 6 * proj_phases["view_batches"])
+    n_batches = proj_phases["view_batches"]
+    gpu_launches = args.steps * (4 + 6 * n_batches + (3 if n_batches > 1 else 0))
     vox_launches = args.steps * 12
     if rank != 0:
         return
