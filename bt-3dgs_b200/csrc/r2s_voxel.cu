@@ -617,9 +617,11 @@ voxel_rows8_kernel(const float4* __restrict__ vsplats, const int32_t* __restrict
 // fewer records per SM (a z-slab of a multi-GPU split, a small grid) finish
 // sooner with four (2-4M records: 0.43-0.54 ms against 0.63-0.69 ms), since
 // with one group an SM runs a handful of heavy bricks at low occupancy once
-// the light ones are done.  The two cross near 6M records on 148 SMs.
+// the light ones are done.  On centred slabs of the config-2 grid four groups
+// are 14 % faster at 3.8M records and 3 % slower at 7.7M; they cross near
+// 6.5M records on 148 SMs.
 constexpr int kVFwd8Batch = 128;  // records staged per group and batch
-constexpr int64_t kVFwd8GroupedRecordsPerSM = 32768;  // fewer per launch: four groups
+constexpr int64_t kVFwd8GroupedRecordsPerSM = 44032;  // fewer per launch: four groups
 
 template <int GROUPS>
 __global__ void __launch_bounds__(64 * GROUPS)
