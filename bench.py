@@ -1196,6 +1196,51 @@ def run_reference(args, cfg, dev, local, flush):
     print(json.dumps(line))
 
 
+def run_rank_shares(args, cfg, dev, flush):
+    """Each rank's share of an N-GPU strong-scaling job, timed in turn on one
+    GPU: the projection with the rank's views (view r, r + N, ...), the voxel
+    step with the rank's z-slab (the same split the N-GPU run computes), each
+    a step object of the N-GPU run with its gradient all-reduce left out.
+    The largest rank time against the one-GPU time / N bounds the N-GPU
+    efficiency before the all-reduce; the phases name what limits it."""
+    n = args.rank_shares
+    if n < 1:
+        raise SystemExit("--rank-shares needs N >= 1")
+    ranks = []
+    with ClockSampler(0) as clk:
+        for world, rank in [(1, 0)] + [(n, r) for r in range(n)]:
+            proj = OursProjection(cfg, world, rank, dev, "strong")
+            proj.world = 1  # no collective: one process
+            ms = time_steps(proj.step, args.steps, args.warmup, 1, flush)
+            proj.phases()
+            pph = proj.phases()
+            views = proj.views
+            del proj
+            torch.cuda.empty_cache()
+            vox = OursVoxel(cfg, world, rank, dev, wl.make_gaussians(cfg))
+            vox.world = 1
+            vms = time_steps(vox.step, args.steps, args.warmup, 1, flush)
+            vox.phases()
+            vph = vox.phases()
+            del vox
+            torch.cuda.empty_cache()
+            ranks.append({"world": world, "rank": rank, "views": views,
+                          "projection_ms": round(ms, 3), "voxel_ms": round(vms, 3),
+                          "layers": vph["layers"], "records": vph["records"],
+                          "projection_phases": pph["ms"], "voxel_phases": vph["ms"]})
+    one, shares = ranks[0], ranks[1:]
+    p_max = max(r["projection_ms"] for r in shares)
+    v_max = max(r["voxel_ms"] for r in shares)
+    print(json.dumps({
+        "mode": f"rank shares of a {n}-GPU strong-scaling job, timed in turn on one GPU",
+        "config": job_config(cfg, cfg.n_views), "steps": args.steps, "warmup": args.warmup,
+        "projection": {"one_gpu_ms": one["projection_ms"], "largest_share_ms": p_max,
+                       "efficiency_before_allreduce": round(one["projection_ms"] / n / p_max, 4)},
+        "voxelize": {"one_gpu_ms": one["voxel_ms"], "largest_share_ms": v_max,
+                     "efficiency_before_allreduce": round(one["voxel_ms"] / n / v_max, 4)},
+        "ranks": ranks, "clocks": clk.summary()}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1209,6 +1254,9 @@ def main():
     ap.add_argument("--views", type=int, default=None,
                     help="override the job's views (small profiling cases)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--rank-shares", type=int, default=None, metavar="N",
+                    help="one GPU: time each rank's share of an N-GPU strong-scaling job "
+                         "in turn (no collective) and print the per-rank step times")
     args = ap.parse_args()
     if args.impl == "reference" and int(os.environ.get("RANK", "0")) != 0:
         return  # the reference arm runs on rank 0 only
@@ -1226,6 +1274,11 @@ def main():
     hbm_peak, peak_kind = _peaks()
     if args.config == 4:
         run_train_bench(args, cfg, dev, world, rank, local, flush)
+        return
+    if args.rank_shares is not None:
+        if world != 1 or args.impl != "ours":
+            raise SystemExit("--rank-shares runs this build on one GPU")
+        run_rank_shares(args, cfg, dev, flush)
         return
     if args.impl == "reference":
         run_reference(args, cfg, dev, local, flush)
