@@ -490,9 +490,10 @@ constexpr int kFwd16Batch = 256;
 // compiled for that pattern: no per-record group tests, straight-line group
 // bodies.  Each
 // group is 2 pixels per lane in packed pairs.  The four warps' partial sums
-// are added in shared memory at the end.  Ten resident CTAs per SM (48
-// registers) measured faster than the 63 registers the compiler picks alone.
-__global__ void __launch_bounds__(kFwd16Threads, 10)
+// are added in shared memory at the end.  Nine resident CTAs per SM (56
+// registers) measured fastest: 23.71 ms at config 2 against 24.14 ms for
+// eight, 24.71 ms for ten and more for twelve or the compiler's own 63.
+__global__ void __launch_bounds__(kFwd16Threads, 9)
 raster_fwd16_kernel(const float4* __restrict__ splats, const int32_t* __restrict__ offsets,
                     const int32_t* __restrict__ flatten_ids, int64_t n_keys, int64_t n_isects,
                     int64_t n_splats, uint32_t W, uint32_t H, uint32_t ntx, uint32_t nty,
