@@ -22,8 +22,14 @@ views are dealt to the ranks, every N-th view starting at the rank
 per-Gaussian gradients are summed with one NCCL all-reduce per step;
 ``--scaling weak`` gives every rank 75 views of a 75*N-view orbit instead.
 The voxel grid is split into N z-slabs of whole brick layers, balanced by
-records per layer (strong scaling).  ``value`` is the whole job's
-Gaussian*views over the max-over-ranks step time.
+each layer's records plus a per-brick cost (strong scaling).  ``value`` is the
+whole job's Gaussian*views over the max-over-ranks step time.  Each timed step
+lies between its own pair of CUDA events; the 256 MiB L2 flush before each
+step lies outside them.
+
+``--rank-shares N`` (one GPU) times each rank's share of an N-GPU strong-scaling
+job in turn, with the same step objects and no collective, and prints the
+per-rank step times and phases: what limits N GPUs, measured on one.
 
 ``--impl reference`` runs the reference implementation of the path on rank 0:
 its own Python op layer, unchanged (``baseline/_ref``), over its own CUDA
