@@ -14,7 +14,7 @@ from __future__ import annotations
 
 import ctypes
 import os
-from typing import Optional, Tuple
+from typing import Optional
 
 import torch
 

@@ -1,7 +1,6 @@
 """Edge cases of the float32 op layer (the fused kernels) against the live
 reference build: ragged detector tiles and voxel bricks, Gaussians that are
 all culled, non-finite means, a single Gaussian, very large footprints."""
-import math
 
 import pytest
 import torch
